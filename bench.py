@@ -1,0 +1,368 @@
+"""Benchmark: fwd+bwd attention TFLOPS on B200 (BASELINE.json metric).
+
+Workload (the metric's headline config): bf16
+Llama-3-8B-style GQA layer, B=4 per GPU, Hq=32, Hkv=8, D=128, S=4096, causal,
+scale 1/sqrt(128); q, k, v, grad_out ~ N(0,1) seeded, synthetic.
+
+One step = one forward + one backward of that layer through the library's
+C ABI (bfa_fwd, then Δ, dK/dV, dQ). FLOPs count only unmasked (i, j) pairs,
+element-exact: 4·D per pair forward, 10·D backward.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 is launched with torchrun (one process per GPU); each rank runs its own
+batch shard (weak scaling, no collective on the data path); the step time is
+the max over ranks. `--impl reference` times the reference's math path on the
+host CPU cores (the CPU restatement in oracle/; the reference itself is
+Triton for Ascend NPUs and has no GPU or CPU build that runs here).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "npu-flex-att_b200"))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "fwd+bwd attention TFLOPS/GPU (unmasked FLOPs) and % of bf16 tensor peak"
+CFG = dict(B=4, Hq=32, Hkv=8, S=4096, D=128, causal=True)
+WORKLOAD = "c3: bf16 GQA B=4/GPU Hq=32 Hkv=8 D=128 S=4096 causal fwd+bwd"
+
+
+def causal_pairs(s: int) -> int:
+    return s * (s + 1) // 2
+
+
+def step_flops(cfg=CFG) -> float:
+    pairs = causal_pairs(cfg["S"]) * cfg["B"] * cfg["Hq"]
+    return 14.0 * cfg["D"] * pairs
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            m = json.load(f)
+        return float(m["bf16_tflops"]), float(m["hbm_gbs"]), "measured"
+    except Exception:
+        return 1590.0, 6650.0, "fallback"
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [num(r[1]) for r in rows if num(r[1])]
+        smax = max((num(r[2]) or 0) for r in rows)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def make_inputs(seed, device, cfg=CFG):
+    g = torch.Generator().manual_seed(seed)
+    B, Hq, Hkv, S, D = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["S"], cfg["D"]
+    # Generated on the device from a seeded generator (the full tensors are GBs).
+    gd = torch.Generator(device=device).manual_seed(seed)
+    q = torch.randn(B, Hq, S, D, generator=gd, device=device, dtype=torch.bfloat16)
+    k = torch.randn(B, Hkv, S, D, generator=gd, device=device, dtype=torch.bfloat16)
+    v = torch.randn(B, Hkv, S, D, generator=gd, device=device, dtype=torch.bfloat16)
+    do = torch.randn(B, Hq, S, D, generator=gd, device=device, dtype=torch.bfloat16)
+    del g
+    return q, k, v, do
+
+
+def cpu_baseline_sample(budget_s: float = 15.0):
+    """The reference's math path (oracle restatement) on the host cores.
+
+    Times fwd+bwd of single (b, q-head) slices of the workload (S=4096,
+    D=128, causal, fp32) until ~budget_s seconds of CPU work, and scales FLOPs
+    per slice; returns (TFLOPS, threads, slices)."""
+    from oracle.attention_math import attention_backward, attention_forward
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    S, D = CFG["S"], CFG["D"]
+    q, k, v, do = (torch.randn(1, 1, S, D, generator=g) for _ in range(4))
+    slice_flops = 14.0 * D * causal_pairs(S)
+    attention_forward(q[:, :, :256], k[:, :, :256], v[:, :, :256], causal=True, dtype=torch.float32)
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        o, lse = attention_forward(q, k, v, causal=True, dtype=torch.float32)
+        attention_backward(q, k, v, do, causal=True, out=o, lse=lse, dtype=torch.float32)
+        n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return n * slice_flops / dt / 1e12, threads, n
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    per_step = []
+    tflops_all = []
+    for i in range(args.warmup + args.steps):
+        tf, threads, n = cpu_baseline_sample(budget_s=2.0)
+        if i >= args.warmup:
+            tflops_all.append(tf)
+            per_step.append(n)
+    value = statistics.median(tflops_all)
+    ms = step_flops() / (value * 1e12) * 1e3
+    out = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": "TFLOPS",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": WORKLOAD, "global_batch": CFG["B"] * args.gpus, "seq_len": CFG["S"],
+                   "parallelism": "host CPU, all cores"},
+        "cpu_baseline": {"value": round(value, 6), "unit": "TFLOPS", "cores": threads,
+                         "kind": "port",
+                         "sample": "per step: fwd+bwd of whole (b, q-head) slices of the workload "
+                                   "(S=4096, D=128, causal, fp32) for ~2 s; TFLOPS scale per slice"},
+        "e2e": {"value": round(value, 6), "unit": "TFLOPS", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
+def run_ours(args):
+    import bfa_lib
+    import npu_flash_attention as nfa
+
+    rank, world, local = dist_env()
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    lib = bfa_lib.load()
+    q, k, v, do = make_inputs(1234 + rank, dev)
+    B, Hq, Hkv, S, D = CFG["B"], CFG["Hq"], CFG["Hkv"], CFG["S"], CFG["D"]
+    o = torch.empty_like(q)
+    lse = torch.empty(B, Hq, S, device=dev, dtype=torch.float32)
+    grads = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v))
+    pr = nfa._problem(q, k, True, 0, None, 1.0 / math.sqrt(D), 0.0)
+    ws = torch.empty(lib.bfa_bwd_workspace_bytes(pr), dtype=torch.uint8, device=dev)
+    kw = dict(causal=True)
+
+    def step(ev=None):
+        if ev:
+            ev[0].record()
+        out, l_ = nfa.npu_flash_attention_forward(q, k, v, return_lse=True, **kw)
+        if ev:
+            ev[1].record()
+        nfa.npu_flash_attention_backward(q, k, v, out, l_, do, _phases=bfa_lib.PHASE_DELTA,
+                                         _workspace=ws, _outputs=grads, **kw)
+        if ev:
+            ev[2].record()
+        nfa.npu_flash_attention_backward(q, k, v, out, l_, do, _phases=bfa_lib.PHASE_DKDV,
+                                         _workspace=ws, _outputs=grads, **kw)
+        if ev:
+            ev[3].record()
+        nfa.npu_flash_attention_backward(q, k, v, out, l_, do, _phases=bfa_lib.PHASE_DQ,
+                                         _workspace=ws, _outputs=grads, **kw)
+        if ev:
+            ev[4].record()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    nfa.check_device_status(dev)
+
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    launches0 = lib.bfa_launch_count()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(args.steps):
+        step(events[i])
+    end.record()
+    torch.cuda.synchronize()
+    launches = lib.bfa_launch_count() - launches0
+    if world > 1:
+        torch.distributed.barrier()
+    clocks = sampler.stop()
+    nfa.check_device_status(dev)
+    total_ms = start.elapsed_time(end)
+    phase_ms = [sum(events[i][j].elapsed_time(events[i][j + 1]) for i in range(args.steps)) / args.steps
+                for j in range(4)]
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_step = total_ms / args.steps
+    flops = step_flops()
+    value = world * flops / (ms_step * 1e-3) / 1e12
+
+    # ---- e2e: public autograd API, host (pinned) buffers, copies inside the timed region
+    e2e = run_e2e(nfa, dev, args, world)
+
+    peak_tf, _, peak_kind = peaks()
+    pairs = causal_pairs(S) * B * Hq
+    kern_flops = {"fwd": 4.0 * D * pairs, "delta": 0.0, "dkdv": 8.0 * D * pairs, "dq": 6.0 * D * pairs}
+    names = ["fwd", "delta", "dkdv", "dq"]
+    dom = max(range(4), key=lambda j: phase_ms[j])
+    achieved = kern_flops[names[dom]] / (phase_ms[dom] * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "kernel": names[dom], "achieved": round(achieved, 2),
+                "peak": peak_tf, "unit": "TFLOP/s", "frac": round(achieved / peak_tf, 4),
+                "peak_kind": f"bf16 dense burst, {peak_kind}", "traffic": None,
+                "phase_ms": {n: round(x, 4) for n, x in zip(names, phase_ms)}}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tf, threads, n = cpu_baseline_sample(budget_s=args.cpu_budget)
+        cpu = {"value": round(tf, 6), "unit": "TFLOPS", "cores": threads, "kind": "port",
+               "sample": f"{n} whole (b, q-head) slices of the workload (S=4096, D=128, causal, "
+                         f"fp32 fwd+bwd) in ~{args.cpu_budget:.0f} s; TFLOPS scale per slice"}
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": round(value, 3), "unit": "TFLOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1), generated on device)",
+            "config": {"workload": WORKLOAD, "global_batch": B * world, "seq_len": S,
+                       "parallelism": f"batch x head shards on {world} GPU(s), no collective",
+                       "l2": "inputs larger than L2 (q 268 MB, dO 268 MB, k/v 67 MB each)"},
+            "pct_of_peak": round(100.0 * value / world / peak_tf, 2),
+            "gpu_launches": int(launches),
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "clocks": clocks,
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def run_e2e(nfa, dev, args, world):
+    """Same metric through the public autograd API with host buffers: every
+    step copies q, k, v, dO from pinned host memory, runs flex_attention
+    forward + backward, and reads dQ, dK, dV back to pinned host memory."""
+    B, Hq, Hkv, S, D = CFG["B"], CFG["Hq"], CFG["Hkv"], CFG["S"], CFG["D"]
+    shapes = [(B, Hq, S, D), (B, Hkv, S, D), (B, Hkv, S, D), (B, Hq, S, D)]
+    host_in = [torch.randn(*s, dtype=torch.float32).to(torch.bfloat16).pin_memory() for s in shapes]
+    host_out = [torch.empty(*s, dtype=torch.bfloat16).pin_memory() for s in shapes[:3]]
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+
+    def step():
+        qd, kd, vd, dod = (t.to(dev, non_blocking=True) for t in host_in)
+        qd.requires_grad_(True)
+        kd.requires_grad_(True)
+        vd.requires_grad_(True)
+        out = nfa.flex_attention(qd, kd, vd, causal=True)
+        out.backward(dod)
+        for h, d_ in zip(host_out, (qd.grad, kd.grad, vd.grad)):
+            h.copy_(d_, non_blocking=True)
+
+    steps = max(2, min(args.steps, 5))
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    return {"value": round(world * step_flops() / (ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 3),
+            "steps": steps}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,114 @@
+// bfa_common.cuh -- device helpers shared by every attention kernel.
+//
+// The logit transform and the keep-mask follow the reference kernel
+// (npu_flash_attention.py:102-141):
+//   s = (q·k) * scale
+//   s = cap * tanh(s / cap)            if soft_cap > 0       (:105-106)
+//   s = s + slope[hq] * (i - j)        if ALiBi              (:108-109)
+//   keep iff (!causal || i >= j) && (W == 0 || i - j <= W) && j < Sk  (:139,141)
+// with i, j absolute positions (local index + the problem's position offset).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "bfa.h"
+
+namespace bfa {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+__device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); }
+
+// Parameters of one launch, flattened for the device.
+struct Params {
+  const void* q; const void* k; const void* v; void* o;
+  const void* dout; void* dq; void* dk; void* dv;
+  float* lse; float* delta;
+  int64_t sq_[4], sk_[4], sv_[4], so_[4], sdo_[4], sdq_[4], sdk_[4], sdv_[4];
+  int32_t B, Hq, Hkv, G, Sq, Sk, D;
+  int32_t causal, window;
+  float scale, soft_cap;
+  const float* alibi;
+  int64_t q_off, k_off;
+  int32_t* status;
+  uint64_t timeout_ns;
+  uint32_t debug_flags;
+  uint32_t phases;  // backward: mask of BFA_BWD_PHASE_* (never 0 here)
+};
+
+template <typename T> __device__ __forceinline__ float to_f32(T x);
+template <> __device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+
+// Keep-mask on absolute positions.
+__device__ __forceinline__ bool keep_pair(int64_t i, int64_t j, int causal, int window) {
+  if (causal && j > i) return false;
+  if (window > 0 && i - j > window) return false;
+  return true;
+}
+
+// Logit transform (cap then ALiBi). `t_out` receives tanh(s/cap) for the
+// backward chain (1 when no cap).
+__device__ __forceinline__ float transform_logit(float dot, float scale, float cap,
+                                                 float slope, int64_t i, int64_t j,
+                                                 float* t_out) {
+  float s = dot * scale;
+  float t = 0.f;
+  if (cap > 0.f) {
+    t = tanhf(s / cap);
+    s = cap * t;
+  }
+  if (t_out) *t_out = t;
+  s += slope * (float)(i - j);
+  return s;
+}
+
+// Range of key indices [lo, hi) (local) that can be kept for local query
+// rows [r0, r1). Tiles outside it are fully masked and skipped.
+__device__ __forceinline__ void key_range(const Params& p, int r0, int r1, int* lo, int* hi) {
+  int64_t l = 0, h = p.Sk;
+  int64_t i_first = r0 + p.q_off, i_last = (r1 - 1) + p.q_off;
+  if (p.causal) {  // j <= i_last
+    int64_t lim = i_last - p.k_off + 1;
+    if (lim < h) h = lim;
+  }
+  if (p.window > 0) {  // j >= i_first - W
+    int64_t lim = i_first - p.window - p.k_off;
+    if (lim > l) l = lim;
+  }
+  if (h < l) h = l;
+  if (l < 0) l = 0;
+  if (h < 0) h = 0;
+  *lo = (int)l;
+  *hi = (int)h;
+}
+
+// Range of query rows [lo, hi) (local) that can keep any of key rows [c0, c1).
+__device__ __forceinline__ void query_range(const Params& p, int c0, int c1, int* lo, int* hi) {
+  int64_t l = 0, h = p.Sq;
+  int64_t j_first = c0 + p.k_off, j_last = (c1 - 1) + p.k_off;
+  if (p.causal) {  // i >= j_first
+    int64_t lim = j_first - p.q_off;
+    if (lim > l) l = lim;
+  }
+  if (p.window > 0) {  // i <= j_last + W
+    int64_t lim = j_last + p.window - p.q_off + 1;
+    if (lim < h) h = lim;
+  }
+  if (h < l) h = l;
+  if (l < 0) l = 0;
+  if (h < 0) h = 0;
+  *lo = (int)l;
+  *hi = (int)h;
+}
+
+}  // namespace bfa

@@ -1,0 +1,34 @@
+// bfa_internal.h -- host-side declarations shared by the library's .cu files.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "bfa_common.cuh"
+
+namespace bfa {
+
+// Generic CUDA-core path (simt_attention.cu).
+int simt_fwd(const Params& p, int dtype, cudaStream_t st);
+int simt_bwd(const Params& p, int dtype, cudaStream_t st);  // needs p.delta filled
+int launch_delta(const Params& p, int dtype, cudaStream_t st);
+
+// tcgen05 / TMA path (sm100_fwd.cu, sm100_bwd.cu). `*_eligible` say whether
+// the fast path takes this problem; the launchers return a bfa_status.
+bool sm100_fwd_eligible(const Params& p, int dtype);
+int sm100_fwd(const Params& p, int dtype, cudaStream_t st);
+bool sm100_bwd_eligible(const Params& p, int dtype);
+int sm100_bwd(const Params& p, int dtype, cudaStream_t st);
+
+// Partial-result merge (merge.cu).
+int launch_merge(int B, int H, int S, int D, const bfa_tensor& oa, int adt, float* lse_a,
+                 const bfa_tensor& op, int pdt, const float* lse_p, cudaStream_t st);
+
+// Count one kernel launch (bfa_launch_count).
+void note_launch();
+
+// Bytes of one element of a bfa_dtype (0 when invalid).
+inline int dtype_bytes(int dt) {
+  return dt == BFA_DTYPE_F32 ? 4 : (dt == BFA_DTYPE_F16 || dt == BFA_DTYPE_BF16) ? 2 : 0;
+}
+
+}  // namespace bfa

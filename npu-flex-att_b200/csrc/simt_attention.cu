@@ -1,0 +1,410 @@
+// simt_attention.cu -- generic CUDA-core attention kernels (any dtype, any
+// strides, head_dim <= 256).
+//
+// These are the library's fp32 path (the tcgen05 path computes in bf16/fp16
+// operands and cannot meet the fp32 tolerance) and its path for layouts the
+// TMA path does not take (odd head dims, unaligned strides). Every value is
+// carried in fp32. Structure mirrors the reference kernels one-to-one:
+//   simt_fwd_kernel    <- flash_attn_fwd_kernel      npu_flash_attention.py:17-166
+//   simt_bwd_dq_kernel <- flash_attn_bwd_dq_kernel   npu_flash_attention.py:298-402
+//   simt_bwd_dkdv_kernel <- flash_attn_bwd_dkdv_kernel npu_flash_attention.py:407-560,
+//       except that one CTA owns a (b, kv-head, kv-tile) and loops over the
+//       GQA group, so dK/dV come out already summed (the reference sums per-q-head
+//       copies on the host at :735-737) and the sum is deterministic.
+//
+// Tiles are 32 query rows x 32 key rows, 128 threads: thread t owns tile row
+// t/4 and, within it, every 4th key column and every 4th head-dim column.
+#include <cuda_runtime.h>
+
+#include "bfa_common.cuh"
+#include "bfa_internal.h"
+
+namespace bfa {
+namespace {
+
+constexpr int TM = 32;
+constexpr int TN = 32;
+constexpr int NT = 128;
+
+template <typename T>
+__device__ __forceinline__ const T* head_ptr(const void* base, const int64_t* st, int b, int h) {
+  return (const T*)base + (int64_t)b * st[0] + (int64_t)h * st[1];
+}
+
+// Stage rows [row0, row0 + nvalid) x [0, D) of a strided [S, D] slice into
+// shared memory as fp32 with row pitch DP+1; missing rows/cols become 0.
+template <typename T, int DP>
+__device__ __forceinline__ void stage_rows(float* dst, const T* src, int64_t srow, int64_t scol,
+                                           int row0, int nvalid, int D, int nrows) {
+  for (int idx = threadIdx.x; idx < nrows * DP; idx += NT) {
+    const int r = idx / DP, c = idx - r * DP;
+    float val = 0.f;
+    if (r < nvalid && c < D) val = to_f32<T>(src[(int64_t)(row0 + r) * srow + (int64_t)c * scol]);
+    dst[r * (DP + 1) + c] = val;
+  }
+}
+
+template <int DP>
+__device__ __forceinline__ float dot_rows(const float* a, const float* b) {
+  float acc = 0.f;
+#pragma unroll 16
+  for (int d = 0; d < DP; ++d) acc = fmaf(a[d], b[d], acc);
+  return acc;
+}
+
+template <typename T, int DP>
+__global__ void __launch_bounds__(NT) simt_fwd_kernel(Params p) {
+  extern __shared__ float smem[];
+  float* sQ = smem;
+  float* sK = sQ + TM * (DP + 1);
+  float* sV = sK + TN * (DP + 1);
+  float* sP = sV + TN * (DP + 1);  // [TM][TN+1]
+
+  const int r0 = blockIdx.x * TM, hq = blockIdx.y, b = blockIdx.z;
+  const int hkv = hq / p.G;
+  const int rows = min(TM, p.Sq - r0);
+  const T* Q = head_ptr<T>(p.q, p.sq_, b, hq);
+  const T* K = head_ptr<T>(p.k, p.sk_, b, hkv);
+  const T* V = head_ptr<T>(p.v, p.sv_, b, hkv);
+  stage_rows<T, DP>(sQ, Q, p.sq_[2], p.sq_[3], r0, rows, p.D, TM);
+
+  const int tid = threadIdx.x, r = tid >> 2, c = tid & 3;
+  const int64_t gi = (int64_t)r0 + r + p.q_off;
+  const float slope = p.alibi ? p.alibi[hq] : 0.f;
+  float m = neg_inf(), l = 0.f;
+  float acc[DP / 4];
+#pragma unroll
+  for (int e = 0; e < DP / 4; ++e) acc[e] = 0.f;
+
+  int lo, hi;
+  key_range(p, r0, r0 + rows, &lo, &hi);
+  for (int k0 = (lo / TN) * TN; k0 < hi; k0 += TN) {
+    const int kn = min(TN, p.Sk - k0);
+    __syncthreads();
+    stage_rows<T, DP>(sK, K, p.sk_[2], p.sk_[3], k0, kn, p.D, TN);
+    stage_rows<T, DP>(sV, V, p.sv_[2], p.sv_[3], k0, kn, p.D, TN);
+    __syncthreads();
+    float s[TN / 4];
+    float mx = neg_inf();
+#pragma unroll
+    for (int u = 0; u < TN / 4; ++u) {
+      const int jj = c + 4 * u;
+      const int64_t gj = (int64_t)k0 + jj + p.k_off;
+      const float dot = dot_rows<DP>(sQ + r * (DP + 1), sK + jj * (DP + 1));
+      const float val = transform_logit(dot, p.scale, p.soft_cap, slope, gi, gj, nullptr);
+      const bool ok = (jj < kn) && (r < rows) && keep_pair(gi, gj, p.causal, p.window);
+      s[u] = ok ? val : neg_inf();
+      mx = fmaxf(mx, s[u]);
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m, mx);
+    const float alpha = (m_new == neg_inf()) ? 1.f : expf(m - m_new);
+    float rs = 0.f;
+#pragma unroll
+    for (int u = 0; u < TN / 4; ++u) {
+      const float pv = (s[u] == neg_inf()) ? 0.f : expf(s[u] - m_new);
+      sP[r * (TN + 1) + c + 4 * u] = pv;
+      rs += pv;
+    }
+    rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+    rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+    l = l * alpha + rs;
+    m = m_new;
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < DP / 4; ++e) acc[e] *= alpha;
+    for (int jj = 0; jj < TN; ++jj) {
+      const float pv = sP[r * (TN + 1) + jj];
+      const float* vrow = sV + jj * (DP + 1) + c;
+#pragma unroll
+      for (int e = 0; e < DP / 4; ++e) acc[e] = fmaf(pv, vrow[4 * e], acc[e]);
+    }
+  }
+
+  if (r < rows) {
+    const float inv = (l > 0.f) ? 1.f / l : 0.f;
+    T* O = (T*)p.o + (int64_t)b * p.so_[0] + (int64_t)hq * p.so_[1] + (int64_t)(r0 + r) * p.so_[2];
+#pragma unroll
+    for (int e = 0; e < DP / 4; ++e) {
+      const int d = c + 4 * e;
+      if (d < p.D) O[(int64_t)d * p.so_[3]] = from_f32<T>(acc[e] * inv);
+    }
+    if (c == 0) {
+      p.lse[((int64_t)b * p.Hq + hq) * p.Sq + r0 + r] = (l > 0.f) ? m + logf(l) : neg_inf();
+    }
+  }
+}
+
+template <typename T, int DP>
+__global__ void __launch_bounds__(NT) simt_bwd_dq_kernel(Params p) {
+  extern __shared__ float smem[];
+  float* sQ = smem;
+  float* sDO = sQ + TM * (DP + 1);
+  float* sK = sDO + TM * (DP + 1);
+  float* sV = sK + TN * (DP + 1);
+  float* sDS = sV + TN * (DP + 1);  // [TM][TN+1]
+
+  const int r0 = blockIdx.x * TM, hq = blockIdx.y, b = blockIdx.z;
+  const int hkv = hq / p.G;
+  const int rows = min(TM, p.Sq - r0);
+  stage_rows<T, DP>(sQ, head_ptr<T>(p.q, p.sq_, b, hq), p.sq_[2], p.sq_[3], r0, rows, p.D, TM);
+  stage_rows<T, DP>(sDO, head_ptr<T>(p.dout, p.sdo_, b, hq), p.sdo_[2], p.sdo_[3], r0, rows, p.D, TM);
+  const T* K = head_ptr<T>(p.k, p.sk_, b, hkv);
+  const T* V = head_ptr<T>(p.v, p.sv_, b, hkv);
+
+  const int tid = threadIdx.x, r = tid >> 2, c = tid & 3;
+  const int64_t gi = (int64_t)r0 + r + p.q_off;
+  const float slope = p.alibi ? p.alibi[hq] : 0.f;
+  const int64_t row_idx = ((int64_t)b * p.Hq + hq) * p.Sq + r0 + r;
+  const float lse = (r < rows) ? p.lse[row_idx] : 0.f;
+  const float dlt = (r < rows) ? p.delta[row_idx] : 0.f;
+  const bool row_live = (r < rows) && (lse != neg_inf());
+  float acc[DP / 4];
+#pragma unroll
+  for (int e = 0; e < DP / 4; ++e) acc[e] = 0.f;
+
+  int lo, hi;
+  key_range(p, r0, r0 + rows, &lo, &hi);
+  for (int k0 = (lo / TN) * TN; k0 < hi; k0 += TN) {
+    const int kn = min(TN, p.Sk - k0);
+    __syncthreads();
+    stage_rows<T, DP>(sK, K, p.sk_[2], p.sk_[3], k0, kn, p.D, TN);
+    stage_rows<T, DP>(sV, V, p.sv_[2], p.sv_[3], k0, kn, p.D, TN);
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < TN / 4; ++u) {
+      const int jj = c + 4 * u;
+      const int64_t gj = (int64_t)k0 + jj + p.k_off;
+      float ds = 0.f;
+      if (row_live && jj < kn && keep_pair(gi, gj, p.causal, p.window)) {
+        float t;
+        const float dot = dot_rows<DP>(sQ + r * (DP + 1), sK + jj * (DP + 1));
+        const float val = transform_logit(dot, p.scale, p.soft_cap, slope, gi, gj, &t);
+        const float pr = expf(val - lse);
+        const float dp = dot_rows<DP>(sDO + r * (DP + 1), sV + jj * (DP + 1));
+        ds = pr * (dp - dlt);
+        if (p.soft_cap > 0.f) ds *= (1.f - t * t);
+        ds *= p.scale;
+      }
+      sDS[r * (TN + 1) + jj] = ds;
+    }
+    __syncwarp();
+    for (int jj = 0; jj < TN; ++jj) {
+      const float dsv = sDS[r * (TN + 1) + jj];
+      const float* krow = sK + jj * (DP + 1) + c;
+#pragma unroll
+      for (int e = 0; e < DP / 4; ++e) acc[e] = fmaf(dsv, krow[4 * e], acc[e]);
+    }
+  }
+  if (r < rows) {
+    T* DQ = (T*)p.dq + (int64_t)b * p.sdq_[0] + (int64_t)hq * p.sdq_[1] + (int64_t)(r0 + r) * p.sdq_[2];
+#pragma unroll
+    for (int e = 0; e < DP / 4; ++e) {
+      const int d = c + 4 * e;
+      if (d < p.D) DQ[(int64_t)d * p.sdq_[3]] = from_f32<T>(acc[e]);
+    }
+  }
+}
+
+template <typename T, int DP>
+__global__ void __launch_bounds__(NT) simt_bwd_dkdv_kernel(Params p) {
+  extern __shared__ float smem[];
+  float* sK = smem;
+  float* sV = sK + TN * (DP + 1);
+  float* sQ = sV + TN * (DP + 1);
+  float* sDO = sQ + TM * (DP + 1);
+  float* sP = sDO + TM * (DP + 1);   // [TN][TM+1]
+  float* sDS = sP + TN * (TM + 1);   // [TN][TM+1]
+  float* sL = sDS + TN * (TM + 1);   // [TM]
+  float* sDl = sL + TM;              // [TM]
+
+  const int c0 = blockIdx.x * TN, hkv = blockIdx.y, b = blockIdx.z;
+  const int cols = min(TN, p.Sk - c0);
+  stage_rows<T, DP>(sK, head_ptr<T>(p.k, p.sk_, b, hkv), p.sk_[2], p.sk_[3], c0, cols, p.D, TN);
+  stage_rows<T, DP>(sV, head_ptr<T>(p.v, p.sv_, b, hkv), p.sv_[2], p.sv_[3], c0, cols, p.D, TN);
+
+  const int tid = threadIdx.x, r = tid >> 2, c = tid & 3;  // r: kv row in tile
+  const int64_t gj = (int64_t)c0 + r + p.k_off;
+  float adk[DP / 4], adv[DP / 4];
+#pragma unroll
+  for (int e = 0; e < DP / 4; ++e) { adk[e] = 0.f; adv[e] = 0.f; }
+
+  int qlo, qhi;
+  query_range(p, c0, c0 + cols, &qlo, &qhi);
+  for (int g = 0; g < p.G; ++g) {
+    const int hq = hkv * p.G + g;
+    const float slope = p.alibi ? p.alibi[hq] : 0.f;
+    const T* Q = head_ptr<T>(p.q, p.sq_, b, hq);
+    const T* DO = head_ptr<T>(p.dout, p.sdo_, b, hq);
+    for (int q0 = (qlo / TM) * TM; q0 < qhi; q0 += TM) {
+      const int qn = min(TM, p.Sq - q0);
+      __syncthreads();
+      stage_rows<T, DP>(sQ, Q, p.sq_[2], p.sq_[3], q0, qn, p.D, TM);
+      stage_rows<T, DP>(sDO, DO, p.sdo_[2], p.sdo_[3], q0, qn, p.D, TM);
+      if (tid < TM) {
+        const int64_t row_idx = ((int64_t)b * p.Hq + hq) * p.Sq + q0 + tid;
+        sL[tid] = (tid < qn) ? p.lse[row_idx] : neg_inf();
+        sDl[tid] = (tid < qn) ? p.delta[row_idx] : 0.f;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int u = 0; u < TM / 4; ++u) {
+        const int ii = c + 4 * u;
+        const int64_t gi = (int64_t)q0 + ii + p.q_off;
+        float pr = 0.f, ds = 0.f;
+        const float lse = sL[ii];
+        if (r < cols && ii < qn && lse != neg_inf() && keep_pair(gi, gj, p.causal, p.window)) {
+          float t;
+          const float dot = dot_rows<DP>(sQ + ii * (DP + 1), sK + r * (DP + 1));
+          const float val = transform_logit(dot, p.scale, p.soft_cap, slope, gi, gj, &t);
+          pr = expf(val - lse);
+          const float dp = dot_rows<DP>(sDO + ii * (DP + 1), sV + r * (DP + 1));
+          ds = pr * (dp - sDl[ii]);
+          if (p.soft_cap > 0.f) ds *= (1.f - t * t);
+          ds *= p.scale;
+        }
+        sP[r * (TM + 1) + ii] = pr;
+        sDS[r * (TM + 1) + ii] = ds;
+      }
+      __syncwarp();
+      for (int ii = 0; ii < TM; ++ii) {
+        const float pv = sP[r * (TM + 1) + ii];
+        const float dsv = sDS[r * (TM + 1) + ii];
+        const float* dorow = sDO + ii * (DP + 1) + c;
+        const float* qrow = sQ + ii * (DP + 1) + c;
+#pragma unroll
+        for (int e = 0; e < DP / 4; ++e) {
+          adv[e] = fmaf(pv, dorow[4 * e], adv[e]);
+          adk[e] = fmaf(dsv, qrow[4 * e], adk[e]);
+        }
+      }
+    }
+  }
+  if (r < cols) {
+    T* DK = (T*)p.dk + (int64_t)b * p.sdk_[0] + (int64_t)hkv * p.sdk_[1] + (int64_t)(c0 + r) * p.sdk_[2];
+    T* DV = (T*)p.dv + (int64_t)b * p.sdv_[0] + (int64_t)hkv * p.sdv_[1] + (int64_t)(c0 + r) * p.sdv_[2];
+#pragma unroll
+    for (int e = 0; e < DP / 4; ++e) {
+      const int d = c + 4 * e;
+      if (d < p.D) {
+        DK[(int64_t)d * p.sdk_[3]] = from_f32<T>(adk[e]);
+        DV[(int64_t)d * p.sdv_[3]] = from_f32<T>(adv[e]);
+      }
+    }
+  }
+}
+
+// Δ = rowsum(O∘dO): one warp per (b, hq, i) row.
+template <typename T>
+__global__ void __launch_bounds__(256) delta_kernel(Params p) {
+  const int64_t warp = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int64_t nrows = (int64_t)p.B * p.Hq * p.Sq;
+  if (warp >= nrows) return;
+  const int i = (int)(warp % p.Sq);
+  const int hq = (int)((warp / p.Sq) % p.Hq);
+  const int b = (int)(warp / ((int64_t)p.Sq * p.Hq));
+  const T* O = (const T*)p.o + (int64_t)b * p.so_[0] + (int64_t)hq * p.so_[1] + (int64_t)i * p.so_[2];
+  const T* DO = (const T*)p.dout + (int64_t)b * p.sdo_[0] + (int64_t)hq * p.sdo_[1] + (int64_t)i * p.sdo_[2];
+  float acc = 0.f;
+  for (int d = lane; d < p.D; d += 32)
+    acc = fmaf(to_f32<T>(O[(int64_t)d * p.so_[3]]), to_f32<T>(DO[(int64_t)d * p.sdo_[3]]), acc);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) p.delta[warp] = acc;
+}
+
+template <typename T, int DP>
+int launch_fwd_t(const Params& p, cudaStream_t st) {
+  const size_t smem = (size_t)(TM + 2 * TN) * (DP + 1) * 4 + (size_t)TM * (TN + 1) * 4;
+  auto kern = simt_fwd_kernel<T, DP>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return BFA_ERR_CUDA;
+  dim3 grid((p.Sq + TM - 1) / TM, p.Hq, p.B);
+  if (grid.x == 0 || grid.y == 0 || grid.z == 0) return BFA_OK;
+  kern<<<grid, NT, smem, st>>>(p);
+  note_launch();
+  return cudaGetLastError() == cudaSuccess ? BFA_OK : BFA_ERR_CUDA;
+}
+
+template <typename T, int DP>
+int launch_bwd_t(const Params& p, cudaStream_t st) {
+  if (p.phases & BFA_BWD_PHASE_DQ) {
+    const size_t smem = (size_t)(2 * TM + 2 * TN) * (DP + 1) * 4 + (size_t)TM * (TN + 1) * 4;
+    auto kern = simt_bwd_dq_kernel<T, DP>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return BFA_ERR_CUDA;
+    dim3 grid((p.Sq + TM - 1) / TM, p.Hq, p.B);
+    if (grid.x && grid.y && grid.z) {
+      kern<<<grid, NT, smem, st>>>(p);
+      note_launch();
+      if (cudaGetLastError() != cudaSuccess) return BFA_ERR_CUDA;
+    }
+  }
+  if (p.phases & BFA_BWD_PHASE_DKDV) {
+    const size_t smem = (size_t)(2 * TM + 2 * TN) * (DP + 1) * 4 + (size_t)2 * TN * (TM + 1) * 4 + 2 * TM * 4;
+    auto kern = simt_bwd_dkdv_kernel<T, DP>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return BFA_ERR_CUDA;
+    dim3 grid((p.Sk + TN - 1) / TN, p.Hkv, p.B);
+    if (grid.x && grid.y && grid.z) {
+      kern<<<grid, NT, smem, st>>>(p);
+      note_launch();
+      if (cudaGetLastError() != cudaSuccess) return BFA_ERR_CUDA;
+    }
+  }
+  return BFA_OK;
+}
+
+template <typename T>
+int dispatch_dp_fwd(const Params& p, cudaStream_t st) {
+  if (p.D <= 32) return launch_fwd_t<T, 32>(p, st);
+  if (p.D <= 64) return launch_fwd_t<T, 64>(p, st);
+  if (p.D <= 128) return launch_fwd_t<T, 128>(p, st);
+  return launch_fwd_t<T, 256>(p, st);
+}
+
+template <typename T>
+int dispatch_dp_bwd(const Params& p, cudaStream_t st) {
+  if (p.D <= 32) return launch_bwd_t<T, 32>(p, st);
+  if (p.D <= 64) return launch_bwd_t<T, 64>(p, st);
+  if (p.D <= 128) return launch_bwd_t<T, 128>(p, st);
+  return launch_bwd_t<T, 256>(p, st);
+}
+
+}  // namespace
+
+int simt_fwd(const Params& p, int dtype, cudaStream_t st) {
+  switch (dtype) {
+    case BFA_DTYPE_F32: return dispatch_dp_fwd<float>(p, st);
+    case BFA_DTYPE_F16: return dispatch_dp_fwd<__half>(p, st);
+    case BFA_DTYPE_BF16: return dispatch_dp_fwd<__nv_bfloat16>(p, st);
+  }
+  return BFA_ERR_UNSUPPORTED;
+}
+
+int simt_bwd(const Params& p, int dtype, cudaStream_t st) {
+  switch (dtype) {
+    case BFA_DTYPE_F32: return dispatch_dp_bwd<float>(p, st);
+    case BFA_DTYPE_F16: return dispatch_dp_bwd<__half>(p, st);
+    case BFA_DTYPE_BF16: return dispatch_dp_bwd<__nv_bfloat16>(p, st);
+  }
+  return BFA_ERR_UNSUPPORTED;
+}
+
+int launch_delta(const Params& p, int dtype, cudaStream_t st) {
+  const int64_t rows = (int64_t)p.B * p.Hq * p.Sq;
+  if (rows == 0) return BFA_OK;
+  const unsigned blocks = (unsigned)((rows + 7) / 8);
+  switch (dtype) {
+    case BFA_DTYPE_F32: delta_kernel<float><<<blocks, 256, 0, st>>>(p); break;
+    case BFA_DTYPE_F16: delta_kernel<__half><<<blocks, 256, 0, st>>>(p); break;
+    case BFA_DTYPE_BF16: delta_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(p); break;
+    default: return BFA_ERR_UNSUPPORTED;
+  }
+  note_launch();
+  return cudaGetLastError() == cudaSuccess ? BFA_OK : BFA_ERR_CUDA;
+}
+
+}  // namespace bfa

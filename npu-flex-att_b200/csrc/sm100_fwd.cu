@@ -1,0 +1,466 @@
+// sm100_fwd.cu -- tcgen05 / TMA / TMEM flash-attention forward for B200.
+//
+// Replaces flash_attn_fwd_kernel (npu_flash_attention.py:17-166) for bf16/fp16
+// inputs with head_dim 64 or 128. Same math: S = QKᵀ·scale, optional soft-cap
+// and ALiBi, causal / sliding-window masks, online softmax in base 2, O = PV/l
+// and LSE = m + ln(l) in natural log.
+//
+// One CTA owns two 128-row query tiles of one (batch, q-head) and walks the key
+// tiles (128 keys) that any of its rows can see. Warp roles:
+//   warp 0      TMA producer: Q once, then K_j, V_j into a ring of smem slots
+//   warp 1      MMA issuer: S_t = Q_t K_jᵀ into TMEM, O_t += P_t V_j into TMEM
+//   warp 2      TMEM allocator (512 columns)
+//   warps 4-7   softmax for query tile 0, warps 8-11 for tile 1: each thread
+//               owns one query row (one TMEM lane), reads its S row with
+//               tcgen05.ld, writes P (16-bit) into a 128B-swizzled smem tile
+//               that the next MMA reads as its A operand, rescales its O row
+//               in TMEM when the running max grows, and finally writes O via
+//               smem + TMA store and the LSE.
+// The MMA order S_0(j), S_1(j), then per step PV_0(j), S_0(j+1), PV_1(j),
+// S_1(j+1) lets one tile's softmax run while the tensor core works on the
+// other tile. K/V are read with the GQA head map hkv = hq / G
+// (npu_flash_attention.py:42); no K/V expansion happens anywhere.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "bfa_internal.h"
+#include "sm100_host.h"
+#include "sm100_ptx.cuh"
+
+namespace bfa {
+namespace {
+
+using namespace sm100;
+
+constexpr int kBM = 128;
+constexpr int kBN = 128;
+constexpr int kThreads = 384;
+
+template <int D>
+struct FwdLayout {
+  static constexpr int kSub = D / 64;
+  static constexpr int kStages = (D <= 64) ? 6 : 3;
+  static constexpr uint32_t kQBytes = kBM * D * 2;
+  static constexpr uint32_t kKVBytes = kBN * D * 2;
+  static constexpr uint32_t kPBytes = kBM * kBN * 2;
+  static constexpr uint32_t kOffQ = 0;
+  static constexpr uint32_t kOffP = kOffQ + 2 * kQBytes;
+  static constexpr uint32_t kOffKV = kOffP + 2 * kPBytes;
+  static constexpr uint32_t kOffBar = kOffKV + kStages * kKVBytes;
+  static constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
+  static constexpr uint32_t kTmemS = 0;
+  static constexpr uint32_t kTmemO = 2 * kBN;
+  static_assert(kTmemO + 2 * D <= 512, "TMEM budget");
+  static_assert(kSmemBytes <= 232448, "smem budget");
+};
+
+// Bounded wait by lane 0 of the warp, result shared with the whole warp so
+// that warp-collective tcgen05 instructions stay converged.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const WaitCtl& ctl) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, ctl, BFA_ERR_DEVICE_TIMEOUT) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
+
+// Drain wait (ignores the abort flag, still bounded): used before exit so
+// that no async copy or MMA is in flight when the CTA retires.
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, uint64_t timeout_ns) {
+  if (mbar_try_wait(bar, parity)) return;
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > timeout_ns) return;
+  }
+}
+
+// True when every (row, key) pair of the tile is kept and inside Sk.
+__device__ __forceinline__ bool tile_full(const Params& p, int r0, int r1, int c0, int c1) {
+  if (c1 > p.Sk) return false;
+  const int64_t i_min = r0 + p.q_off, i_max = r1 - 1 + p.q_off;
+  const int64_t j_min = c0 + p.k_off, j_max = c1 - 1 + p.k_off;
+  if (p.causal && j_max > i_min) return false;
+  if (p.window > 0 && i_max - j_min > p.window) return false;
+  return true;
+}
+
+template <int D, bool BF16, bool CAP, bool ALIBI>
+__global__ void __launch_bounds__(kThreads, 1)
+    fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+               const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+               const Params p) {
+  using L = FwdLayout<D>;
+  constexpr int NS = L::kStages;
+  enum {
+    kQFull = 0,
+    kKVFull = 1,
+    kKVEmpty = 1 + NS,
+    kSFull = 1 + 2 * NS,
+    kSFree = kSFull + 2,
+    kPFull = kSFree + 2,
+    kODone = kPFull + 2,
+    kDrain = kODone + 2,
+    kNever = kDrain + 1,
+    kNumBars = kNever + 1
+  };
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  const uint32_t sbase = smem_u32(smem);
+  auto bar = [&](int i) -> uint32_t { return sbase + L::kOffBar + 8u * (uint32_t)i; };
+  uint32_t* tmem_slot = (uint32_t*)(smem + L::kOffBar + 8 * kNumBars);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  int* warp_ok = (int*)(tmem_slot + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_mblk = (p.Sq + 2 * kBM - 1) / (2 * kBM);
+  const int bh = blockIdx.x % (p.B * p.Hq);
+  const int mblk = n_mblk - 1 - (int)(blockIdx.x / (p.B * p.Hq));  // heaviest causal blocks first
+  const int hq = bh % p.Hq, b = bh / p.Hq;
+  const int hkv = hq / p.G;
+  const int q0 = mblk * 2 * kBM;
+  int klo, khi;
+  key_range(p, q0, min(q0 + 2 * kBM, p.Sq), &klo, &khi);
+  const int jlo = klo / kBN;
+  const int n_iter = (khi > klo) ? (khi + kBN - 1) / kBN - jlo : 0;
+
+  WaitCtl ctl{abort_flag, p.status, p.timeout_ns};
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kNumBars; ++i) {
+      const bool per_warp = (i >= kSFree && i < kSFree + 2) || (i >= kPFull && i < kPFull + 2);
+      mbar_init(bar(i), per_warp ? 4u : 1u);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(bar(kQFull), 2 * L::kQBytes);
+      for (int t = 0; t < 2; ++t)
+        for (int s = 0; s < L::kSub; ++s)
+          tma_load_4d(sbase + L::kOffQ + t * L::kQBytes + s * (kBM * 128), &tmQ, bar(kQFull),
+                      s * 64, q0 + t * kBM, hq, b);
+      int n = 0;
+      bool ok = true;
+      for (int it = 0; it < n_iter && ok; ++it) {
+        const int j = jlo + it;
+        for (int kv = 0; kv < 2; ++kv) {
+          const int slot = n % NS;
+          if (n >= NS) {
+            ok = mbar_wait(bar(kKVEmpty + slot), ((n / NS) & 1) ^ 1, ctl, BFA_ERR_DEVICE_TIMEOUT);
+            if (!ok) break;
+          }
+          mbar_arrive_expect_tx(bar(kKVFull + slot), L::kKVBytes);
+          for (int s = 0; s < L::kSub; ++s)
+            tma_load_4d(sbase + L::kOffKV + slot * L::kKVBytes + s * (kBN * 128), kv ? &tmV : &tmK,
+                        bar(kKVFull + slot), s * 64, j * kBN, hkv, b);
+          ++n;
+        }
+      }
+      drain_wait(bar(kQFull), 0, p.timeout_ns);
+      for (int i = (n > NS ? n - NS : 0); i < n; ++i)
+        drain_wait(bar(kKVFull + i % NS), (i / NS) & 1, p.timeout_ns);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_f16(kBM, kBN, BF16, false);
+      constexpr uint32_t idO = idesc_f16(kBM, D, BF16, true);
+      auto kv_addr = [&](int idx) -> uint32_t {
+        return sbase + L::kOffKV + (uint32_t)(idx % NS) * L::kKVBytes;
+      };
+      auto issue_s = [&](int t, int idx) {
+        const uint32_t qa = sbase + L::kOffQ + t * L::kQBytes;
+        const uint32_t ka = kv_addr(idx);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t offq = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
+          const uint32_t offk = (kk >> 2) * (kBN * 128) + (kk & 3) * 32;
+          mma_ss(tmem + L::kTmemS + t * kBN, desc_kmajor(qa + offq), desc_kmajor(ka + offk), idS,
+                 kk > 0 ? 1u : 0u);
+        }
+        mma_commit(bar(kSFull + t));
+      };
+      auto issue_pv = [&](int t, int idx, bool acc) {
+        const uint32_t pa = sbase + L::kOffP + t * L::kPBytes;
+        const uint32_t va = kv_addr(idx);
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint32_t offp = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
+          const uint32_t offv = kk * 16 * 128;
+          mma_ss(tmem + L::kTmemO + t * D, desc_kmajor(pa + offp),
+                 desc_mnmajor(va + offv, kBN * 128), idO, (acc || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(bar(kODone + t));
+      };
+      auto wait_load = [&](int idx) {
+        return mbar_wait(bar(kKVFull + idx % NS), (idx / NS) & 1, ctl, BFA_ERR_DEVICE_TIMEOUT);
+      };
+      bool ok = mbar_wait(bar(kQFull), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
+      if (ok && n_iter > 0) {
+        ok = wait_load(0);
+        if (ok) {
+          tc_fence_after();
+          issue_s(0, 0);
+          issue_s(1, 0);
+          mma_commit(bar(kKVEmpty + 0));
+        }
+        for (int it = 0; it < n_iter && ok; ++it) {
+          const int iv = 2 * it + 1, ik = 2 * it + 2;
+          const bool more = it + 1 < n_iter;
+          if (!(ok = wait_load(iv))) break;
+          if (!(ok = mbar_wait(bar(kPFull + 0), it & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
+          tc_fence_after();
+          issue_pv(0, iv, it > 0);
+          if (more) {
+            if (!(ok = wait_load(ik))) break;
+            if (!(ok = mbar_wait(bar(kSFree + 0), it & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
+            tc_fence_after();
+            issue_s(0, ik);
+          }
+          if (!(ok = mbar_wait(bar(kPFull + 1), it & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
+          tc_fence_after();
+          issue_pv(1, iv, it > 0);
+          mma_commit(bar(kKVEmpty + iv % NS));
+          if (more) {
+            if (!(ok = mbar_wait(bar(kSFree + 1), it & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
+            tc_fence_after();
+            issue_s(1, ik);
+            mma_commit(bar(kKVEmpty + ik % NS));
+          }
+        }
+      }
+      mma_commit(bar(kDrain));
+      drain_wait(bar(kDrain), 0, p.timeout_ns);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax
+    const int t = (warp - 4) >> 2;
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const int r_local = q0 + t * kBM + row;
+    const int64_t gi = (int64_t)r_local + p.q_off;
+    const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
+    const uint32_t tS = tmem + lane_base + L::kTmemS + t * kBN;
+    const uint32_t tO = tmem + lane_base + L::kTmemO + t * D;
+    const float sl2 = p.scale * kLog2e;
+    const float cap_in = CAP ? p.scale / p.soft_cap : 0.f;
+    const float cap_out = CAP ? p.soft_cap * kLog2e : 0.f;
+    const float slope2 = ALIBI ? p.alibi[hq] * kLog2e : 0.f;
+    const int tr0 = q0 + t * kBM;
+    uint8_t* Pt = smem + L::kOffP + t * L::kPBytes;
+    float m = neg_inf(), l = 0.f;
+    bool ok = true;
+
+    for (int it = 0; it < n_iter; ++it) {
+      const int c0 = (jlo + it) * kBN;
+      uint32_t wbar = bar(kSFull + t), wpar = (uint32_t)(it & 1);
+      if ((p.debug_flags & BFA_DEBUG_INJECT_STALL) && t == 0 && it == 0) {
+        wbar = bar(kNever);
+        wpar = 0;
+      }
+      if (!(ok = warp_wait(wbar, wpar, ctl))) break;
+      tc_fence_after();
+      uint32_t sr[kBN];
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c)
+        tmem_ld32(tS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&sr[32 * c]));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kSFree + t));
+
+      const bool full = tile_full(p, tr0, tr0 + kBM, c0, c0 + kBN);
+      const float abase = ALIBI ? slope2 * (float)(gi - (int64_t)c0 - p.k_off) : 0.f;
+      float s[kBN];
+      float mx = neg_inf();
+#pragma unroll
+      for (int c = 0; c < kBN; ++c) {
+        const float raw = __uint_as_float(sr[c]);
+        float x = CAP ? cap_out * tanh_exp(raw * cap_in) : raw * sl2;
+        if (ALIBI) x = fmaf(-slope2, (float)c, x + abase);
+        if (!full) {
+          const int64_t gj = (int64_t)c0 + c + p.k_off;
+          const bool keep = (c0 + c < p.Sk) && keep_pair(gi, gj, p.causal, p.window);
+          x = keep ? x : neg_inf();
+        }
+        s[c] = x;
+        mx = fmaxf(mx, x);
+      }
+      const float m_new = fmaxf(m, mx);
+      const float m_use = (m_new == neg_inf()) ? 0.f : m_new;
+      const float alpha = ex2(m - m_use);
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < kBN; ++c) {
+        s[c] = ex2(s[c] - m_use);
+        rs += s[c];
+      }
+      l = l * alpha + rs;
+      if (it > 0) {
+        if (!(ok = warp_wait(bar(kODone + t), (uint32_t)((it - 1) & 1), ctl))) break;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tO + 32 * c, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st32(tO + 32 * c, r);
+          }
+          tmem_st_wait();
+        }
+      }
+      m = m_new;
+#pragma unroll
+      for (int c16 = 0; c16 < kBN / 8; ++c16) {
+        uint4 v;
+        if (BF16) {
+          v.x = pack_bf16(s[8 * c16 + 0], s[8 * c16 + 1]);
+          v.y = pack_bf16(s[8 * c16 + 2], s[8 * c16 + 3]);
+          v.z = pack_bf16(s[8 * c16 + 4], s[8 * c16 + 5]);
+          v.w = pack_bf16(s[8 * c16 + 6], s[8 * c16 + 7]);
+        } else {
+          v.x = pack_f16(s[8 * c16 + 0], s[8 * c16 + 1]);
+          v.y = pack_f16(s[8 * c16 + 2], s[8 * c16 + 3]);
+          v.z = pack_f16(s[8 * c16 + 4], s[8 * c16 + 5]);
+          v.w = pack_f16(s[8 * c16 + 6], s[8 * c16 + 7]);
+        }
+        *reinterpret_cast<uint4*>(Pt + (c16 >> 3) * (kBM * 128) + sw128_offset(row, c16 & 7)) = v;
+      }
+      fence_async_shared();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kPFull + t));
+    }
+
+    // ------------------------------------------------------------ epilogue
+    bool good = ok;
+    if (good && n_iter > 0) good = warp_wait(bar(kODone + t), (uint32_t)((n_iter - 1) & 1), ctl);
+    if (good) {
+      tc_fence_after();
+      const float inv = (l > 0.f) ? 1.f / l : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        if (n_iter > 0) {
+          tmem_ld32(tO + 32 * c, r);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = 0u;
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float f[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(r[8 * q + i]) * inv;
+          uint4 v;
+          if (BF16) {
+            v.x = pack_bf16(f[0], f[1]); v.y = pack_bf16(f[2], f[3]);
+            v.z = pack_bf16(f[4], f[5]); v.w = pack_bf16(f[6], f[7]);
+          } else {
+            v.x = pack_f16(f[0], f[1]); v.y = pack_f16(f[2], f[3]);
+            v.z = pack_f16(f[4], f[5]); v.w = pack_f16(f[6], f[7]);
+          }
+          const int col = 32 * c + 8 * q;
+          *reinterpret_cast<uint4*>(Pt + (col >> 6) * (kBM * 128) + sw128_offset(row, (col & 63) >> 3)) = v;
+        }
+      }
+      fence_async_shared();
+    }
+    if (lane == 0) warp_ok[warp - 4] = good ? 1 : 0;
+    named_sync(1 + t, 128);
+    if (wq == 0 && lane == 0) {
+      const bool all = warp_ok[4 * t] && warp_ok[4 * t + 1] && warp_ok[4 * t + 2] && warp_ok[4 * t + 3];
+      if (all) {
+        for (int s = 0; s < L::kSub; ++s)
+          tma_store_4d(&tmO, smem_u32(Pt) + s * (kBM * 128), s * 64, tr0, hq, b);
+        tma_store_commit();
+        tma_store_wait_all();
+      }
+    }
+    if (good && r_local < p.Sq) {
+      p.lse[((int64_t)b * p.Hq + hq) * p.Sq + r_local] =
+          (l > 0.f) ? (m + lg2(l)) * kLn2 : neg_inf();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int D, bool BF16, bool CAP, bool ALIBI>
+int launch_fwd(const Params& p, const Tmaps4& tm, cudaStream_t st) {
+  using L = FwdLayout<D>;
+  auto kern = fwd_kernel<D, BF16, CAP, ALIBI>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)L::kSmemBytes);
+  });
+  if (attr_err != cudaSuccess) return BFA_ERR_CUDA;
+  const int n_mblk = (p.Sq + 2 * kBM - 1) / (2 * kBM);
+  const unsigned grid = (unsigned)n_mblk * (unsigned)p.B * (unsigned)p.Hq;
+  kern<<<grid, kThreads, L::kSmemBytes, st>>>(tm.m[0], tm.m[1], tm.m[2], tm.m[3], p);
+  note_launch();
+  return cudaGetLastError() == cudaSuccess ? BFA_OK : BFA_ERR_CUDA;
+}
+
+template <int D, bool BF16>
+int dispatch_flags(const Params& p, const Tmaps4& tm, cudaStream_t st) {
+  const bool cap = p.soft_cap > 0.f, alibi = p.alibi != nullptr;
+  if (cap && alibi) return launch_fwd<D, BF16, true, true>(p, tm, st);
+  if (cap) return launch_fwd<D, BF16, true, false>(p, tm, st);
+  if (alibi) return launch_fwd<D, BF16, false, true>(p, tm, st);
+  return launch_fwd<D, BF16, false, false>(p, tm, st);
+}
+
+}  // namespace
+
+bool sm100_fwd_eligible(const Params& p, int dtype) {
+  if (dtype != BFA_DTYPE_BF16 && dtype != BFA_DTYPE_F16) return false;
+  if (p.D != 64 && p.D != 128) return false;
+  if (p.Sq < 1 || p.Sk < 1 || p.B < 1 || p.Hq < 1) return false;
+  if (!device_is_sm100()) return false;
+  return tma_layout_ok(p.q, p.sq_, 2) && tma_layout_ok(p.k, p.sk_, 2) &&
+         tma_layout_ok(p.v, p.sv_, 2) && tma_layout_ok(p.o, p.so_, 2);
+}
+
+int sm100_fwd(const Params& p, int dtype, cudaStream_t st) {
+  Tmaps4 tm;
+  if (!make_tmap_bhsd(&tm.m[0], p.q, dtype, p.D, p.Sq, p.Hq, p.B, p.sq_, kBM) ||
+      !make_tmap_bhsd(&tm.m[1], p.k, dtype, p.D, p.Sk, p.Hkv, p.B, p.sk_, kBN) ||
+      !make_tmap_bhsd(&tm.m[2], p.v, dtype, p.D, p.Sk, p.Hkv, p.B, p.sv_, kBN) ||
+      !make_tmap_bhsd(&tm.m[3], p.o, dtype, p.D, p.Sq, p.Hq, p.B, p.so_, kBM))
+    return simt_fwd(p, dtype, st);
+  const bool bf16 = dtype == BFA_DTYPE_BF16;
+  if (p.D == 64) return bf16 ? dispatch_flags<64, true>(p, tm, st) : dispatch_flags<64, false>(p, tm, st);
+  return bf16 ? dispatch_flags<128, true>(p, tm, st) : dispatch_flags<128, false>(p, tm, st);
+}
+
+}  // namespace bfa

@@ -1,0 +1,320 @@
+"""B200 flash attention with the operator surface of npu_flash_attention.py.
+
+Drop-in replacement for dropletzhu/npu-flex-att's ``npu_flash_attention``
+module: the same function names, arguments, defaults, return values, layouts
+([B, H, S, D]) and errors. Every call runs hand-written sm_100a CUDA kernels
+through the C ABI of ``libbfa.so`` (include/bfa.h); there is no Triton, no
+multi-backend dispatch and no CPU fallback.
+
+Reference map (file:line in npu_flash_attention.py):
+  npu_flash_attention_forward   :606-656
+  npu_flash_attention_backward  :659-739
+  NPUFlexAttention              :742-781
+  npu_flex_attention            :784-794
+  AttentionConfig               :820-844
+  flex_attention                :847-886
+
+Differences that are deliberate:
+  * ``block_m`` / ``block_n`` are accepted for compatibility and ignored; the
+    kernels pick their own tiles (128 x 128 on the tcgen05 path).
+  * The backward honours ``alibi_slope`` and returns the true gradient of the
+    forward (the reference backward drops the slopes, :663, :696-732).
+  * Key columns past the key length never enter the softmax (the reference's
+    non-causal path lets zero-padded keys in, :98, :125).
+"""
+from __future__ import annotations
+
+import math
+import os
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+import bfa_lib as _bfa
+
+__all__ = [
+    "npu_flash_attention_forward",
+    "npu_flash_attention_backward",
+    "NPUFlexAttention",
+    "npu_flex_attention",
+    "AttentionConfig",
+    "flex_attention",
+    "check_device_status",
+]
+
+_CHECK_STATUS = os.environ.get("BFA_CHECK_STATUS", "0") == "1"
+
+
+def _fast_layout(t: torch.Tensor) -> torch.Tensor:
+    """Give 16-bit tensors a layout the TMA path can read (unit inner stride,
+    16-byte aligned outer strides); other tensors pass through unchanged and
+    the library's generic CUDA kernels handle their strides."""
+    if t.dtype not in (torch.float16, torch.bfloat16):
+        return t
+    ok = (t.stride(-1) == 1 and t.data_ptr() % 16 == 0
+          and all(s > 0 and (s * 2) % 16 == 0 for s in t.stride()[:-1]))
+    return t if ok else t.contiguous()
+
+
+def _problem(query, key, causal, sliding_window, alibi, scale, soft_cap, q_pos=0, k_pos=0):
+    B, Hq, Sq, D = query.shape
+    _, Hkv, Sk, _ = key.shape
+    pr = _bfa.Problem()
+    pr.batch, pr.heads_q, pr.heads_kv = B, Hq, Hkv
+    pr.seqlen_q, pr.seqlen_k, pr.head_dim = Sq, Sk, D
+    pr.dtype = _bfa.bfa_dtype(query.dtype)
+    pr.causal = 1 if causal else 0
+    pr.sliding_window = int(sliding_window)
+    pr.scale = float(scale)
+    pr.soft_cap = float(soft_cap)
+    pr.alibi_slopes = alibi.data_ptr() if alibi is not None else None
+    pr.q_pos_offset, pr.k_pos_offset = int(q_pos), int(k_pos)
+    return pr
+
+
+def _alibi(alibi_slope, hq: int, device) -> Optional[torch.Tensor]:
+    if alibi_slope is None:
+        return None
+    a = torch.as_tensor(alibi_slope, dtype=torch.float32).to(device).reshape(-1).contiguous()
+    if a.numel() != hq:
+        raise RuntimeError(f"alibi_slope must have one slope per query head ({hq}), got {a.numel()}")
+    return a
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("npu_flash_attention (B200 build) needs CUDA tensors; "
+                               "there is no CPU path")
+
+
+def _after_call(device):
+    if _CHECK_STATUS:
+        check_device_status(device)
+
+
+def check_device_status(device=None) -> None:
+    """Synchronise and raise if a kernel on `device` reported a device-side
+    timeout since the last check (then clear the report)."""
+    device = torch.device(device) if device is not None else torch.device(
+        "cuda", torch.cuda.current_device())
+    code = _bfa.read_and_clear_status(device)
+    if code != 0:
+        _bfa.check(code)
+
+
+def npu_flash_attention_forward(
+    query, key, value,
+    causal=False,
+    sliding_window=0,
+    alibi_slope=None,
+    scale=None,
+    block_m=16,
+    block_n=64,
+    return_lse=False,
+    soft_cap=0.0,
+    *,
+    q_pos_offset=0,
+    k_pos_offset=0,
+    _wait_timeout_ns=0,
+    _debug_flags=0,
+):
+    """Attention forward: O (and the fp32 natural-log LSE when `return_lse`).
+
+    Mirrors npu_flash_attention.py:606-656. Keyword-only extras (not in the
+    reference): absolute position offsets for context-parallel shards.
+    """
+    B, Hq, Sq, D = query.shape
+    Bk, Hkv, Sk, Dk = key.shape
+    Bv, Hkv2, Sv, Dv = value.shape
+    assert D == Dk, "Q and K head dims must match"
+    assert Dv == D, "V head dim must match Q head dim for this kernel"
+    assert Hq % Hkv == 0, "Hq must be divisible by Hkv"
+    _require_cuda(query, key, value)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    dev = query.device
+    alibi = _alibi(alibi_slope, Hq, dev)
+    q, k, v = _fast_layout(query), _fast_layout(key), _fast_layout(value)
+    O = torch.empty_like(query)
+    o_k = _fast_layout(O) if O.data_ptr() else O
+    LSE = torch.empty(B, Hq, Sq, device=dev, dtype=torch.float32)
+    lib = _bfa.load()
+    pr = _problem(q, k, causal, sliding_window, alibi, scale, soft_cap, q_pos_offset, k_pos_offset)
+    args = _bfa.FwdArgs()
+    args.q, args.k, args.v, args.o = _bfa.tensor(q), _bfa.tensor(k), _bfa.tensor(v), _bfa.tensor(o_k)
+    args.lse = LSE.data_ptr()
+    args.status = _bfa.status_word(dev).data_ptr()
+    args.wait_timeout_ns = int(_wait_timeout_ns)
+    args.debug_flags = int(_debug_flags)
+    with torch.cuda.device(dev):
+        _bfa.check(lib.bfa_fwd(pr, args, _bfa.stream_ptr(dev)))
+    if o_k is not O:
+        O.copy_(o_k)
+    _after_call(dev)
+    if return_lse:
+        return O, LSE
+    return O
+
+
+def npu_flash_attention_backward(
+    query, key, value, out, lse, grad_out,
+    causal=False,
+    sliding_window=0,
+    alibi_slope=None,
+    scale=None,
+    block_m=16,
+    block_n=32,
+    soft_cap=0.0,
+    *,
+    q_pos_offset=0,
+    k_pos_offset=0,
+    _wait_timeout_ns=0,
+    _debug_flags=0,
+    _phases=0,
+    _workspace=None,
+    _outputs=None,
+):
+    """Attention backward: (dQ, dK, dV), dK/dV summed over each GQA group.
+
+    ``_phases`` / ``_workspace`` / ``_outputs`` (internal) let a benchmark
+    launch Δ, dK/dV and dQ as separate calls on one workspace and reuse the
+    gradient buffers, so each kernel can be timed on its own.
+
+    Mirrors npu_flash_attention.py:659-739; Δ, both gradient kernels and the
+    GQA reduction run on the device in one library call.
+    """
+    B, Hq, Sq, D = query.shape
+    Bk, Hkv, Sk, Dk = key.shape
+    assert D == Dk, "Q and K head dims must match"
+    assert Hq % Hkv == 0, "Hq must be divisible by Hkv"
+    assert out is not None, "backward requires forward output `out` to compute Delta"
+    _require_cuda(query, key, value, out, lse, grad_out)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    dev = query.device
+    alibi = _alibi(alibi_slope, Hq, dev)
+    q, k, v = _fast_layout(query), _fast_layout(key), _fast_layout(value)
+    o, do = _fast_layout(out), _fast_layout(grad_out.to(query.dtype))
+    lse_c = lse.to(torch.float32).contiguous()
+    if _outputs is not None:
+        DQ, DK, DV = _outputs
+    else:
+        DQ = torch.empty_like(query)
+        DK = torch.empty(B, Hkv, Sk, D, device=dev, dtype=key.dtype)
+        DV = torch.empty(B, Hkv, Sk, D, device=dev, dtype=value.dtype)
+    dq_k = _fast_layout(DQ) if DQ.data_ptr() else DQ
+    lib = _bfa.load()
+    pr = _problem(q, k, causal, sliding_window, alibi, scale, soft_cap, q_pos_offset, k_pos_offset)
+    args = _bfa.BwdArgs()
+    args.q, args.k, args.v = _bfa.tensor(q), _bfa.tensor(k), _bfa.tensor(v)
+    args.o, args.dout = _bfa.tensor(o), _bfa.tensor(do)
+    args.lse = lse_c.data_ptr()
+    args.dq, args.dk, args.dv = _bfa.tensor(dq_k), _bfa.tensor(DK), _bfa.tensor(DV)
+    args.status = _bfa.status_word(dev).data_ptr()
+    args.wait_timeout_ns = int(_wait_timeout_ns)
+    args.debug_flags = int(_debug_flags)
+    args.phases = int(_phases)
+    ws_bytes = lib.bfa_bwd_workspace_bytes(pr)
+    ws = _workspace if _workspace is not None else torch.empty(
+        max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    assert ws.numel() >= ws_bytes
+    with torch.cuda.device(dev):
+        _bfa.check(lib.bfa_bwd(pr, args, ws.data_ptr(), ws_bytes, _bfa.stream_ptr(dev)))
+    if dq_k is not DQ:
+        DQ.copy_(dq_k)
+    _after_call(dev)
+    return DQ, DK, DV
+
+
+class NPUFlexAttention(torch.autograd.Function):
+    """Autograd wrapper (npu_flash_attention.py:742-781)."""
+
+    @staticmethod
+    def forward(ctx, query, key, value, causal=False, sliding_window=0,
+                alibi_slope=None, scale=None, block_m=16, block_n=64, soft_cap=0.0):
+        ctx.causal = causal
+        ctx.sliding_window = sliding_window
+        ctx.alibi_slope = alibi_slope
+        ctx.scale = scale
+        ctx.block_m = block_m
+        ctx.block_n = block_n
+        ctx.soft_cap = soft_cap
+        with torch.no_grad():
+            out, lse = npu_flash_attention_forward(
+                query, key, value,
+                causal=causal, sliding_window=sliding_window,
+                alibi_slope=alibi_slope, scale=scale,
+                block_m=block_m, block_n=block_n, return_lse=True,
+                soft_cap=soft_cap,
+            )
+        ctx.save_for_backward(query, key, value, lse, out)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        query, key, value, lse, out = ctx.saved_tensors
+        DQ, DK, DV = npu_flash_attention_backward(
+            query, key, value, out, lse, grad_out,
+            causal=ctx.causal, sliding_window=ctx.sliding_window,
+            alibi_slope=ctx.alibi_slope, scale=ctx.scale,
+            block_m=ctx.block_m, block_n=ctx.block_n,
+            soft_cap=ctx.soft_cap,
+        )
+        return DQ, DK, DV, None, None, None, None, None, None, None
+
+
+def npu_flex_attention(
+    query, key, value,
+    causal=False, sliding_window=0,
+    alibi_slope=None, scale=None,
+    block_m=16, block_n=64,
+    soft_cap=0.0,
+):
+    """Differentiable attention (npu_flash_attention.py:784-794)."""
+    return NPUFlexAttention.apply(
+        query, key, value, causal, sliding_window,
+        alibi_slope, scale, block_m, block_n, soft_cap,
+    )
+
+
+@dataclass
+class AttentionConfig:
+    """Composable attention pattern (npu_flash_attention.py:820-844).
+
+    Example -- Gemma2-style attention:
+        config = AttentionConfig(causal=True, sliding_window=1024, soft_cap=50.0)
+        out = flex_attention(q, k, v, config=config)
+    """
+    causal: bool = False
+    sliding_window: int = 0
+    alibi_slope: Optional[torch.Tensor] = None
+    scale: Optional[float] = None
+    soft_cap: float = 0.0
+    block_m: int = 16
+    block_n: int = 64
+
+    def __post_init__(self):
+        if self.sliding_window < 0:
+            raise ValueError("sliding_window must be >= 0")
+        if self.soft_cap < 0:
+            raise ValueError("soft_cap must be >= 0")
+
+
+def flex_attention(query, key, value, config: Optional[AttentionConfig] = None, **kwargs):
+    """Config-driven entry (npu_flash_attention.py:847-886): builds an
+    AttentionConfig from kwargs when no config is given (kwargs are ignored
+    when one is) and runs the differentiable attention."""
+    if config is None:
+        config = AttentionConfig(**kwargs)
+    return npu_flex_attention(
+        query, key, value,
+        causal=config.causal,
+        sliding_window=config.sliding_window,
+        alibi_slope=config.alibi_slope,
+        scale=config.scale,
+        block_m=config.block_m,
+        block_n=config.block_n,
+        soft_cap=config.soft_cap,
+    )

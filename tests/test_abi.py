@@ -1,0 +1,88 @@
+"""The C-ABI library loads and exports every entry point include/bfa.h declares.
+
+CPU-only: the calls made here are rejected by argument validation before any
+CUDA work, so no GPU is needed.
+"""
+import ctypes
+import os
+import re
+
+import pytest
+
+import bfa_lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "bfa.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|uint64_t|const char\*)\s+(bfa_\w+)\s*\(",
+                                 text, re.M)))
+
+
+def test_header_matches_binding_list():
+    assert declared_symbols() == sorted(bfa_lib.EXPORTED)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = bfa_lib.load()
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert lib.bfa_abi_version() == bfa_lib.ABI_VERSION
+
+
+def test_strerror_covers_every_status():
+    lib = bfa_lib.load()
+    for code in range(0, -7, -1):
+        msg = lib.bfa_strerror(code).decode()
+        assert msg and "unknown" not in msg
+    assert "unknown" in lib.bfa_strerror(-99).decode()
+
+
+def _problem(**kw):
+    pr = bfa_lib.Problem()
+    pr.batch, pr.heads_q, pr.heads_kv = 1, 4, 2
+    pr.seqlen_q, pr.seqlen_k, pr.head_dim = 16, 16, 64
+    pr.dtype, pr.scale = bfa_lib.DTYPE_BF16, 0.125
+    for k, v in kw.items():
+        setattr(pr, k, v)
+    return pr
+
+
+@pytest.mark.parametrize("kw,code", [
+    ({"heads_q": 3, "heads_kv": 2}, -2),     # Hq % Hkv != 0 (reference asserts, :622)
+    ({"head_dim": 300}, -3),                 # beyond 256
+    ({"dtype": 7}, -3),                      # no such dtype
+    ({"batch": -1}, -1),
+    ({"sliding_window": -4}, -1),            # AttentionConfig rejects it too (:841-842)
+    ({"soft_cap": -1.0}, -1),
+    ({"heads_kv": 0}, -1),
+])
+def test_fwd_rejects_bad_problems_before_any_cuda_work(kw, code):
+    lib = bfa_lib.load()
+    args = bfa_lib.FwdArgs()
+    assert lib.bfa_fwd(ctypes.byref(_problem(**kw)), ctypes.byref(args), None) == code
+
+
+def test_null_arguments_are_rejected():
+    lib = bfa_lib.load()
+    assert lib.bfa_fwd(None, None, None) == -1
+    assert lib.bfa_fwd(ctypes.byref(_problem()), ctypes.byref(bfa_lib.FwdArgs()), None) == -1
+    ws = lib.bfa_bwd_workspace_bytes(ctypes.byref(_problem()))
+    assert ws >= 4 * 16 * 4
+    assert lib.bfa_bwd(ctypes.byref(_problem()), ctypes.byref(bfa_lib.BwdArgs()), None, 0, None) == -1
+
+
+def test_empty_problem_is_a_no_op():
+    lib = bfa_lib.load()
+    # B*Hq*Sq == 0: nothing to compute, nothing launched.
+    assert lib.bfa_fwd(ctypes.byref(_problem(seqlen_q=0)), ctypes.byref(bfa_lib.FwdArgs()), None) == 0
+
+
+def test_merge_partial_validates():
+    lib = bfa_lib.load()
+    t = bfa_lib.Tensor()
+    assert lib.bfa_merge_partial(1, 1, 1, 0, t, 0, None, t, 0, None, None) == -1
+    assert lib.bfa_merge_partial(1, 1, 1, 64, t, 9, None, t, 0, None, None) == -3
+    assert lib.bfa_merge_partial(0, 1, 1, 64, t, 0, None, t, 0, None, None) == 0

@@ -1,0 +1,73 @@
+"""Host-side behaviour of the drop-in module (CPU only, no kernels run).
+
+Mirrors the reference's argument handling: AttentionConfig validation
+(npu_flash_attention.py:840-844), flex_attention's config/kwargs rule
+(:875-876) and the shape assertions (:620-622, tested by
+test/test_real_world.py:65-85).
+"""
+import inspect
+
+import pytest
+import torch
+
+import npu_flash_attention as nfa
+
+
+def test_attention_config_validation():
+    with pytest.raises(ValueError):
+        nfa.AttentionConfig(sliding_window=-1)
+    with pytest.raises(ValueError):
+        nfa.AttentionConfig(soft_cap=-0.5)
+    cfg = nfa.AttentionConfig(causal=True, sliding_window=1024, soft_cap=50.0)
+    assert (cfg.causal, cfg.sliding_window, cfg.soft_cap, cfg.block_m, cfg.block_n) == (True, 1024, 50.0, 16, 64)
+
+
+def test_signatures_match_reference():
+    sig = inspect.signature(nfa.npu_flash_attention_forward)
+    names = list(sig.parameters)[:11]
+    assert names == ["query", "key", "value", "causal", "sliding_window", "alibi_slope",
+                     "scale", "block_m", "block_n", "return_lse", "soft_cap"]
+    assert sig.parameters["block_m"].default == 16 and sig.parameters["block_n"].default == 64
+    sig = inspect.signature(nfa.npu_flash_attention_backward)
+    names = list(sig.parameters)[:13]
+    assert names == ["query", "key", "value", "out", "lse", "grad_out", "causal",
+                     "sliding_window", "alibi_slope", "scale", "block_m", "block_n", "soft_cap"]
+    assert sig.parameters["block_n"].default == 32
+    sig = inspect.signature(nfa.npu_flex_attention)
+    assert list(sig.parameters) == ["query", "key", "value", "causal", "sliding_window",
+                                    "alibi_slope", "scale", "block_m", "block_n", "soft_cap"]
+
+
+def test_shape_assertions_fire_before_device_work():
+    q = torch.randn(1, 1, 8, 64)
+    with pytest.raises(AssertionError):
+        nfa.npu_flash_attention_forward(q, torch.randn(1, 1, 8, 128), torch.randn(1, 1, 8, 64))
+    with pytest.raises(AssertionError):
+        nfa.npu_flash_attention_forward(torch.randn(1, 3, 8, 64), torch.randn(1, 2, 8, 64),
+                                        torch.randn(1, 2, 8, 64))
+    with pytest.raises(AssertionError):
+        nfa.npu_flash_attention_forward(q, q, torch.randn(1, 1, 8, 32))
+    with pytest.raises(AssertionError):
+        nfa.npu_flash_attention_backward(q, q, q, None, torch.zeros(1, 1, 8), q)
+
+
+def test_cpu_tensors_are_refused_not_computed():
+    q = torch.randn(1, 1, 8, 64)
+    with pytest.raises(RuntimeError, match="no CPU path"):
+        nfa.npu_flash_attention_forward(q, q, q)
+
+
+def test_flex_attention_ignores_kwargs_when_config_given(monkeypatch):
+    seen = {}
+
+    def fake(query, key, value, **kw):
+        seen.update(kw)
+        return query
+    monkeypatch.setattr(nfa, "npu_flex_attention", fake)
+    cfg = nfa.AttentionConfig(causal=True, soft_cap=3.0)
+    nfa.flex_attention(torch.zeros(1), torch.zeros(1), torch.zeros(1), config=cfg, causal=False)
+    assert seen["causal"] is True and seen["soft_cap"] == 3.0
+    nfa.flex_attention(torch.zeros(1), torch.zeros(1), torch.zeros(1), sliding_window=7)
+    assert seen["sliding_window"] == 7 and seen["causal"] is False
+    with pytest.raises(ValueError):
+        nfa.flex_attention(torch.zeros(1), torch.zeros(1), torch.zeros(1), sliding_window=-2)
