@@ -1,12 +1,741 @@
-// sm100_bwd.cu -- tcgen05 / TMA backward kernels (dK/dV and dQ) for B200.
+// sm100_bwd.cu -- tcgen05 / TMA / TMEM attention backward for B200.
+//
+// Replaces flash_attn_bwd_dkdv_kernel (npu_flash_attention.py:407-560),
+// flash_attn_bwd_dq_kernel (:298-402) and the host GQA sum (:735-737) for
+// bf16/fp16 inputs with head_dim 64 or 128. Per pair (i, j):
+//   P  = exp(u_ij − lse_i)        u = transformed logit (cap, ALiBi), masked
+//   dP = dO_i · V_j
+//   dS = P ∘ (dP − Δ_i) · scale · (1 − tanh²)   (tanh term only with soft-cap)
+//   dV_j += P_ij dO_i,  dK_j += dS_ij Q_i,  dQ_i += dS_ij K_j
+// ALiBi enters P exactly as in the forward, so these are the true gradients
+// of the forward (the reference backward leaves the slopes out).
+//
+// dkdv_kernel: one CTA per (batch, kv-head, 128-key tile); loops over the
+//   GQA group's q-heads and their 64-row query tiles, so dK/dV are summed over
+//   the group in fp32 TMEM -- no per-q-head copies, no atomics, deterministic.
+//   MMAs (M = 128 keys): Sᵀ = K Qᵢᵀ, dPᵀ = V dOᵢᵀ (N = 64), then
+//   dV += Pᵀ dOᵢ and dK += dSᵀ Qᵢ (N = D, B operand MN-major).
+// dq_kernel: one CTA per (batch, q-head, 128-row query tile); loops over
+//   64-key tiles: S = Q Kⱼᵀ, dP = dO Vⱼᵀ, dQ += dS Kⱼ.
+// Warp roles in both: warp 0 TMA producer (+ LSE/Δ staging), warp 1 MMA
+// issuer, warp 2 TMEM allocator, warps 4-7 elementwise (one row per thread).
+// S/dP are double-buffered in TMEM so the MMAs of step i+1 overlap the
+// elementwise work of step i.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "bfa_internal.h"
+#include "sm100_host.h"
+#include "sm100_ptx.cuh"
 
 namespace bfa {
+namespace {
 
-bool sm100_bwd_eligible(const Params&, int) { return false; }
+using namespace sm100;
 
-int sm100_bwd(const Params& p, int dtype, cudaStream_t st) { return simt_bwd(p, dtype, st); }
+constexpr int kThreads = 256;
+constexpr int kRows = 128;  // TMEM lanes / rows owned by the elementwise warps
+constexpr int kInner = 64;  // columns of one S/dP step
+
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const WaitCtl& ctl) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, ctl, BFA_ERR_DEVICE_TIMEOUT) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
+
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, uint64_t timeout_ns) {
+  if (mbar_try_wait(bar, parity)) return;
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > timeout_ns) return;
+  }
+}
+
+__device__ __forceinline__ bool tile_full(const Params& p, int r0, int r1, int c0, int c1) {
+  if (r1 > p.Sq || c1 > p.Sk) return false;
+  const int64_t i_min = r0 + p.q_off, i_max = r1 - 1 + p.q_off;
+  const int64_t j_min = c0 + p.k_off, j_max = c1 - 1 + p.k_off;
+  if (p.causal && j_max > i_min) return false;
+  if (p.window > 0 && i_max - j_min > p.window) return false;
+  return true;
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  return BF16 ? pack_bf16(a, b) : pack_f16(a, b);
+}
+
+// Logit in the base-2 domain: (cap·tanh(s·scale/cap) or s·scale)·log2(e).
+// `t` receives tanh(s·scale/cap) for the soft-cap chain.
+template <bool CAP>
+__device__ __forceinline__ float logit2(float raw, float sl2, float cap_in, float cap_out, float* t) {
+  if (CAP) {
+    const float th = tanh_exp(raw * cap_in);
+    *t = th;
+    return cap_out * th;
+  }
+  *t = 0.f;
+  return raw * sl2;
+}
+
+// Write one row of 64 fp32 values as 16-bit into a 128B-swizzled sub-tile.
+template <bool BF16>
+__device__ __forceinline__ void store_row64(uint8_t* tile, int row, const float* v) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint4 w;
+    w.x = pack2<BF16>(v[8 * c + 0], v[8 * c + 1]);
+    w.y = pack2<BF16>(v[8 * c + 2], v[8 * c + 3]);
+    w.z = pack2<BF16>(v[8 * c + 4], v[8 * c + 5]);
+    w.w = pack2<BF16>(v[8 * c + 6], v[8 * c + 7]);
+    *reinterpret_cast<uint4*>(tile + sw128_offset(row, c)) = w;
+  }
+}
+
+// Read a TMEM row of D fp32 columns, convert, and write it into a staging
+// area of D/64 swizzled sub-tiles of 128 rows (for a TMA store).
+template <int D, bool BF16>
+__device__ __forceinline__ void stage_tmem_row(uint32_t taddr, uint8_t* stage, int row, bool zero) {
+#pragma unroll 1
+  for (int c = 0; c < D / 32; ++c) {
+    uint32_t r[32];
+    if (!zero) {
+      tmem_ld32(taddr + 32 * c, r);
+      tmem_ld_wait();
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) r[i] = 0u;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 w;
+      w.x = pack2<BF16>(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
+      w.y = pack2<BF16>(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
+      w.z = pack2<BF16>(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
+      w.w = pack2<BF16>(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
+      const int col = 32 * c + 8 * q;
+      *reinterpret_cast<uint4*>(stage + (col >> 6) * (kRows * 128) + sw128_offset(row, (col & 63) >> 3)) = w;
+    }
+  }
+}
+
+// ============================================================== dK / dV
+template <int D>
+struct DkdvLayout {
+  static constexpr int kSub = D / 64;
+  static constexpr int kStages = (D <= 64) ? 4 : 2;
+  static constexpr uint32_t kKVBytes = kRows * D * 2;    // K or V tile (128 keys)
+  static constexpr uint32_t kQBytes = kInner * D * 2;    // Q or dO tile (64 rows)
+  static constexpr uint32_t kPBytes = kRows * kInner * 2;
+  static constexpr uint32_t kOffK = 0;
+  static constexpr uint32_t kOffV = kOffK + kKVBytes;
+  static constexpr uint32_t kOffStage = kOffV + kKVBytes;       // Q_s, dO_s per stage
+  static constexpr uint32_t kStageBytes = 2 * kQBytes;
+  static constexpr uint32_t kOffPT = kOffStage + kStages * kStageBytes;  // Pᵀ[2], dSᵀ[2]
+  static constexpr uint32_t kOffDS = kOffPT + 2 * kPBytes;
+  static constexpr uint32_t kOffRow = kOffDS + 2 * kPBytes;     // lse2[64], delta[64] per stage
+  static constexpr uint32_t kOffBar = kOffRow + kStages * 512;
+  static constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
+  static constexpr uint32_t kTmemS = 0, kTmemDP = 128, kTmemDV = 256, kTmemDK = 256 + D;
+  static_assert(kTmemDK + D <= 512, "TMEM budget");
+  static_assert(kSmemBytes <= 232448, "smem budget");
+  static_assert(2 * kPBytes >= (uint32_t)kRows * D * 2, "staging for dV / dK");
+};
+
+template <int D, bool BF16, bool CAP, bool ALIBI>
+__global__ void __launch_bounds__(kThreads, 1)
+    dkdv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                const __grid_constant__ CUtensorMap tmDK, const __grid_constant__ CUtensorMap tmDV,
+                const Params p) {
+  using L = DkdvLayout<D>;
+  constexpr int NS = L::kStages;
+  enum {
+    kKVFull = 0,
+    kQFull = 1,
+    kQEmpty = 1 + NS,
+    kSPFull = 1 + 2 * NS,
+    kSPFree = kSPFull + 2,
+    kDSFull = kSPFree + 2,
+    kDSFree = kDSFull + 2,
+    kAccDone = kDSFree + 2,
+    kDrain = kAccDone + 1,
+    kNever = kDrain + 1,
+    kNumBars = kNever + 1
+  };
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  const uint32_t sbase = smem_u32(smem);
+  auto bar = [&](int i) -> uint32_t { return sbase + L::kOffBar + 8u * (uint32_t)i; };
+  uint32_t* tmem_slot = (uint32_t*)(smem + L::kOffBar + 8 * kNumBars);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  int* warp_ok = (int*)(tmem_slot + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_kt = (p.Sk + kRows - 1) / kRows;
+  const int kt = blockIdx.x % n_kt;
+  const int bh = blockIdx.x / n_kt;
+  const int hkv = bh % p.Hkv, b = bh / p.Hkv;
+  const int c0 = kt * kRows;
+  int qlo, qhi;
+  query_range(p, c0, min(c0 + kRows, p.Sk), &qlo, &qhi);
+  const int qt0 = qlo / kInner;
+  const int n_qt = (qhi > qlo) ? (qhi + kInner - 1) / kInner - qt0 : 0;
+  const int n_iter = n_qt * p.G;
+
+  WaitCtl ctl{abort_flag, p.status, p.timeout_ns};
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kNumBars; ++i) {
+      uint32_t cnt = 1;
+      if (i >= kQFull && i < kQFull + NS) cnt = 2;
+      if ((i >= kSPFree && i < kSPFree + 2) || (i >= kDSFull && i < kDSFull + 2)) cnt = 4;
+      mbar_init(bar(i), cnt);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(bar(kKVFull), 2 * L::kKVBytes);
+      for (int s = 0; s < L::kSub; ++s) {
+        tma_load_4d(sbase + L::kOffK + s * (kRows * 128), &tmK, bar(kKVFull), s * 64, c0, hkv, b);
+        tma_load_4d(sbase + L::kOffV + s * (kRows * 128), &tmV, bar(kKVFull), s * 64, c0, hkv, b);
+      }
+    }
+    int issued = 0;
+    for (int i = 0; i < n_iter; ++i) {
+      const int st = i % NS;
+      if (i >= NS && !warp_wait(bar(kQEmpty + st), ((i / NS) & 1) ^ 1, ctl)) break;
+      const int g = i / n_qt;
+      const int hq = hkv * p.G + g;
+      const int q0 = (qt0 + i % n_qt) * kInner;
+      const uint32_t qs = sbase + L::kOffStage + st * L::kStageBytes;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(bar(kQFull + st), L::kStageBytes);
+        for (int s = 0; s < L::kSub; ++s) {
+          tma_load_4d(qs + s * (kInner * 128), &tmQ, bar(kQFull + st), s * 64, q0, hq, b);
+          tma_load_4d(qs + L::kQBytes + s * (kInner * 128), &tmDO, bar(kQFull + st), s * 64, q0, hq, b);
+        }
+      }
+      float* rowv = (float*)(smem + L::kOffRow + st * 512);
+      const int64_t rbase = ((int64_t)b * p.Hq + hq) * p.Sq;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int r = lane + 32 * h;
+        const int qi = q0 + r;
+        float l2 = __int_as_float(0x7f800000), dl = 0.f;
+        if (qi < p.Sq) {
+          const float lse = p.lse[rbase + qi];
+          l2 = (lse == neg_inf()) ? __int_as_float(0x7f800000) : lse * kLog2e;
+          dl = p.delta[rbase + qi];
+        }
+        rowv[r] = l2;
+        rowv[64 + r] = dl;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kQFull + st));
+      issued = i + 1;
+    }
+    if (lane == 0) {
+      drain_wait(bar(kKVFull), 0, p.timeout_ns);
+      for (int i = (issued > NS ? issued - NS : 0); i < issued; ++i)
+        drain_wait(bar(kQFull + i % NS), (i / NS) & 1, p.timeout_ns);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idSP = idesc_f16(kRows, kInner, BF16, false);
+      constexpr uint32_t idAcc = idesc_f16(kRows, D, BF16, true);
+      auto stage = [&](int i) -> uint32_t { return sbase + L::kOffStage + (i % NS) * L::kStageBytes; };
+      auto issue_sp = [&](int i) {
+        const int bf = i & 1;
+        const uint32_t qa = stage(i), da = stage(i) + L::kQBytes;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t offkv = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
+          const uint32_t offq = (kk >> 2) * (kInner * 128) + (kk & 3) * 32;
+          mma_ss(tmem + L::kTmemS + 64 * bf, desc_kmajor(sbase + L::kOffK + offkv),
+                 desc_kmajor(qa + offq), idSP, kk > 0 ? 1u : 0u);
+          mma_ss(tmem + L::kTmemDP + 64 * bf, desc_kmajor(sbase + L::kOffV + offkv),
+                 desc_kmajor(da + offq), idSP, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(bar(kSPFull + bf));
+      };
+      bool ok = mbar_wait(bar(kKVFull), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
+      if (ok && n_iter > 0) {
+        ok = mbar_wait(bar(kQFull), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
+        if (ok) {
+          tc_fence_after();
+          issue_sp(0);
+        }
+      }
+      for (int i = 0; i < n_iter && ok; ++i) {
+        const int bf = i & 1, k = i >> 1;
+        if (i + 1 < n_iter) {
+          const int n1 = i + 1;
+          if (!(ok = mbar_wait(bar(kQFull + n1 % NS), (n1 / NS) & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
+          if (n1 >= 2 && !(ok = mbar_wait(bar(kSPFree + (n1 & 1)), ((n1 >> 1) - 1) & 1, ctl,
+                                          BFA_ERR_DEVICE_TIMEOUT)))
+            break;
+          tc_fence_after();
+          issue_sp(n1);
+        }
+        if (!(ok = mbar_wait(bar(kDSFull + bf), k & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
+        tc_fence_after();
+        const uint32_t qa = stage(i), da = stage(i) + L::kQBytes;
+        const uint32_t pt = sbase + L::kOffPT + bf * L::kPBytes;
+        const uint32_t ds = sbase + L::kOffDS + bf * L::kPBytes;
+#pragma unroll
+        for (int kk = 0; kk < kInner / 16; ++kk) {
+          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+          mma_ss(tmem + L::kTmemDV, desc_kmajor(pt + kk * 32),
+                 desc_mnmajor(da + kk * 2048, kInner * 128), idAcc, acc);
+          mma_ss(tmem + L::kTmemDK, desc_kmajor(ds + kk * 32),
+                 desc_mnmajor(qa + kk * 2048, kInner * 128), idAcc, acc);
+        }
+        mma_commit(bar(kDSFree + bf));
+        mma_commit(bar(kQEmpty + i % NS));
+      }
+      mma_commit(bar(kAccDone));
+      mma_commit(bar(kDrain));
+      drain_wait(bar(kDrain), 0, p.timeout_ns);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ elementwise
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;  // key row within the tile
+    const int kj = c0 + row;
+    const int64_t gj = (int64_t)kj + p.k_off;
+    const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
+    const float sl2 = p.scale * kLog2e;
+    const float cap_in = CAP ? p.scale / p.soft_cap : 0.f;
+    const float cap_out = CAP ? p.soft_cap * kLog2e : 0.f;
+    bool ok = true;
+    for (int i = 0; i < n_iter; ++i) {
+      const int bf = i & 1, k = i >> 1, st = i % NS;
+      const int g = i / n_qt;
+      const int hq = hkv * p.G + g;
+      const int q0 = (qt0 + i % n_qt) * kInner;
+      uint32_t wbar = bar(kSPFull + bf), wpar = (uint32_t)(k & 1);
+      if ((p.debug_flags & BFA_DEBUG_INJECT_STALL) && i == 0) {
+        wbar = bar(kNever);
+        wpar = 0;
+      }
+      if (!(ok = warp_wait(wbar, wpar, ctl))) break;
+      if (!(ok = warp_wait(bar(kQFull + st), (uint32_t)((i / NS) & 1), ctl))) break;
+      tc_fence_after();
+      uint32_t sr[64], dr[64];
+      tmem_ld32(tmem + lane_base + L::kTmemS + 64 * bf, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+      tmem_ld32(tmem + lane_base + L::kTmemS + 64 * bf + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      tmem_ld32(tmem + lane_base + L::kTmemDP + 64 * bf, *reinterpret_cast<uint32_t(*)[32]>(&dr[0]));
+      tmem_ld32(tmem + lane_base + L::kTmemDP + 64 * bf + 32, *reinterpret_cast<uint32_t(*)[32]>(&dr[32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kSPFree + bf));
+
+      const float* rowv = (const float*)(smem + L::kOffRow + st * 512);
+      const bool full = tile_full(p, q0, q0 + kInner, c0, c0 + kRows);
+      const float slope2 = ALIBI ? p.alibi[hq] * kLog2e : 0.f;
+      const float abase = ALIBI ? slope2 * (float)((int64_t)q0 + p.q_off - gj) : 0.f;
+      float pv[64], dsv[64];
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        float t;
+        float x = logit2<CAP>(__uint_as_float(sr[c]), sl2, cap_in, cap_out, &t);
+        if (ALIBI) x = fmaf(slope2, (float)c, x + abase);
+        float pr = ex2(x - rowv[c]);
+        if (!full) {
+          const int qi = q0 + c;
+          const bool keep = (qi < p.Sq) && (kj < p.Sk) && keep_pair((int64_t)qi + p.q_off, gj, p.causal, p.window);
+          pr = keep ? pr : 0.f;
+        }
+        float ds = pr * (__uint_as_float(dr[c]) - rowv[64 + c]) * p.scale;
+        if (CAP) ds *= (1.f - t * t);
+        pv[c] = pr;
+        dsv[c] = ds;
+      }
+      if (k >= 1 && !(ok = warp_wait(bar(kDSFree + bf), (uint32_t)((k - 1) & 1), ctl))) break;
+      store_row64<BF16>(smem + L::kOffPT + bf * L::kPBytes, row, pv);
+      store_row64<BF16>(smem + L::kOffDS + bf * L::kPBytes, row, dsv);
+      fence_async_shared();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kDSFull + bf));
+    }
+    bool good = ok;
+    if (good && n_iter > 0) good = warp_wait(bar(kAccDone), 0, ctl);
+    uint8_t* stage_dv = smem + L::kOffPT;  // Pᵀ[0..1] (32 KB) free once the MMAs are done
+    uint8_t* stage_dk = smem + L::kOffDS;
+    if (good) {
+      tc_fence_after();
+      stage_tmem_row<D, BF16>(tmem + lane_base + L::kTmemDV, stage_dv, row, n_iter == 0);
+      stage_tmem_row<D, BF16>(tmem + lane_base + L::kTmemDK, stage_dk, row, n_iter == 0);
+      fence_async_shared();
+    }
+    if (lane == 0) warp_ok[wq] = good ? 1 : 0;
+    named_sync(1, 128);
+    if (wq == 0 && lane == 0 && warp_ok[0] && warp_ok[1] && warp_ok[2] && warp_ok[3]) {
+      for (int s = 0; s < L::kSub; ++s) {
+        tma_store_4d(&tmDV, smem_u32(stage_dv) + s * (kRows * 128), s * 64, c0, hkv, b);
+        tma_store_4d(&tmDK, smem_u32(stage_dk) + s * (kRows * 128), s * 64, c0, hkv, b);
+      }
+      tma_store_commit();
+      tma_store_wait_all();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ============================================================== dQ
+template <int D>
+struct DqLayout {
+  static constexpr int kSub = D / 64;
+  static constexpr int kStages = (D <= 64) ? 6 : 3;
+  static constexpr uint32_t kQBytes = kRows * D * 2;     // Q or dO tile (128 rows)
+  static constexpr uint32_t kKVBytes = kInner * D * 2;   // K or V tile (64 keys)
+  static constexpr uint32_t kSBytes = kRows * kInner * 2;
+  static constexpr uint32_t kOffQ = 0;
+  static constexpr uint32_t kOffDO = kOffQ + kQBytes;
+  static constexpr uint32_t kOffStage = kOffDO + kQBytes;
+  static constexpr uint32_t kStageBytes = 2 * kKVBytes;
+  static constexpr uint32_t kOffDS = kOffStage + kStages * kStageBytes;
+  static constexpr uint32_t kOffBar = kOffDS + 2 * kSBytes;
+  static constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
+  static constexpr uint32_t kTmemS = 0, kTmemDP = 128, kTmemDQ = 256;
+  static_assert(kTmemDQ + D <= 512, "TMEM budget");
+  static_assert(kSmemBytes <= 232448, "smem budget");
+  static_assert(2 * kSBytes >= (uint32_t)kRows * D * 2, "staging for dQ");
+};
+
+template <int D, bool BF16, bool CAP, bool ALIBI>
+__global__ void __launch_bounds__(kThreads, 1)
+    dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+              const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+              const __grid_constant__ CUtensorMap tmDQ, const Params p) {
+  using L = DqLayout<D>;
+  constexpr int NS = L::kStages;
+  enum {
+    kQFull = 0,
+    kKVFull = 1,
+    kKVEmpty = 1 + NS,
+    kSPFull = 1 + 2 * NS,
+    kSPFree = kSPFull + 2,
+    kDSFull = kSPFree + 2,
+    kDSFree = kDSFull + 2,
+    kAccDone = kDSFree + 2,
+    kDrain = kAccDone + 1,
+    kNever = kDrain + 1,
+    kNumBars = kNever + 1
+  };
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  const uint32_t sbase = smem_u32(smem);
+  auto bar = [&](int i) -> uint32_t { return sbase + L::kOffBar + 8u * (uint32_t)i; };
+  uint32_t* tmem_slot = (uint32_t*)(smem + L::kOffBar + 8 * kNumBars);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  int* warp_ok = (int*)(tmem_slot + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_qt = (p.Sq + kRows - 1) / kRows;
+  const int bh = blockIdx.x % (p.B * p.Hq);
+  const int qt = n_qt - 1 - (int)(blockIdx.x / (p.B * p.Hq));  // heaviest causal tiles first
+  const int hq = bh % p.Hq, b = bh / p.Hq;
+  const int hkv = hq / p.G;
+  const int q0 = qt * kRows;
+  int klo, khi;
+  key_range(p, q0, min(q0 + kRows, p.Sq), &klo, &khi);
+  const int jt0 = klo / kInner;
+  const int n_iter = (khi > klo) ? (khi + kInner - 1) / kInner - jt0 : 0;
+
+  WaitCtl ctl{abort_flag, p.status, p.timeout_ns};
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kNumBars; ++i) {
+      uint32_t cnt = 1;
+      if ((i >= kSPFree && i < kSPFree + 2) || (i >= kDSFull && i < kDSFull + 2)) cnt = 4;
+      mbar_init(bar(i), cnt);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(bar(kQFull), 2 * L::kQBytes);
+      for (int s = 0; s < L::kSub; ++s) {
+        tma_load_4d(sbase + L::kOffQ + s * (kRows * 128), &tmQ, bar(kQFull), s * 64, q0, hq, b);
+        tma_load_4d(sbase + L::kOffDO + s * (kRows * 128), &tmDO, bar(kQFull), s * 64, q0, hq, b);
+      }
+      int n = 0;
+      for (int i = 0; i < n_iter; ++i) {
+        const int st = i % NS;
+        if (i >= NS && !mbar_wait(bar(kKVEmpty + st), ((i / NS) & 1) ^ 1, ctl, BFA_ERR_DEVICE_TIMEOUT)) break;
+        const int j0 = (jt0 + i) * kInner;
+        const uint32_t ks = sbase + L::kOffStage + st * L::kStageBytes;
+        mbar_arrive_expect_tx(bar(kKVFull + st), L::kStageBytes);
+        for (int s = 0; s < L::kSub; ++s) {
+          tma_load_4d(ks + s * (kInner * 128), &tmK, bar(kKVFull + st), s * 64, j0, hkv, b);
+          tma_load_4d(ks + L::kKVBytes + s * (kInner * 128), &tmV, bar(kKVFull + st), s * 64, j0, hkv, b);
+        }
+        n = i + 1;
+      }
+      drain_wait(bar(kQFull), 0, p.timeout_ns);
+      for (int i = (n > NS ? n - NS : 0); i < n; ++i)
+        drain_wait(bar(kKVFull + i % NS), (i / NS) & 1, p.timeout_ns);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idSP = idesc_f16(kRows, kInner, BF16, false);
+      constexpr uint32_t idAcc = idesc_f16(kRows, D, BF16, true);
+      auto stage = [&](int i) -> uint32_t { return sbase + L::kOffStage + (i % NS) * L::kStageBytes; };
+      auto issue_sp = [&](int i) {
+        const int bf = i & 1;
+        const uint32_t ka = stage(i), va = stage(i) + L::kKVBytes;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t offq = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
+          const uint32_t offk = (kk >> 2) * (kInner * 128) + (kk & 3) * 32;
+          mma_ss(tmem + L::kTmemS + 64 * bf, desc_kmajor(sbase + L::kOffQ + offq),
+                 desc_kmajor(ka + offk), idSP, kk > 0 ? 1u : 0u);
+          mma_ss(tmem + L::kTmemDP + 64 * bf, desc_kmajor(sbase + L::kOffDO + offq),
+                 desc_kmajor(va + offk), idSP, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(bar(kSPFull + bf));
+      };
+      bool ok = mbar_wait(bar(kQFull), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
+      if (ok && n_iter > 0) {
+        ok = mbar_wait(bar(kKVFull), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
+        if (ok) {
+          tc_fence_after();
+          issue_sp(0);
+        }
+      }
+      for (int i = 0; i < n_iter && ok; ++i) {
+        const int bf = i & 1, k = i >> 1;
+        if (i + 1 < n_iter) {
+          const int n1 = i + 1;
+          if (!(ok = mbar_wait(bar(kKVFull + n1 % NS), (n1 / NS) & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
+          if (n1 >= 2 && !(ok = mbar_wait(bar(kSPFree + (n1 & 1)), ((n1 >> 1) - 1) & 1, ctl,
+                                          BFA_ERR_DEVICE_TIMEOUT)))
+            break;
+          tc_fence_after();
+          issue_sp(n1);
+        }
+        if (!(ok = mbar_wait(bar(kDSFull + bf), k & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
+        tc_fence_after();
+        const uint32_t ka = stage(i);
+        const uint32_t ds = sbase + L::kOffDS + bf * L::kSBytes;
+#pragma unroll
+        for (int kk = 0; kk < kInner / 16; ++kk) {
+          mma_ss(tmem + L::kTmemDQ, desc_kmajor(ds + kk * 32),
+                 desc_mnmajor(ka + kk * 2048, kInner * 128), idAcc, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(bar(kDSFree + bf));
+        mma_commit(bar(kKVEmpty + i % NS));
+      }
+      mma_commit(bar(kAccDone));
+      mma_commit(bar(kDrain));
+      drain_wait(bar(kDrain), 0, p.timeout_ns);
+    }
+  } else if (warp >= 4) {
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const int qi = q0 + row;
+    const int64_t gi = (int64_t)qi + p.q_off;
+    const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
+    const float sl2 = p.scale * kLog2e;
+    const float cap_in = CAP ? p.scale / p.soft_cap : 0.f;
+    const float cap_out = CAP ? p.soft_cap * kLog2e : 0.f;
+    const float slope2 = ALIBI ? p.alibi[hq] * kLog2e : 0.f;
+    const int64_t ridx = ((int64_t)b * p.Hq + hq) * p.Sq + qi;
+    float lse2 = __int_as_float(0x7f800000), dlt = 0.f;
+    if (qi < p.Sq) {
+      const float lse = p.lse[ridx];
+      lse2 = (lse == neg_inf()) ? __int_as_float(0x7f800000) : lse * kLog2e;
+      dlt = p.delta[ridx];
+    }
+    bool ok = true;
+    for (int i = 0; i < n_iter; ++i) {
+      const int bf = i & 1, k = i >> 1;
+      const int j0 = (jt0 + i) * kInner;
+      uint32_t wbar = bar(kSPFull + bf), wpar = (uint32_t)(k & 1);
+      if ((p.debug_flags & BFA_DEBUG_INJECT_STALL) && i == 0) {
+        wbar = bar(kNever);
+        wpar = 0;
+      }
+      if (!(ok = warp_wait(wbar, wpar, ctl))) break;
+      tc_fence_after();
+      uint32_t sr[64], dr[64];
+      tmem_ld32(tmem + lane_base + L::kTmemS + 64 * bf, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+      tmem_ld32(tmem + lane_base + L::kTmemS + 64 * bf + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      tmem_ld32(tmem + lane_base + L::kTmemDP + 64 * bf, *reinterpret_cast<uint32_t(*)[32]>(&dr[0]));
+      tmem_ld32(tmem + lane_base + L::kTmemDP + 64 * bf + 32, *reinterpret_cast<uint32_t(*)[32]>(&dr[32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kSPFree + bf));
+
+      const bool full = tile_full(p, q0, q0 + kRows, j0, j0 + kInner);
+      const float abase = ALIBI ? slope2 * (float)(gi - (int64_t)j0 - p.k_off) : 0.f;
+      float dsv[64];
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        float t;
+        float x = logit2<CAP>(__uint_as_float(sr[c]), sl2, cap_in, cap_out, &t);
+        if (ALIBI) x = fmaf(-slope2, (float)c, x + abase);
+        float pr = ex2(x - lse2);
+        if (!full) {
+          const int kj = j0 + c;
+          const bool keep = (qi < p.Sq) && (kj < p.Sk) && keep_pair(gi, (int64_t)kj + p.k_off, p.causal, p.window);
+          pr = keep ? pr : 0.f;
+        }
+        float ds = pr * (__uint_as_float(dr[c]) - dlt) * p.scale;
+        if (CAP) ds *= (1.f - t * t);
+        dsv[c] = ds;
+      }
+      if (k >= 1 && !(ok = warp_wait(bar(kDSFree + bf), (uint32_t)((k - 1) & 1), ctl))) break;
+      store_row64<BF16>(smem + L::kOffDS + bf * L::kSBytes, row, dsv);
+      fence_async_shared();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kDSFull + bf));
+    }
+    bool good = ok;
+    if (good && n_iter > 0) good = warp_wait(bar(kAccDone), 0, ctl);
+    uint8_t* stage_dq = smem + L::kOffDS;
+    if (good) {
+      tc_fence_after();
+      stage_tmem_row<D, BF16>(tmem + lane_base + L::kTmemDQ, stage_dq, row, n_iter == 0);
+      fence_async_shared();
+    }
+    if (lane == 0) warp_ok[wq] = good ? 1 : 0;
+    named_sync(1, 128);
+    if (wq == 0 && lane == 0 && warp_ok[0] && warp_ok[1] && warp_ok[2] && warp_ok[3]) {
+      for (int s = 0; s < L::kSub; ++s)
+        tma_store_4d(&tmDQ, smem_u32(stage_dq) + s * (kRows * 128), s * 64, q0, hq, b);
+      tma_store_commit();
+      tma_store_wait_all();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <typename K>
+bool set_smem(K kern, uint32_t bytes) {
+  return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) ==
+         cudaSuccess;
+}
+
+template <int D, bool BF16, bool CAP, bool ALIBI>
+int launch_bwd(const Params& p, int dtype, cudaStream_t st) {
+  if (p.phases & BFA_BWD_PHASE_DKDV) {
+    using L = DkdvLayout<D>;
+    auto kern = dkdv_kernel<D, BF16, CAP, ALIBI>;
+    static std::once_flag once;
+    static bool attr_ok = false;
+    std::call_once(once, [&] { attr_ok = set_smem(kern, L::kSmemBytes); });
+    if (!attr_ok) return BFA_ERR_CUDA;
+    CUtensorMap m[6];
+    if (!make_tmap_bhsd(&m[0], p.k, dtype, D, p.Sk, p.Hkv, p.B, p.sk_, kRows) ||
+        !make_tmap_bhsd(&m[1], p.v, dtype, D, p.Sk, p.Hkv, p.B, p.sv_, kRows) ||
+        !make_tmap_bhsd(&m[2], p.q, dtype, D, p.Sq, p.Hq, p.B, p.sq_, kInner) ||
+        !make_tmap_bhsd(&m[3], p.dout, dtype, D, p.Sq, p.Hq, p.B, p.sdo_, kInner) ||
+        !make_tmap_bhsd(&m[4], p.dk, dtype, D, p.Sk, p.Hkv, p.B, p.sdk_, kRows) ||
+        !make_tmap_bhsd(&m[5], p.dv, dtype, D, p.Sk, p.Hkv, p.B, p.sdv_, kRows))
+      return BFA_ERR_CUDA;
+    const unsigned grid = (unsigned)((p.Sk + kRows - 1) / kRows) * p.Hkv * p.B;
+    kern<<<grid, kThreads, L::kSmemBytes, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], p);
+    note_launch();
+    if (cudaGetLastError() != cudaSuccess) return BFA_ERR_CUDA;
+  }
+  if (p.phases & BFA_BWD_PHASE_DQ) {
+    using L = DqLayout<D>;
+    auto kern = dq_kernel<D, BF16, CAP, ALIBI>;
+    static std::once_flag once;
+    static bool attr_ok = false;
+    std::call_once(once, [&] { attr_ok = set_smem(kern, L::kSmemBytes); });
+    if (!attr_ok) return BFA_ERR_CUDA;
+    CUtensorMap m[5];
+    if (!make_tmap_bhsd(&m[0], p.q, dtype, D, p.Sq, p.Hq, p.B, p.sq_, kRows) ||
+        !make_tmap_bhsd(&m[1], p.dout, dtype, D, p.Sq, p.Hq, p.B, p.sdo_, kRows) ||
+        !make_tmap_bhsd(&m[2], p.k, dtype, D, p.Sk, p.Hkv, p.B, p.sk_, kInner) ||
+        !make_tmap_bhsd(&m[3], p.v, dtype, D, p.Sk, p.Hkv, p.B, p.sv_, kInner) ||
+        !make_tmap_bhsd(&m[4], p.dq, dtype, D, p.Sq, p.Hq, p.B, p.sdq_, kRows))
+      return BFA_ERR_CUDA;
+    const unsigned grid = (unsigned)((p.Sq + kRows - 1) / kRows) * p.Hq * p.B;
+    kern<<<grid, kThreads, L::kSmemBytes, st>>>(m[0], m[1], m[2], m[3], m[4], p);
+    note_launch();
+    if (cudaGetLastError() != cudaSuccess) return BFA_ERR_CUDA;
+  }
+  return BFA_OK;
+}
+
+template <int D, bool BF16>
+int dispatch_flags(const Params& p, int dtype, cudaStream_t st) {
+  const bool cap = p.soft_cap > 0.f, alibi = p.alibi != nullptr;
+  if (cap && alibi) return launch_bwd<D, BF16, true, true>(p, dtype, st);
+  if (cap) return launch_bwd<D, BF16, true, false>(p, dtype, st);
+  if (alibi) return launch_bwd<D, BF16, false, true>(p, dtype, st);
+  return launch_bwd<D, BF16, false, false>(p, dtype, st);
+}
+
+}  // namespace
+
+bool sm100_bwd_eligible(const Params& p, int dtype) {
+  if (dtype != BFA_DTYPE_BF16 && dtype != BFA_DTYPE_F16) return false;
+  if (p.D != 64 && p.D != 128) return false;
+  if (p.Sq < 1 || p.Sk < 1 || p.B < 1 || p.Hq < 1) return false;
+  if (!device_is_sm100()) return false;
+  return tma_layout_ok(p.q, p.sq_, 2) && tma_layout_ok(p.k, p.sk_, 2) &&
+         tma_layout_ok(p.v, p.sv_, 2) && tma_layout_ok(p.dout, p.sdo_, 2) &&
+         tma_layout_ok(p.dq, p.sdq_, 2) && tma_layout_ok(p.dk, p.sdk_, 2) &&
+         tma_layout_ok(p.dv, p.sdv_, 2);
+}
+
+int sm100_bwd(const Params& p, int dtype, cudaStream_t st) {
+  const bool bf16 = dtype == BFA_DTYPE_BF16;
+  if (p.D == 64) return bf16 ? dispatch_flags<64, true>(p, dtype, st) : dispatch_flags<64, false>(p, dtype, st);
+  return bf16 ? dispatch_flags<128, true>(p, dtype, st) : dispatch_flags<128, false>(p, dtype, st);
+}
 
 }  // namespace bfa

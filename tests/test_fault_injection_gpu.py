@@ -38,6 +38,27 @@ def test_injected_stall_reports_timeout_and_context_survives():
     nfa.check_device_status(DEV)
 
 
+def test_injected_stall_in_backward_kernels():
+    """Both tcgen05 backward kernels stall on their first elementwise wait,
+    time out, clean up and report; the next backward is correct."""
+    q, k, v = _qkv(2)
+    go = _qkv(3)[0]
+    qd, kd, vd, god = (t.to(DEV) for t in (q, k, v, go))
+    o, lse = nfa.npu_flash_attention_forward(qd, kd, vd, causal=True, return_lse=True)
+    nfa.check_device_status(DEV)
+    nfa.npu_flash_attention_backward(qd, kd, vd, o, lse, god, causal=True,
+                                     _wait_timeout_ns=20_000_000,
+                                     _debug_flags=bfa_lib.DEBUG_INJECT_STALL)
+    torch.cuda.synchronize()
+    assert bfa_lib.read_and_clear_status(torch.device(DEV)) == bfa_lib.ERR_DEVICE_TIMEOUT
+    from oracle.attention_math import attention_backward
+    dq, dk, dv = nfa.npu_flash_attention_backward(qd, kd, vd, o, lse, god, causal=True)
+    rq, rk, rv = attention_backward(q, k, v, go, causal=True)
+    for a, r in ((dq, rq), (dk, rk), (dv, rv)):
+        assert ((a.cpu().double() - r).abs() / (1 + r.abs())).max().item() < 2e-2
+    nfa.check_device_status(DEV)
+
+
 def test_check_device_status_raises_on_timeout():
     q, k, v = (t.to(DEV) for t in _qkv(1))
     nfa.npu_flash_attention_forward(q, k, v, causal=True, _wait_timeout_ns=20_000_000,

@@ -31,11 +31,18 @@ def _inputs(seed, b, hq, hkv, sq, sk, d, dtype, scale_in=1.0):
 
 
 def _err(a, ref):
+    """Largest |a − ref| / (1 + |ref|): below `tol` exactly when
+    torch.allclose(a, ref, atol=tol, rtol=tol) holds, the form the reference's
+    own tests use (e.g. test/test_bf16_full.py with TOL_FWD = 2e-2). A pure
+    absolute bound is not attainable for 16-bit outputs above ~5 (half an
+    ulp of bf16 at 8 is 0.031)."""
     a = a.detach().cpu().double()
     ref = ref.double()
     fin = torch.isfinite(ref)
     assert torch.equal(torch.isfinite(a), fin), "inf/nan pattern differs"
-    return (a[fin] - ref[fin]).abs().max().item() if fin.any() else 0.0
+    if not fin.any():
+        return 0.0
+    return ((a[fin] - ref[fin]).abs() / (1.0 + ref[fin].abs())).max().item()
 
 
 def _lse_err(lse, ref):
@@ -148,7 +155,9 @@ def test_stability_cases():
     q, k, v, go = _inputs(3, 1, 1, 1, 128, 128, 64, torch.float32, scale_in=10.0)
     o = nfa.npu_flash_attention_forward(q.to(DEV), k.to(DEV), v.to(DEV), causal=True, scale=10.0)
     assert torch.isfinite(o).all()
-    check_case(q, k, v, go, causal=True, scale=10.0)
+    # Logits reach |u| ~ 1e4 here; one fp32 ulp there is ~1e-3, so fp32
+    # arithmetic (the reference's as well) agrees with fp64 only to ~1e-3.
+    check_case(q, k, v, go, causal=True, scale=10.0, tol=5e-3)
     check_case(q, k, v, go, causal=True, scale=0.01)
     q16, k16, v16, go16 = _inputs(4, 1, 1, 1, 128, 128, 64, torch.float16, scale_in=100.0)
     o = nfa.npu_flash_attention_forward(q16.to(DEV), k16.to(DEV), v16.to(DEV), causal=True)
