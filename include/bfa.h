@@ -60,7 +60,8 @@ typedef enum bfa_status {
   BFA_ERR_UNSUPPORTED = -3,       /* dtype or head_dim outside what is built */
   BFA_ERR_WORKSPACE = -4,         /* workspace missing or too small */
   BFA_ERR_CUDA = -5,              /* a CUDA runtime/driver call failed */
-  BFA_ERR_DEVICE_TIMEOUT = -6     /* a device-side wait ran out (status word) */
+  BFA_ERR_DEVICE_TIMEOUT = -6,    /* a device-side wait ran out (status word) */
+  BFA_ERR_SCRATCH_LIMIT = -7      /* bfa_bwd_noalloc: problem larger than its static scratch */
 } bfa_status;
 
 /* Problem description: the reference host API's arguments
@@ -150,6 +151,18 @@ int bfa_bwd_delta(const bfa_problem* problem, const bfa_bwd_args* args,
  * bfa_bwd_workspace_bytes(problem) bytes, 256-byte aligned. */
 int bfa_bwd(const bfa_problem* problem, const bfa_bwd_args* args,
             void* workspace, size_t workspace_bytes, void* stream);
+
+/* Backward that allocates nothing (no reference counterpart).
+ * Same inputs, outputs and results as bfa_bwd, for callers that cannot
+ * allocate device memory: a plugin whose host framework owns all device
+ * allocations and passes only the input/output buffers, or a hot path that
+ * must not call cudaMalloc because it can synchronise the device. Δ goes to a
+ * static device array of 2^21 query rows (batch*heads_q*seqlen_q; 8 MiB per
+ * GPU that loads the library, held until exit); larger problems return
+ * BFA_ERR_SCRATCH_LIMIT. All calls share that array: calls that overlap on the
+ * GPU race, so serialise them. The first call on each device looks up the
+ * array's address and should come before any stream capture. */
+int bfa_bwd_noalloc(const bfa_problem* problem, const bfa_bwd_args* args, void* stream);
 
 /* Merge a partial attention result into a running one, in place:
  *   lse' = logaddexp(lse_acc, lse_part)

@@ -21,7 +21,10 @@ DEBUG_INJECT_STALL = 1
 ERR_DEVICE_TIMEOUT = -6
 
 EXPORTED = ("bfa_abi_version", "bfa_launch_count", "bfa_strerror", "bfa_fwd",
-            "bfa_bwd_workspace_bytes", "bfa_bwd_delta", "bfa_bwd", "bfa_merge_partial")
+            "bfa_bwd_workspace_bytes", "bfa_bwd_delta", "bfa_bwd", "bfa_bwd_noalloc",
+            "bfa_merge_partial")
+ERR_SCRATCH_LIMIT = -7
+NOALLOC_MAX_ROWS = 1 << 21
 PHASE_DELTA, PHASE_DKDV, PHASE_DQ = 1, 2, 4
 
 _TORCH_TO_BFA = {torch.float32: DTYPE_F32, torch.float16: DTYPE_F16,
@@ -87,6 +90,9 @@ def load() -> ctypes.CDLL:
         lib.bfa_bwd.restype = ctypes.c_int
         lib.bfa_bwd.argtypes = [ctypes.POINTER(Problem), ctypes.POINTER(BwdArgs),
                                 ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+        lib.bfa_bwd_noalloc.restype = ctypes.c_int
+        lib.bfa_bwd_noalloc.argtypes = [ctypes.POINTER(Problem), ctypes.POINTER(BwdArgs),
+                                        ctypes.c_void_p]
         lib.bfa_merge_partial.restype = ctypes.c_int
         lib.bfa_merge_partial.argtypes = [ctypes.c_int32] * 4 + [
             Tensor, ctypes.c_int32, ctypes.c_void_p, Tensor, ctypes.c_int32, ctypes.c_void_p,

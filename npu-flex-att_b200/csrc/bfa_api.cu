@@ -77,6 +77,8 @@ const char* bfa_strerror(int status) {
     case BFA_ERR_WORKSPACE: return "bfa: workspace missing or smaller than bfa_bwd_workspace_bytes()";
     case BFA_ERR_CUDA: return "bfa: a CUDA runtime call or kernel launch failed";
     case BFA_ERR_DEVICE_TIMEOUT: return "bfa: a device-side wait timed out (pipeline stalled)";
+    case BFA_ERR_SCRATCH_LIMIT:
+      return "bfa: problem exceeds bfa_bwd_noalloc's static scratch (batch*heads_q*seqlen_q > 2097152)";
   }
   return "bfa: unknown status";
 }

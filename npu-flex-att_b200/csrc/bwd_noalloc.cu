@@ -1,0 +1,70 @@
+// bwd_noalloc.cu -- bfa_bwd_noalloc: the attention backward for callers that
+// cannot allocate device memory.
+//
+// bfa_bwd needs a caller-provided workspace for Δ = rowsum(O∘dO) (fp32, one
+// value per query row). Some callers cannot provide one: a plugin inside a
+// host framework that owns every device allocation and hands the plugin only
+// its input and output buffers, or a caller whose hot path must not call
+// cudaMalloc (it can synchronise the device). For them this entry point keeps
+// Δ in a file-scope device array of fixed size instead.
+//
+// Limits and sharing:
+//  * The array holds kMaxRows = 2^21 query rows (batch * heads_q * seqlen_q),
+//    8 MiB of fp32 (+512 bytes of alignment slack). Larger problems are
+//    rejected with BFA_ERR_SCRATCH_LIMIT.
+//  * Every GPU that loads this library holds the array until process exit.
+//  * All calls share the one array per device and it keeps the last call's
+//    contents. Calls whose work overlaps on the GPU (different streams, or
+//    different host threads on the same device) race on it; serialise them.
+//    Δ is fully rewritten by each call before it is read, so nothing needs
+//    clearing.
+//  * The first call on a device looks up the array's device address
+//    (cudaGetSymbolAddress, with that device current) and caches it; make that
+//    first call before any stream capture.
+//  * Nothing here calls cudaMalloc, cudaFree or an allocating library routine.
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "bfa.h"
+#include "bfa_internal.h"
+
+namespace {
+
+constexpr int64_t kMaxRows = int64_t(1) << 21;
+constexpr size_t kScratchFloats = (size_t)kMaxRows + 128;  // + 512 B: bfa_bwd's workspace slack
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) float g_delta_scratch[kScratchFloats];
+
+std::mutex g_mu;
+float* g_addr[kMaxDevices] = {};
+
+// Device address of g_delta_scratch on the current device (looked up once).
+int scratch_address(float** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return BFA_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (!g_addr[dev]) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_delta_scratch) != cudaSuccess || !ptr) return BFA_ERR_CUDA;
+    g_addr[dev] = static_cast<float*>(ptr);
+  }
+  *out = g_addr[dev];
+  return BFA_OK;
+}
+
+}  // namespace
+
+extern "C" int bfa_bwd_noalloc(const bfa_problem* problem, const bfa_bwd_args* args,
+                               void* stream) {
+  if (!problem) return BFA_ERR_INVALID_ARGUMENT;
+  if (problem->batch >= 0 && problem->heads_q >= 0 && problem->seqlen_q >= 0) {
+    const int64_t rows = (int64_t)problem->batch * problem->heads_q * problem->seqlen_q;
+    if (rows > kMaxRows) return BFA_ERR_SCRATCH_LIMIT;
+  }
+  float* scratch = nullptr;
+  const int rc = scratch_address(&scratch);
+  if (rc != BFA_OK) return rc;
+  return bfa_bwd(problem, args, scratch, kScratchFloats * sizeof(float), stream);
+}
