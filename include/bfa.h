@@ -156,10 +156,11 @@ int bfa_bwd(const bfa_problem* problem, const bfa_bwd_args* args,
  * Same inputs, outputs and results as bfa_bwd, for callers that cannot
  * allocate device memory: a plugin whose host framework owns all device
  * allocations and passes only the input/output buffers, or a hot path that
- * must not call cudaMalloc because it can synchronise the device. Δ goes to a
- * static device array of 2^21 query rows (batch*heads_q*seqlen_q; 8 MiB per
- * GPU that loads the library, held until exit); larger problems return
- * BFA_ERR_SCRATCH_LIMIT. All calls share that array: calls that overlap on the
+ * must not call cudaMalloc because it can synchronise the device. The row
+ * statistics (Δ, scaled LSE) go to a static device array sized for 2^21 query
+ * rows, each head's rows rounded up to 64 (batch*heads_q*ceil(seqlen_q/64)*64;
+ * 16 MiB per GPU that loads the library, held until exit); larger problems
+ * return BFA_ERR_SCRATCH_LIMIT. All calls share that array: calls that overlap on the
  * GPU race, so serialise them. The first call on each device looks up the
  * array's address and should come before any stream capture. */
 int bfa_bwd_noalloc(const bfa_problem* problem, const bfa_bwd_args* args, void* stream);

@@ -78,7 +78,8 @@ const char* bfa_strerror(int status) {
     case BFA_ERR_CUDA: return "bfa: a CUDA runtime call or kernel launch failed";
     case BFA_ERR_DEVICE_TIMEOUT: return "bfa: a device-side wait timed out (pipeline stalled)";
     case BFA_ERR_SCRATCH_LIMIT:
-      return "bfa: problem exceeds bfa_bwd_noalloc's static scratch (batch*heads_q*seqlen_q > 2097152)";
+      return "bfa: problem exceeds bfa_bwd_noalloc's static scratch "
+             "(batch*heads_q*ceil(seqlen_q/64)*64 > 2097152)";
   }
   return "bfa: unknown status";
 }
@@ -103,10 +104,18 @@ int bfa_fwd(const bfa_problem* pr, const bfa_fwd_args* a, void* stream) {
   return bfa::simt_fwd(p, pr->dtype, st);
 }
 
+// Backward workspace: Δ and lse·log2(e), each [B, Hq, Sq_pad] fp32 with the
+// row pitch padded to a multiple of 64 (one bulk copy per 64-row tile).
+static int32_t padded_rows(int32_t sq) { return (sq + 63) / 64 * 64; }
+
+static size_t rowstat_bytes(const bfa_problem* pr) {
+  const size_t n = (size_t)pr->batch * pr->heads_q * padded_rows(pr->seqlen_q) * sizeof(float);
+  return (n + 255) / 256 * 256;
+}
+
 size_t bfa_bwd_workspace_bytes(const bfa_problem* pr) {
   if (check_problem(pr)) return 0;
-  const size_t delta = (size_t)pr->batch * pr->heads_q * pr->seqlen_q * sizeof(float);
-  return (delta + 255) / 256 * 256 + 256;
+  return 2 * rowstat_bytes(pr) + 256;
 }
 
 static int fill_bwd(const bfa_problem* pr, const bfa_bwd_args* a, Params* p) {
@@ -139,6 +148,8 @@ int bfa_bwd_delta(const bfa_problem* pr, const bfa_bwd_args* a, float* delta, vo
   if (rc) return rc;
   if (!delta) return BFA_ERR_INVALID_ARGUMENT;
   p.delta = delta;
+  p.lse2 = nullptr;
+  p.Sq_pad = pr->seqlen_q;  // the caller's buffer is [B, Hq, Sq] contiguous
   return bfa::launch_delta(p, pr->dtype, (cudaStream_t)stream);
 }
 
@@ -153,6 +164,8 @@ int bfa_bwd(const bfa_problem* pr, const bfa_bwd_args* a, void* workspace, size_
   if (!workspace || ws_bytes < bfa_bwd_workspace_bytes(pr)) return BFA_ERR_WORKSPACE;
   if (((uintptr_t)workspace & 255u) != 0) return BFA_ERR_WORKSPACE;
   p.delta = (float*)workspace;
+  p.lse2 = (float*)((char*)workspace + rowstat_bytes(pr));
+  p.Sq_pad = padded_rows(pr->seqlen_q);
   if (!empty_q(pr) && (p.phases & BFA_BWD_PHASE_DELTA)) {
     rc = bfa::launch_delta(p, pr->dtype, st);
     if (rc) return rc;

@@ -27,6 +27,11 @@ struct Params {
   const void* q; const void* k; const void* v; void* o;
   const void* dout; void* dq; void* dk; void* dv;
   float* lse; float* delta;
+  // Backward row statistics, one row pitch `Sq_pad` per (b, hq): `delta` holds
+  // Δ and `lse2` (may be null) holds lse·log2(e), +inf for rows past Sq or
+  // rows that see no key, so that exp2(x − lse2) is 0 there.
+  float* lse2;
+  int32_t Sq_pad;
   int64_t sq_[4], sk_[4], sv_[4], so_[4], sdo_[4], sdq_[4], sdk_[4], sdv_[4];
   int32_t B, Hq, Hkv, G, Sq, Sk, D;
   int32_t causal, window;

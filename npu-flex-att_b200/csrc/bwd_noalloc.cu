@@ -9,9 +9,11 @@
 // Δ in a file-scope device array of fixed size instead.
 //
 // Limits and sharing:
-//  * The array holds kMaxRows = 2^21 query rows (batch * heads_q * seqlen_q),
-//    8 MiB of fp32 (+512 bytes of alignment slack). Larger problems are
-//    rejected with BFA_ERR_SCRATCH_LIMIT.
+//  * The array holds the backward's row statistics (Δ and lse·log2 e, fp32)
+//    for kMaxRows = 2^21 query rows, counting each head's rows rounded up to
+//    a multiple of 64 (batch * heads_q * ceil(seqlen_q / 64) * 64): 16 MiB
+//    (+512 bytes of alignment slack). Larger problems are rejected with
+//    BFA_ERR_SCRATCH_LIMIT.
 //  * Every GPU that loads this library holds the array until process exit.
 //  * All calls share the one array per device and it keeps the last call's
 //    contents. Calls whose work overlaps on the GPU (different streams, or
@@ -32,7 +34,7 @@
 namespace {
 
 constexpr int64_t kMaxRows = int64_t(1) << 21;
-constexpr size_t kScratchFloats = (size_t)kMaxRows + 128;  // + 512 B: bfa_bwd's workspace slack
+constexpr size_t kScratchFloats = 2 * (size_t)kMaxRows + 128;  // + 512 B: bfa_bwd's workspace slack
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) float g_delta_scratch[kScratchFloats];
@@ -60,7 +62,8 @@ extern "C" int bfa_bwd_noalloc(const bfa_problem* problem, const bfa_bwd_args* a
                                void* stream) {
   if (!problem) return BFA_ERR_INVALID_ARGUMENT;
   if (problem->batch >= 0 && problem->heads_q >= 0 && problem->seqlen_q >= 0) {
-    const int64_t rows = (int64_t)problem->batch * problem->heads_q * problem->seqlen_q;
+    const int64_t rows =
+        (int64_t)problem->batch * problem->heads_q * (((int64_t)problem->seqlen_q + 63) / 64 * 64);
     if (rows > kMaxRows) return BFA_ERR_SCRATCH_LIMIT;
   }
   float* scratch = nullptr;

@@ -158,7 +158,7 @@ __global__ void __launch_bounds__(NT) simt_bwd_dq_kernel(Params p) {
   const float slope = p.alibi ? p.alibi[hq] : 0.f;
   const int64_t row_idx = ((int64_t)b * p.Hq + hq) * p.Sq + r0 + r;
   const float lse = (r < rows) ? p.lse[row_idx] : 0.f;
-  const float dlt = (r < rows) ? p.delta[row_idx] : 0.f;
+  const float dlt = (r < rows) ? p.delta[((int64_t)b * p.Hq + hq) * p.Sq_pad + r0 + r] : 0.f;
   const bool row_live = (r < rows) && (lse != neg_inf());
   float acc[DP / 4];
 #pragma unroll
@@ -245,7 +245,7 @@ __global__ void __launch_bounds__(NT) simt_bwd_dkdv_kernel(Params p) {
       if (tid < TM) {
         const int64_t row_idx = ((int64_t)b * p.Hq + hq) * p.Sq + q0 + tid;
         sL[tid] = (tid < qn) ? p.lse[row_idx] : neg_inf();
-        sDl[tid] = (tid < qn) ? p.delta[row_idx] : 0.f;
+        sDl[tid] = (tid < qn) ? p.delta[((int64_t)b * p.Hq + hq) * p.Sq_pad + q0 + tid] : 0.f;
       }
       __syncthreads();
 #pragma unroll
@@ -295,24 +295,38 @@ __global__ void __launch_bounds__(NT) simt_bwd_dkdv_kernel(Params p) {
   }
 }
 
-// Δ = rowsum(O∘dO): one warp per (b, hq, i) row.
+// Δ = rowsum(O∘dO): one warp per (b, hq, i) row of pitch Sq_pad; rows past Sq
+// get Δ = 0. When `lse2` is set the kernel also writes lse·log2(e) there
+// (+inf for rows past Sq and rows whose LSE is −inf).
 template <typename T>
 __global__ void __launch_bounds__(256) delta_kernel(Params p) {
   const int64_t warp = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  const int64_t nrows = (int64_t)p.B * p.Hq * p.Sq;
+  const int64_t nrows = (int64_t)p.B * p.Hq * p.Sq_pad;
   if (warp >= nrows) return;
-  const int i = (int)(warp % p.Sq);
-  const int hq = (int)((warp / p.Sq) % p.Hq);
-  const int b = (int)(warp / ((int64_t)p.Sq * p.Hq));
-  const T* O = (const T*)p.o + (int64_t)b * p.so_[0] + (int64_t)hq * p.so_[1] + (int64_t)i * p.so_[2];
-  const T* DO = (const T*)p.dout + (int64_t)b * p.sdo_[0] + (int64_t)hq * p.sdo_[1] + (int64_t)i * p.sdo_[2];
+  const int i = (int)(warp % p.Sq_pad);
+  const int hq = (int)((warp / p.Sq_pad) % p.Hq);
+  const int b = (int)(warp / ((int64_t)p.Sq_pad * p.Hq));
   float acc = 0.f;
-  for (int d = lane; d < p.D; d += 32)
-    acc = fmaf(to_f32<T>(O[(int64_t)d * p.so_[3]]), to_f32<T>(DO[(int64_t)d * p.sdo_[3]]), acc);
+  if (i < p.Sq) {
+    const T* O = (const T*)p.o + (int64_t)b * p.so_[0] + (int64_t)hq * p.so_[1] + (int64_t)i * p.so_[2];
+    const T* DO = (const T*)p.dout + (int64_t)b * p.sdo_[0] + (int64_t)hq * p.sdo_[1] + (int64_t)i * p.sdo_[2];
+    for (int d = lane; d < p.D; d += 32)
+      acc = fmaf(to_f32<T>(O[(int64_t)d * p.so_[3]]), to_f32<T>(DO[(int64_t)d * p.sdo_[3]]), acc);
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (lane == 0) p.delta[warp] = acc;
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  }
+  if (lane == 0) {
+    p.delta[warp] = acc;
+    if (p.lse2) {
+      float l2 = __int_as_float(0x7f800000);
+      if (i < p.Sq) {
+        const float lse = p.lse[((int64_t)b * p.Hq + hq) * p.Sq + i];
+        if (lse != neg_inf()) l2 = lse * kLog2e;
+      }
+      p.lse2[warp] = l2;
+    }
+  }
 }
 
 template <typename T, int DP>
@@ -394,7 +408,7 @@ int simt_bwd(const Params& p, int dtype, cudaStream_t st) {
 }
 
 int launch_delta(const Params& p, int dtype, cudaStream_t st) {
-  const int64_t rows = (int64_t)p.B * p.Hq * p.Sq;
+  const int64_t rows = (int64_t)p.B * p.Hq * p.Sq_pad;
   if (rows == 0) return BFA_OK;
   const unsigned blocks = (unsigned)((rows + 7) / 8);
   switch (dtype) {

@@ -82,20 +82,6 @@ __device__ __forceinline__ float logit2(float raw, float sl2, float cap_in, floa
   return raw * sl2;
 }
 
-// Write one row of 64 fp32 values as 16-bit into a 128B-swizzled sub-tile.
-template <bool BF16>
-__device__ __forceinline__ void store_row64(uint8_t* tile, int row, const float* v) {
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    uint4 w;
-    w.x = pack2<BF16>(v[8 * c + 0], v[8 * c + 1]);
-    w.y = pack2<BF16>(v[8 * c + 2], v[8 * c + 3]);
-    w.z = pack2<BF16>(v[8 * c + 4], v[8 * c + 5]);
-    w.w = pack2<BF16>(v[8 * c + 6], v[8 * c + 7]);
-    *reinterpret_cast<uint4*>(tile + sw128_offset(row, c)) = w;
-  }
-}
-
 // Read a TMEM row of D fp32 columns, convert, and write it into a staging
 // area of D/64 swizzled sub-tiles of 128 rows (for a TMA store).
 template <int D, bool BF16>
@@ -124,26 +110,27 @@ __device__ __forceinline__ void stage_tmem_row(uint32_t taddr, uint8_t* stage, i
 }
 
 // ============================================================== dK / dV
+// TMEM: Sᵀ(b) at 64·b, dPᵀ(b) at 128 + 64·b (b = step parity, fp32, 64
+// columns each); the elementwise warps overwrite the first 32 columns of each
+// with Pᵀ / dSᵀ (16-bit, two per column), the A operands of the dV / dK MMAs.
+// dV at 256, dK at 256 + D.
 template <int D>
 struct DkdvLayout {
   static constexpr int kSub = D / 64;
-  static constexpr int kStages = (D <= 64) ? 4 : 2;
+  static constexpr int kStages = (D <= 64) ? 8 : 4;
   static constexpr uint32_t kKVBytes = kRows * D * 2;    // K or V tile (128 keys)
   static constexpr uint32_t kQBytes = kInner * D * 2;    // Q or dO tile (64 rows)
-  static constexpr uint32_t kPBytes = kRows * kInner * 2;
   static constexpr uint32_t kOffK = 0;
   static constexpr uint32_t kOffV = kOffK + kKVBytes;
   static constexpr uint32_t kOffStage = kOffV + kKVBytes;       // Q_s, dO_s per stage
   static constexpr uint32_t kStageBytes = 2 * kQBytes;
-  static constexpr uint32_t kOffPT = kOffStage + kStages * kStageBytes;  // Pᵀ[2], dSᵀ[2]
-  static constexpr uint32_t kOffDS = kOffPT + 2 * kPBytes;
-  static constexpr uint32_t kOffRow = kOffDS + 2 * kPBytes;     // lse2[64], delta[64] per stage
+  static constexpr uint32_t kOffRow = kOffStage + kStages * kStageBytes;  // lse2_s[64], delta_s[64]
   static constexpr uint32_t kOffBar = kOffRow + kStages * 512;
   static constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
   static constexpr uint32_t kTmemS = 0, kTmemDP = 128, kTmemDV = 256, kTmemDK = 256 + D;
   static_assert(kTmemDK + D <= 512, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "smem budget");
-  static_assert(2 * kPBytes >= (uint32_t)kRows * D * 2, "staging for dV / dK");
+  static_assert((2 * kQBytes) % 1024 == 0, "stage alignment");
 };
 
 template <int D, bool BF16, bool CAP, bool ALIBI>
@@ -159,10 +146,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     kQFull = 1,
     kQEmpty = 1 + NS,
     kSPFull = 1 + 2 * NS,
-    kSPFree = kSPFull + 2,
-    kDSFull = kSPFree + 2,
-    kDSFree = kDSFull + 2,
-    kAccDone = kDSFree + 2,
+    kDSFull = kSPFull + 2,
+    kAccDone = kDSFull + 2,
     kDrain = kAccDone + 1,
     kNever = kDrain + 1,
     kNumBars = kNever + 1
@@ -192,12 +177,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   WaitCtl ctl{abort_flag, p.status, p.timeout_ns};
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kNumBars; ++i) {
-      uint32_t cnt = 1;
-      if (i >= kQFull && i < kQFull + NS) cnt = 2;
-      if ((i >= kSPFree && i < kSPFree + 2) || (i >= kDSFull && i < kDSFull + 2)) cnt = 4;
-      mbar_init(bar(i), cnt);
-    }
+    for (int i = 0; i < kNumBars; ++i)
+      mbar_init(bar(i), (i >= kDSFull && i < kDSFull + 2) ? 4u : 1u);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -213,53 +194,43 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      mbar_arrive_expect_tx(bar(kKVFull), 2 * L::kKVBytes);
-      for (int s = 0; s < L::kSub; ++s) {
-        tma_load_4d(sbase + L::kOffK + s * (kRows * 128), &tmK, bar(kKVFull), s * 64, c0, hkv, b);
-        tma_load_4d(sbase + L::kOffV + s * (kRows * 128), &tmV, bar(kKVFull), s * 64, c0, hkv, b);
+      // A key tile no query sees loads nothing: its epilogue stages zeros in
+      // the K / V tiles, which must not have a TMA write in flight.
+      if (n_iter > 0) {
+        mbar_arrive_expect_tx(bar(kKVFull), 2 * L::kKVBytes);
+        for (int s = 0; s < L::kSub; ++s) {
+          tma_load_4d(sbase + L::kOffK + s * (kRows * 128), &tmK, bar(kKVFull), s * 64, c0, hkv, b);
+          tma_load_4d(sbase + L::kOffV + s * (kRows * 128), &tmV, bar(kKVFull), s * 64, c0, hkv, b);
+        }
       }
-    }
-    int issued = 0;
-    for (int i = 0; i < n_iter; ++i) {
-      const int st = i % NS;
-      if (i >= NS && !warp_wait(bar(kQEmpty + st), ((i / NS) & 1) ^ 1, ctl)) break;
-      const int g = i / n_qt;
-      const int hq = hkv * p.G + g;
-      const int q0 = (qt0 + i % n_qt) * kInner;
-      const uint32_t qs = sbase + L::kOffStage + st * L::kStageBytes;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(bar(kQFull + st), L::kStageBytes);
+      int issued = 0;
+      for (int i = 0; i < n_iter; ++i) {
+        const int st = i % NS;
+        if (i >= NS && !mbar_wait(bar(kQEmpty + st), ((i / NS) & 1) ^ 1, ctl, BFA_ERR_DEVICE_TIMEOUT))
+          break;
+        const int hq = hkv * p.G + i / n_qt;
+        const int q0 = (qt0 + i % n_qt) * kInner;
+        const uint32_t qs = sbase + L::kOffStage + st * L::kStageBytes;
+        const int64_t rrow = ((int64_t)b * p.Hq + hq) * p.Sq_pad + q0;
+        const uint32_t rs = sbase + L::kOffRow + st * 512;
+        mbar_arrive_expect_tx(bar(kQFull + st), L::kStageBytes + 512);
         for (int s = 0; s < L::kSub; ++s) {
           tma_load_4d(qs + s * (kInner * 128), &tmQ, bar(kQFull + st), s * 64, q0, hq, b);
           tma_load_4d(qs + L::kQBytes + s * (kInner * 128), &tmDO, bar(kQFull + st), s * 64, q0, hq, b);
         }
+        bulk_load(rs, p.lse2 + rrow, 256, bar(kQFull + st));
+        bulk_load(rs + 256, p.delta + rrow, 256, bar(kQFull + st));
+        issued = i + 1;
       }
-      float* rowv = (float*)(smem + L::kOffRow + st * 512);
-      const int64_t rbase = ((int64_t)b * p.Hq + hq) * p.Sq;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int r = lane + 32 * h;
-        const int qi = q0 + r;
-        float l2 = __int_as_float(0x7f800000), dl = 0.f;
-        if (qi < p.Sq) {
-          const float lse = p.lse[rbase + qi];
-          l2 = (lse == neg_inf()) ? __int_as_float(0x7f800000) : lse * kLog2e;
-          dl = p.delta[rbase + qi];
-        }
-        rowv[r] = l2;
-        rowv[64 + r] = dl;
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kQFull + st));
-      issued = i + 1;
-    }
-    if (lane == 0) {
-      drain_wait(bar(kKVFull), 0, p.timeout_ns);
+      if (n_iter > 0) drain_wait(bar(kKVFull), 0, p.timeout_ns);
       for (int i = (issued > NS ? issued - NS : 0); i < issued; ++i)
         drain_wait(bar(kQFull + i % NS), (i / NS) & 1, p.timeout_ns);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // Per step i: S/dP(i+1) are issued before dV/dK(i) so that they overlap
+    // the elementwise work of step i. S/dP(i+2) reuse the TMEM of Pᵀ/dSᵀ(i);
+    // they are issued after dV/dK(i), and one thread's MMAs run in order.
     if (lane == 0) {
       constexpr uint32_t idSP = idesc_f16(kRows, kInner, BF16, false);
       constexpr uint32_t idAcc = idesc_f16(kRows, D, BF16, true);
@@ -278,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit(bar(kSPFull + bf));
       };
-      bool ok = mbar_wait(bar(kKVFull), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
+      bool ok = n_iter == 0 || mbar_wait(bar(kKVFull), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
       if (ok && n_iter > 0) {
         ok = mbar_wait(bar(kQFull), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
         if (ok) {
@@ -291,26 +262,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (i + 1 < n_iter) {
           const int n1 = i + 1;
           if (!(ok = mbar_wait(bar(kQFull + n1 % NS), (n1 / NS) & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
-          if (n1 >= 2 && !(ok = mbar_wait(bar(kSPFree + (n1 & 1)), ((n1 >> 1) - 1) & 1, ctl,
-                                          BFA_ERR_DEVICE_TIMEOUT)))
-            break;
           tc_fence_after();
           issue_sp(n1);
         }
         if (!(ok = mbar_wait(bar(kDSFull + bf), k & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
         tc_fence_after();
         const uint32_t qa = stage(i), da = stage(i) + L::kQBytes;
-        const uint32_t pt = sbase + L::kOffPT + bf * L::kPBytes;
-        const uint32_t ds = sbase + L::kOffDS + bf * L::kPBytes;
 #pragma unroll
         for (int kk = 0; kk < kInner / 16; ++kk) {
           const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-          mma_ss(tmem + L::kTmemDV, desc_kmajor(pt + kk * 32),
+          mma_ts(tmem + L::kTmemDV, tmem + L::kTmemS + 64 * bf + kk * 8,
                  desc_mnmajor(da + kk * 2048, kInner * 128), idAcc, acc);
-          mma_ss(tmem + L::kTmemDK, desc_kmajor(ds + kk * 32),
+          mma_ts(tmem + L::kTmemDK, tmem + L::kTmemDP + 64 * bf + kk * 8,
                  desc_mnmajor(qa + kk * 2048, kInner * 128), idAcc, acc);
         }
-        mma_commit(bar(kDSFree + bf));
         mma_commit(bar(kQEmpty + i % NS));
       }
       mma_commit(bar(kAccDone));
@@ -330,8 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int i = 0; i < n_iter; ++i) {
       const int bf = i & 1, k = i >> 1, st = i % NS;
-      const int g = i / n_qt;
-      const int hq = hkv * p.G + g;
+      const int hq = hkv * p.G + i / n_qt;
       const int q0 = (qt0 + i % n_qt) * kInner;
       uint32_t wbar = bar(kSPFull + bf), wpar = (uint32_t)(k & 1);
       if ((p.debug_flags & BFA_DEBUG_INJECT_STALL) && i == 0) {
@@ -339,51 +303,59 @@ __global__ void __launch_bounds__(kThreads, 1)
         wpar = 0;
       }
       if (!(ok = warp_wait(wbar, wpar, ctl))) break;
+      // The stage's lse2 / Δ arrived with its Q / dO (same barrier phase).
       if (!(ok = warp_wait(bar(kQFull + st), (uint32_t)((i / NS) & 1), ctl))) break;
       tc_fence_after();
+      const uint32_t tSb = tmem + lane_base + L::kTmemS + 64 * bf;
+      const uint32_t tDb = tmem + lane_base + L::kTmemDP + 64 * bf;
       uint32_t sr[64], dr[64];
-      tmem_ld32(tmem + lane_base + L::kTmemS + 64 * bf, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-      tmem_ld32(tmem + lane_base + L::kTmemS + 64 * bf + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-      tmem_ld32(tmem + lane_base + L::kTmemDP + 64 * bf, *reinterpret_cast<uint32_t(*)[32]>(&dr[0]));
-      tmem_ld32(tmem + lane_base + L::kTmemDP + 64 * bf + 32, *reinterpret_cast<uint32_t(*)[32]>(&dr[32]));
+      tmem_ld32(tSb, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+      tmem_ld32(tSb + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      tmem_ld32(tDb, *reinterpret_cast<uint32_t(*)[32]>(&dr[0]));
+      tmem_ld32(tDb + 32, *reinterpret_cast<uint32_t(*)[32]>(&dr[32]));
       tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kSPFree + bf));
 
       const float* rowv = (const float*)(smem + L::kOffRow + st * 512);
       const bool full = tile_full(p, q0, q0 + kInner, c0, c0 + kRows);
       const float slope2 = ALIBI ? p.alibi[hq] * kLog2e : 0.f;
       const float abase = ALIBI ? slope2 * (float)((int64_t)q0 + p.q_off - gj) : 0.f;
-      float pv[64], dsv[64];
+      uint32_t ppk[32], dpk[32];
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        float t;
-        float x = logit2<CAP>(__uint_as_float(sr[c]), sl2, cap_in, cap_out, &t);
-        if (ALIBI) x = fmaf(slope2, (float)c, x + abase);
-        float pr = ex2(x - rowv[c]);
-        if (!full) {
-          const int qi = q0 + c;
-          const bool keep = (qi < p.Sq) && (kj < p.Sk) && keep_pair((int64_t)qi + p.q_off, gj, p.causal, p.window);
-          pr = keep ? pr : 0.f;
+      for (int c = 0; c < 64; c += 2) {
+        float pr2[2], ds2[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int cc = c + h;
+          float t;
+          float x = logit2<CAP>(__uint_as_float(sr[cc]), sl2, cap_in, cap_out, &t);
+          if (ALIBI) x = fmaf(slope2, (float)cc, x + abase);
+          float pr = ex2(x - rowv[cc]);
+          if (!full) {
+            const int qi = q0 + cc;
+            const bool keep = (qi < p.Sq) && (kj < p.Sk) &&
+                              keep_pair((int64_t)qi + p.q_off, gj, p.causal, p.window);
+            pr = keep ? pr : 0.f;
+          }
+          float ds = pr * (__uint_as_float(dr[cc]) - rowv[64 + cc]) * p.scale;
+          if (CAP) ds *= (1.f - t * t);
+          pr2[h] = pr;
+          ds2[h] = ds;
         }
-        float ds = pr * (__uint_as_float(dr[c]) - rowv[64 + c]) * p.scale;
-        if (CAP) ds *= (1.f - t * t);
-        pv[c] = pr;
-        dsv[c] = ds;
+        ppk[c / 2] = pack2<BF16>(pr2[0], pr2[1]);
+        dpk[c / 2] = pack2<BF16>(ds2[0], ds2[1]);
       }
-      if (k >= 1 && !(ok = warp_wait(bar(kDSFree + bf), (uint32_t)((k - 1) & 1), ctl))) break;
-      store_row64<BF16>(smem + L::kOffPT + bf * L::kPBytes, row, pv);
-      store_row64<BF16>(smem + L::kOffDS + bf * L::kPBytes, row, dsv);
-      fence_async_shared();
+      tmem_st32(tSb, ppk);
+      tmem_st32(tDb, dpk);
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kDSFull + bf));
     }
     bool good = ok;
     if (good && n_iter > 0) good = warp_wait(bar(kAccDone), 0, ctl);
-    uint8_t* stage_dv = smem + L::kOffPT;  // Pᵀ[0..1] (32 KB) free once the MMAs are done
-    uint8_t* stage_dk = smem + L::kOffDS;
+    // K and V tiles are free once every MMA is done: they stage dK and dV.
+    uint8_t* stage_dk = smem + L::kOffK;
+    uint8_t* stage_dv = smem + L::kOffV;
     if (good) {
       tc_fence_after();
       stage_tmem_row<D, BF16>(tmem + lane_base + L::kTmemDV, stage_dv, row, n_iter == 0);
@@ -411,24 +383,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ============================================================== dQ
+// TMEM: S(b) at 64·b, dP(b) at 128 + 64·b; dS (16-bit) overwrites the first
+// 32 columns of dP(b) and is the A operand of dQ += dS·K. dQ at 256.
 template <int D>
 struct DqLayout {
   static constexpr int kSub = D / 64;
-  static constexpr int kStages = (D <= 64) ? 6 : 3;
+  static constexpr int kStages = (D <= 64) ? 10 : 5;
   static constexpr uint32_t kQBytes = kRows * D * 2;     // Q or dO tile (128 rows)
   static constexpr uint32_t kKVBytes = kInner * D * 2;   // K or V tile (64 keys)
-  static constexpr uint32_t kSBytes = kRows * kInner * 2;
   static constexpr uint32_t kOffQ = 0;
   static constexpr uint32_t kOffDO = kOffQ + kQBytes;
   static constexpr uint32_t kOffStage = kOffDO + kQBytes;
   static constexpr uint32_t kStageBytes = 2 * kKVBytes;
-  static constexpr uint32_t kOffDS = kOffStage + kStages * kStageBytes;
-  static constexpr uint32_t kOffBar = kOffDS + 2 * kSBytes;
+  static constexpr uint32_t kOffBar = kOffStage + kStages * kStageBytes;
   static constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
   static constexpr uint32_t kTmemS = 0, kTmemDP = 128, kTmemDQ = 256;
   static_assert(kTmemDQ + D <= 512, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "smem budget");
-  static_assert(2 * kSBytes >= (uint32_t)kRows * D * 2, "staging for dQ");
 };
 
 template <int D, bool BF16, bool CAP, bool ALIBI>
@@ -443,10 +414,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     kKVFull = 1,
     kKVEmpty = 1 + NS,
     kSPFull = 1 + 2 * NS,
-    kSPFree = kSPFull + 2,
-    kDSFull = kSPFree + 2,
-    kDSFree = kDSFull + 2,
-    kAccDone = kDSFree + 2,
+    kDSFull = kSPFull + 2,
+    kAccDone = kDSFull + 2,
     kDrain = kAccDone + 1,
     kNever = kDrain + 1,
     kNumBars = kNever + 1
@@ -476,11 +445,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   WaitCtl ctl{abort_flag, p.status, p.timeout_ns};
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kNumBars; ++i) {
-      uint32_t cnt = 1;
-      if ((i >= kSPFree && i < kSPFree + 2) || (i >= kDSFull && i < kDSFull + 2)) cnt = 4;
-      mbar_init(bar(i), cnt);
-    }
+    for (int i = 0; i < kNumBars; ++i)
+      mbar_init(bar(i), (i >= kDSFull && i < kDSFull + 2) ? 4u : 1u);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -495,10 +461,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(bar(kQFull), 2 * L::kQBytes);
-      for (int s = 0; s < L::kSub; ++s) {
-        tma_load_4d(sbase + L::kOffQ + s * (kRows * 128), &tmQ, bar(kQFull), s * 64, q0, hq, b);
-        tma_load_4d(sbase + L::kOffDO + s * (kRows * 128), &tmDO, bar(kQFull), s * 64, q0, hq, b);
+      // A query tile that sees no key loads nothing: its epilogue stages zeros
+      // in the Q tile, which must not have a TMA write in flight.
+      if (n_iter > 0) {
+        mbar_arrive_expect_tx(bar(kQFull), 2 * L::kQBytes);
+        for (int s = 0; s < L::kSub; ++s) {
+          tma_load_4d(sbase + L::kOffQ + s * (kRows * 128), &tmQ, bar(kQFull), s * 64, q0, hq, b);
+          tma_load_4d(sbase + L::kOffDO + s * (kRows * 128), &tmDO, bar(kQFull), s * 64, q0, hq, b);
+        }
       }
       int n = 0;
       for (int i = 0; i < n_iter; ++i) {
@@ -513,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         n = i + 1;
       }
-      drain_wait(bar(kQFull), 0, p.timeout_ns);
+      if (n_iter > 0) drain_wait(bar(kQFull), 0, p.timeout_ns);
       for (int i = (n > NS ? n - NS : 0); i < n; ++i)
         drain_wait(bar(kKVFull + i % NS), (i / NS) & 1, p.timeout_ns);
     }
@@ -536,7 +506,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit(bar(kSPFull + bf));
       };
-      bool ok = mbar_wait(bar(kQFull), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
+      bool ok = n_iter == 0 || mbar_wait(bar(kQFull), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
       if (ok && n_iter > 0) {
         ok = mbar_wait(bar(kKVFull), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
         if (ok) {
@@ -549,22 +519,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (i + 1 < n_iter) {
           const int n1 = i + 1;
           if (!(ok = mbar_wait(bar(kKVFull + n1 % NS), (n1 / NS) & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
-          if (n1 >= 2 && !(ok = mbar_wait(bar(kSPFree + (n1 & 1)), ((n1 >> 1) - 1) & 1, ctl,
-                                          BFA_ERR_DEVICE_TIMEOUT)))
-            break;
           tc_fence_after();
           issue_sp(n1);
         }
         if (!(ok = mbar_wait(bar(kDSFull + bf), k & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
         tc_fence_after();
         const uint32_t ka = stage(i);
-        const uint32_t ds = sbase + L::kOffDS + bf * L::kSBytes;
 #pragma unroll
         for (int kk = 0; kk < kInner / 16; ++kk) {
-          mma_ss(tmem + L::kTmemDQ, desc_kmajor(ds + kk * 32),
+          mma_ts(tmem + L::kTmemDQ, tmem + L::kTmemDP + 64 * bf + kk * 8,
                  desc_mnmajor(ka + kk * 2048, kInner * 128), idAcc, (i > 0 || kk > 0) ? 1u : 0u);
         }
-        mma_commit(bar(kDSFree + bf));
         mma_commit(bar(kKVEmpty + i % NS));
       }
       mma_commit(bar(kAccDone));
@@ -581,13 +546,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float cap_in = CAP ? p.scale / p.soft_cap : 0.f;
     const float cap_out = CAP ? p.soft_cap * kLog2e : 0.f;
     const float slope2 = ALIBI ? p.alibi[hq] * kLog2e : 0.f;
-    const int64_t ridx = ((int64_t)b * p.Hq + hq) * p.Sq + qi;
-    float lse2 = __int_as_float(0x7f800000), dlt = 0.f;
-    if (qi < p.Sq) {
-      const float lse = p.lse[ridx];
-      lse2 = (lse == neg_inf()) ? __int_as_float(0x7f800000) : lse * kLog2e;
-      dlt = p.delta[ridx];
-    }
+    const int64_t ridx = ((int64_t)b * p.Hq + hq) * p.Sq_pad + qi;
+    const float lse2 = p.lse2[ridx];
+    const float dlt = p.delta[ridx];
     bool ok = true;
     for (int i = 0; i < n_iter; ++i) {
       const int bf = i & 1, k = i >> 1;
@@ -599,44 +560,49 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!(ok = warp_wait(wbar, wpar, ctl))) break;
       tc_fence_after();
+      const uint32_t tSb = tmem + lane_base + L::kTmemS + 64 * bf;
+      const uint32_t tDb = tmem + lane_base + L::kTmemDP + 64 * bf;
       uint32_t sr[64], dr[64];
-      tmem_ld32(tmem + lane_base + L::kTmemS + 64 * bf, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-      tmem_ld32(tmem + lane_base + L::kTmemS + 64 * bf + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-      tmem_ld32(tmem + lane_base + L::kTmemDP + 64 * bf, *reinterpret_cast<uint32_t(*)[32]>(&dr[0]));
-      tmem_ld32(tmem + lane_base + L::kTmemDP + 64 * bf + 32, *reinterpret_cast<uint32_t(*)[32]>(&dr[32]));
+      tmem_ld32(tSb, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+      tmem_ld32(tSb + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      tmem_ld32(tDb, *reinterpret_cast<uint32_t(*)[32]>(&dr[0]));
+      tmem_ld32(tDb + 32, *reinterpret_cast<uint32_t(*)[32]>(&dr[32]));
       tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kSPFree + bf));
 
       const bool full = tile_full(p, q0, q0 + kRows, j0, j0 + kInner);
       const float abase = ALIBI ? slope2 * (float)(gi - (int64_t)j0 - p.k_off) : 0.f;
-      float dsv[64];
+      uint32_t dpk[32];
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        float t;
-        float x = logit2<CAP>(__uint_as_float(sr[c]), sl2, cap_in, cap_out, &t);
-        if (ALIBI) x = fmaf(-slope2, (float)c, x + abase);
-        float pr = ex2(x - lse2);
-        if (!full) {
-          const int kj = j0 + c;
-          const bool keep = (qi < p.Sq) && (kj < p.Sk) && keep_pair(gi, (int64_t)kj + p.k_off, p.causal, p.window);
-          pr = keep ? pr : 0.f;
+      for (int c = 0; c < 64; c += 2) {
+        float ds2[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int cc = c + h;
+          float t;
+          float x = logit2<CAP>(__uint_as_float(sr[cc]), sl2, cap_in, cap_out, &t);
+          if (ALIBI) x = fmaf(-slope2, (float)cc, x + abase);
+          float pr = ex2(x - lse2);
+          if (!full) {
+            const int kj = j0 + cc;
+            const bool keep = (qi < p.Sq) && (kj < p.Sk) &&
+                              keep_pair(gi, (int64_t)kj + p.k_off, p.causal, p.window);
+            pr = keep ? pr : 0.f;
+          }
+          float ds = pr * (__uint_as_float(dr[cc]) - dlt) * p.scale;
+          if (CAP) ds *= (1.f - t * t);
+          ds2[h] = ds;
         }
-        float ds = pr * (__uint_as_float(dr[c]) - dlt) * p.scale;
-        if (CAP) ds *= (1.f - t * t);
-        dsv[c] = ds;
+        dpk[c / 2] = pack2<BF16>(ds2[0], ds2[1]);
       }
-      if (k >= 1 && !(ok = warp_wait(bar(kDSFree + bf), (uint32_t)((k - 1) & 1), ctl))) break;
-      store_row64<BF16>(smem + L::kOffDS + bf * L::kSBytes, row, dsv);
-      fence_async_shared();
+      tmem_st32(tDb, dpk);
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kDSFull + bf));
     }
     bool good = ok;
     if (good && n_iter > 0) good = warp_wait(bar(kAccDone), 0, ctl);
-    uint8_t* stage_dq = smem + L::kOffDS;
+    uint8_t* stage_dq = smem + L::kOffQ;  // Q's tile is free once every MMA is done
     if (good) {
       tc_fence_after();
       stage_tmem_row<D, BF16>(tmem + lane_base + L::kTmemDQ, stage_dq, row, n_iter == 0);

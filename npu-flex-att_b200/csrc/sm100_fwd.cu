@@ -37,19 +37,23 @@ using namespace sm100;
 constexpr int kBM = 128;
 constexpr int kBN = 128;
 constexpr int kThreads = 384;
+// Rescale O only when a row's running max grows by more than this (base-2
+// units). Until then P is computed against the stale max, so P <= 2^8; the
+// final O/l and LSE are exact either way.
+constexpr float kRescaleThreshold = 8.0f;
 
 template <int D>
 struct FwdLayout {
   static constexpr int kSub = D / 64;
-  static constexpr int kStages = (D <= 64) ? 6 : 3;
   static constexpr uint32_t kQBytes = kBM * D * 2;
   static constexpr uint32_t kKVBytes = kBN * D * 2;
-  static constexpr uint32_t kPBytes = kBM * kBN * 2;
+  static constexpr int kStages = (D <= 64) ? 8 : 5;  // K/V ring slots
   static constexpr uint32_t kOffQ = 0;
-  static constexpr uint32_t kOffP = kOffQ + 2 * kQBytes;
-  static constexpr uint32_t kOffKV = kOffP + 2 * kPBytes;
+  static constexpr uint32_t kOffKV = kOffQ + 2 * kQBytes;
   static constexpr uint32_t kOffBar = kOffKV + kStages * kKVBytes;
   static constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
+  // TMEM: S_t (fp32, 128 columns) at t * kBN; P_t (16-bit, packed two per
+  // column) overwrites the first 64 columns of S_t; O_t at kTmemO + t * D.
   static constexpr uint32_t kTmemS = 0;
   static constexpr uint32_t kTmemO = 2 * kBN;
   static_assert(kTmemO + 2 * D <= 512, "TMEM budget");
@@ -86,6 +90,11 @@ __device__ __forceinline__ bool tile_full(const Params& p, int r0, int r1, int c
   return true;
 }
 
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  return BF16 ? pack_bf16(a, b) : pack_f16(a, b);
+}
+
 template <int D, bool BF16, bool CAP, bool ALIBI>
 __global__ void __launch_bounds__(kThreads, 1)
     fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -98,8 +107,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     kKVFull = 1,
     kKVEmpty = 1 + NS,
     kSFull = 1 + 2 * NS,
-    kSFree = kSFull + 2,
-    kPFull = kSFree + 2,
+    kPFull = kSFull + 2,
     kODone = kPFull + 2,
     kDrain = kODone + 2,
     kNever = kDrain + 1,
@@ -130,10 +138,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   WaitCtl ctl{abort_flag, p.status, p.timeout_ns};
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kNumBars; ++i) {
-      const bool per_warp = (i >= kSFree && i < kSFree + 2) || (i >= kPFull && i < kPFull + 2);
-      mbar_init(bar(i), per_warp ? 4u : 1u);
-    }
+    for (int i = 0; i < kNumBars; ++i)
+      mbar_init(bar(i), (i >= kPFull && i < kPFull + 2) ? 4u : 1u);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -152,11 +158,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(bar(kQFull), 2 * L::kQBytes);
-      for (int t = 0; t < 2; ++t)
-        for (int s = 0; s < L::kSub; ++s)
-          tma_load_4d(sbase + L::kOffQ + t * L::kQBytes + s * (kBM * 128), &tmQ, bar(kQFull),
-                      s * 64, q0 + t * kBM, hq, b);
+      // A block that sees no key loads nothing: its epilogue stages zeros in
+      // the Q tiles, which must not have a TMA write in flight.
+      if (n_iter > 0) {
+        mbar_arrive_expect_tx(bar(kQFull), 2 * L::kQBytes);
+        for (int t = 0; t < 2; ++t)
+          for (int s = 0; s < L::kSub; ++s)
+            tma_load_4d(sbase + L::kOffQ + t * L::kQBytes + s * (kBM * 128), &tmQ, bar(kQFull),
+                        s * 64, q0 + t * kBM, hq, b);
+      }
       int n = 0;
       bool ok = true;
       for (int it = 0; it < n_iter && ok; ++it) {
@@ -174,12 +184,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++n;
         }
       }
-      drain_wait(bar(kQFull), 0, p.timeout_ns);
+      if (n_iter > 0) drain_wait(bar(kQFull), 0, p.timeout_ns);
       for (int i = (n > NS ? n - NS : 0); i < n; ++i)
         drain_wait(bar(kKVFull + i % NS), (i / NS) & 1, p.timeout_ns);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // Order: S_0(j), S_1(j), then per step PV_0(j), S_0(j+1), PV_1(j), S_1(j+1).
+    // tcgen05 MMAs of one thread run in issue order, so S_t(j+1) (which
+    // overwrites the TMEM holding P_t(j)) runs after PV_t(j) has read P_t(j).
     if (lane == 0) {
       constexpr uint32_t idS = idesc_f16(kBM, kBN, BF16, false);
       constexpr uint32_t idO = idesc_f16(kBM, D, BF16, true);
@@ -199,21 +212,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(bar(kSFull + t));
       };
       auto issue_pv = [&](int t, int idx, bool acc) {
-        const uint32_t pa = sbase + L::kOffP + t * L::kPBytes;
         const uint32_t va = kv_addr(idx);
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint32_t offp = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
-          const uint32_t offv = kk * 16 * 128;
-          mma_ss(tmem + L::kTmemO + t * D, desc_kmajor(pa + offp),
-                 desc_mnmajor(va + offv, kBN * 128), idO, (acc || kk > 0) ? 1u : 0u);
+          mma_ts(tmem + L::kTmemO + t * D, tmem + L::kTmemS + t * kBN + kk * 8,
+                 desc_mnmajor(va + kk * 16 * 128, kBN * 128), idO, (acc || kk > 0) ? 1u : 0u);
         }
         mma_commit(bar(kODone + t));
       };
       auto wait_load = [&](int idx) {
         return mbar_wait(bar(kKVFull + idx % NS), (idx / NS) & 1, ctl, BFA_ERR_DEVICE_TIMEOUT);
       };
-      bool ok = mbar_wait(bar(kQFull), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
+      bool ok = n_iter == 0 || mbar_wait(bar(kQFull), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
       if (ok && n_iter > 0) {
         ok = wait_load(0);
         if (ok) {
@@ -231,7 +241,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           issue_pv(0, iv, it > 0);
           if (more) {
             if (!(ok = wait_load(ik))) break;
-            if (!(ok = mbar_wait(bar(kSFree + 0), it & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
             tc_fence_after();
             issue_s(0, ik);
           }
@@ -240,8 +249,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           issue_pv(1, iv, it > 0);
           mma_commit(bar(kKVEmpty + iv % NS));
           if (more) {
-            if (!(ok = mbar_wait(bar(kSFree + 1), it & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
-            tc_fence_after();
             issue_s(1, ik);
             mma_commit(bar(kKVEmpty + ik % NS));
           }
@@ -265,7 +272,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float cap_out = CAP ? p.soft_cap * kLog2e : 0.f;
     const float slope2 = ALIBI ? p.alibi[hq] * kLog2e : 0.f;
     const int tr0 = q0 + t * kBM;
-    uint8_t* Pt = smem + L::kOffP + t * L::kPBytes;
     float m = neg_inf(), l = 0.f;
     bool ok = true;
 
@@ -283,13 +289,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < kBN / 32; ++c)
         tmem_ld32(tS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&sr[32 * c]));
       tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kSFree + t));
 
       const bool full = tile_full(p, tr0, tr0 + kBM, c0, c0 + kBN);
       const float abase = ALIBI ? slope2 * (float)(gi - (int64_t)c0 - p.k_off) : 0.f;
-      float s[kBN];
       float mx = neg_inf();
 #pragma unroll
       for (int c = 0; c < kBN; ++c) {
@@ -301,23 +303,34 @@ __global__ void __launch_bounds__(kThreads, 1)
           const bool keep = (c0 + c < p.Sk) && keep_pair(gi, gj, p.causal, p.window);
           x = keep ? x : neg_inf();
         }
-        s[c] = x;
+        sr[c] = __float_as_uint(x);
         mx = fmaxf(mx, x);
       }
-      const float m_new = fmaxf(m, mx);
+      // Raise the reference max only when it grows by more than the threshold
+      // (or is still -inf); the decision is warp-uniform because the O rescale
+      // uses warp-collective TMEM loads/stores.
+      const bool grow = (mx > m + kRescaleThreshold) || (m == neg_inf() && mx != neg_inf());
+      const bool rescale = __any_sync(0xffffffffu, grow) && it > 0;
+      float m_new = m;
+      if (__any_sync(0xffffffffu, grow)) m_new = fmaxf(m, mx);
       const float m_use = (m_new == neg_inf()) ? 0.f : m_new;
       const float alpha = ex2(m - m_use);
       float rs = 0.f;
+      uint32_t pk[kBN / 2];
 #pragma unroll
-      for (int c = 0; c < kBN; ++c) {
-        s[c] = ex2(s[c] - m_use);
-        rs += s[c];
+      for (int c = 0; c < kBN; c += 2) {
+        const float p0 = ex2(__uint_as_float(sr[c]) - m_use);
+        const float p1 = ex2(__uint_as_float(sr[c + 1]) - m_use);
+        rs += p0 + p1;
+        pk[c / 2] = pack2<BF16>(p0, p1);
       }
       l = l * alpha + rs;
+      m = m_new;
       if (it > 0) {
+        // PV_t(it-1) is complete (its commit precedes S_t(it)'s), so O_t is stable.
         if (!(ok = warp_wait(bar(kODone + t), (uint32_t)((it - 1) & 1), ctl))) break;
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+        if (rescale) {
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
             uint32_t r[32];
@@ -327,27 +340,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
             tmem_st32(tO + 32 * c, r);
           }
-          tmem_st_wait();
         }
       }
-      m = m_new;
-#pragma unroll
-      for (int c16 = 0; c16 < kBN / 8; ++c16) {
-        uint4 v;
-        if (BF16) {
-          v.x = pack_bf16(s[8 * c16 + 0], s[8 * c16 + 1]);
-          v.y = pack_bf16(s[8 * c16 + 2], s[8 * c16 + 3]);
-          v.z = pack_bf16(s[8 * c16 + 4], s[8 * c16 + 5]);
-          v.w = pack_bf16(s[8 * c16 + 6], s[8 * c16 + 7]);
-        } else {
-          v.x = pack_f16(s[8 * c16 + 0], s[8 * c16 + 1]);
-          v.y = pack_f16(s[8 * c16 + 2], s[8 * c16 + 3]);
-          v.z = pack_f16(s[8 * c16 + 4], s[8 * c16 + 5]);
-          v.w = pack_f16(s[8 * c16 + 6], s[8 * c16 + 7]);
-        }
-        *reinterpret_cast<uint4*>(Pt + (c16 >> 3) * (kBM * 128) + sw128_offset(row, c16 & 7)) = v;
-      }
-      fence_async_shared();
+      tmem_st32(tS, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
+      tmem_st32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kPFull + t));
@@ -356,6 +353,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     bool good = ok;
     if (good && n_iter > 0) good = warp_wait(bar(kODone + t), (uint32_t)((n_iter - 1) & 1), ctl);
+    // Q_t's smem tile is free once the last S_t MMA has run; it stages O_t.
+    uint8_t* Ot = smem + L::kOffQ + t * L::kQBytes;
     if (good) {
       tc_fence_after();
       const float inv = (l > 0.f) ? 1.f / l : 0.f;
@@ -371,19 +370,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          float f[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(r[8 * q + i]) * inv;
           uint4 v;
-          if (BF16) {
-            v.x = pack_bf16(f[0], f[1]); v.y = pack_bf16(f[2], f[3]);
-            v.z = pack_bf16(f[4], f[5]); v.w = pack_bf16(f[6], f[7]);
-          } else {
-            v.x = pack_f16(f[0], f[1]); v.y = pack_f16(f[2], f[3]);
-            v.z = pack_f16(f[4], f[5]); v.w = pack_f16(f[6], f[7]);
-          }
+          v.x = pack2<BF16>(__uint_as_float(r[8 * q + 0]) * inv, __uint_as_float(r[8 * q + 1]) * inv);
+          v.y = pack2<BF16>(__uint_as_float(r[8 * q + 2]) * inv, __uint_as_float(r[8 * q + 3]) * inv);
+          v.z = pack2<BF16>(__uint_as_float(r[8 * q + 4]) * inv, __uint_as_float(r[8 * q + 5]) * inv);
+          v.w = pack2<BF16>(__uint_as_float(r[8 * q + 6]) * inv, __uint_as_float(r[8 * q + 7]) * inv);
           const int col = 32 * c + 8 * q;
-          *reinterpret_cast<uint4*>(Pt + (col >> 6) * (kBM * 128) + sw128_offset(row, (col & 63) >> 3)) = v;
+          *reinterpret_cast<uint4*>(Ot + (col >> 6) * (kBM * 128) + sw128_offset(row, (col & 63) >> 3)) = v;
         }
       }
       fence_async_shared();
@@ -394,7 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool all = warp_ok[4 * t] && warp_ok[4 * t + 1] && warp_ok[4 * t + 2] && warp_ok[4 * t + 3];
       if (all) {
         for (int s = 0; s < L::kSub; ++s)
-          tma_store_4d(&tmO, smem_u32(Pt) + s * (kBM * 128), s * 64, tr0, hq, b);
+          tma_store_4d(&tmO, smem_u32(Ot) + s * (kBM * 128), s * 64, tr0, hq, b);
         tma_store_commit();
         tma_store_wait_all();
       }

@@ -3,8 +3,9 @@
 Some callers cannot give the library a workspace: a plugin inside a host
 framework that owns all device memory and hands over only the input and
 output buffers, or a hot path that must not call cudaMalloc because it can
-synchronise the device. bfa_bwd_noalloc keeps the backward's Δ scratch in a
-static device array (2^21 query rows) instead. These tests call it through
+synchronise the device. bfa_bwd_noalloc keeps the backward's row statistics
+in a static device array (2^21 query rows, each head's rows rounded up to 64)
+instead. These tests call it through
 the C ABI and check it against the regular bfa_bwd entry point.
 
 The file is named so that pytest collects it last.
