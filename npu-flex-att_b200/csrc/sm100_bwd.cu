@@ -35,7 +35,7 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;  // warps 0-3: TMA / MMA / TMEM alloc / idle; 4-11: two elementwise warpgroups
 constexpr int kRows = 128;  // TMEM lanes / rows owned by the elementwise warps
 constexpr int kInner = 64;  // columns of one S/dP step
 
@@ -284,6 +284,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ elementwise
+    // Two warpgroups take alternate steps (step parity = TMEM buffer), so the
+    // exp / scale work of consecutive steps overlaps. Each thread owns one key
+    // row (TMEM lane) and walks the 64 query columns in two halves of 32.
+    const int eg = (warp - 4) >> 2;
     const int wq = warp & 3;
     const int row = wq * 32 + lane;  // key row within the tile
     const int kj = c0 + row;
@@ -293,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float cap_in = CAP ? p.scale / p.soft_cap : 0.f;
     const float cap_out = CAP ? p.soft_cap * kLog2e : 0.f;
     bool ok = true;
-    for (int i = 0; i < n_iter; ++i) {
+    for (int i = eg; i < n_iter; i += 2) {
       const int bf = i & 1, k = i >> 1, st = i % NS;
       const int hq = hkv * p.G + i / n_qt;
       const int q0 = (qt0 + i % n_qt) * kInner;
@@ -308,69 +312,86 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t tSb = tmem + lane_base + L::kTmemS + 64 * bf;
       const uint32_t tDb = tmem + lane_base + L::kTmemDP + 64 * bf;
-      uint32_t sr[64], dr[64];
-      tmem_ld32(tSb, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-      tmem_ld32(tSb + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-      tmem_ld32(tDb, *reinterpret_cast<uint32_t(*)[32]>(&dr[0]));
-      tmem_ld32(tDb + 32, *reinterpret_cast<uint32_t(*)[32]>(&dr[32]));
-      tmem_ld_wait();
-
       const float* rowv = (const float*)(smem + L::kOffRow + st * 512);
       const bool full = tile_full(p, q0, q0 + kInner, c0, c0 + kRows);
       const float slope2 = ALIBI ? p.alibi[hq] * kLog2e : 0.f;
       const float abase = ALIBI ? slope2 * (float)((int64_t)q0 + p.q_off - gj) : 0.f;
-      uint32_t ppk[32], dpk[32];
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        uint32_t sr[32], dr[32];
+        tmem_ld32(tSb + 32 * half, sr);
+        tmem_ld32(tDb + 32 * half, dr);
+        tmem_ld_wait();
+        uint32_t ppk[16], dpk[16];
 #pragma unroll
-      for (int c = 0; c < 64; c += 2) {
-        float pr2[2], ds2[2];
+        for (int c = 0; c < 32; c += 4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(rowv + 32 * half + c);
+          const float4 d4 = *reinterpret_cast<const float4*>(rowv + 64 + 32 * half + c);
+          const float lse_c[4] = {l4.x, l4.y, l4.z, l4.w};
+          const float dl_c[4] = {d4.x, d4.y, d4.z, d4.w};
+          float pr4[4], ds4[4];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int cc = c + h;
-          float t;
-          float x = logit2<CAP>(__uint_as_float(sr[cc]), sl2, cap_in, cap_out, &t);
-          if (ALIBI) x = fmaf(slope2, (float)cc, x + abase);
-          float pr = ex2(x - rowv[cc]);
-          if (!full) {
-            const int qi = q0 + cc;
-            const bool keep = (qi < p.Sq) && (kj < p.Sk) &&
-                              keep_pair((int64_t)qi + p.q_off, gj, p.causal, p.window);
-            pr = keep ? pr : 0.f;
+          for (int h = 0; h < 4; ++h) {
+            const int cc = 32 * half + c + h;
+            const float raw = __uint_as_float(sr[c + h]);
+            float pr, t = 0.f;
+            if (CAP || ALIBI) {
+              float x = logit2<CAP>(raw, sl2, cap_in, cap_out, &t);
+              if (ALIBI) x = fmaf(slope2, (float)cc, x + abase);
+              pr = ex2(x - lse_c[h]);
+            } else {
+              pr = ex2(fmaf(raw, sl2, -lse_c[h]));
+            }
+            if (!full) {
+              const int qi = q0 + cc;
+              const bool keep = (qi < p.Sq) && (kj < p.Sk) &&
+                                keep_pair((int64_t)qi + p.q_off, gj, p.causal, p.window);
+              pr = keep ? pr : 0.f;
+            }
+            float ds = pr * (__uint_as_float(dr[c + h]) - dl_c[h]) * p.scale;
+            if (CAP) ds *= (1.f - t * t);
+            pr4[h] = pr;
+            ds4[h] = ds;
           }
-          float ds = pr * (__uint_as_float(dr[cc]) - rowv[64 + cc]) * p.scale;
-          if (CAP) ds *= (1.f - t * t);
-          pr2[h] = pr;
-          ds2[h] = ds;
+          ppk[c / 2] = pack2<BF16>(pr4[0], pr4[1]);
+          ppk[c / 2 + 1] = pack2<BF16>(pr4[2], pr4[3]);
+          dpk[c / 2] = pack2<BF16>(ds4[0], ds4[1]);
+          dpk[c / 2 + 1] = pack2<BF16>(ds4[2], ds4[3]);
         }
-        ppk[c / 2] = pack2<BF16>(pr2[0], pr2[1]);
-        dpk[c / 2] = pack2<BF16>(ds2[0], ds2[1]);
+        // Pᵀ / dSᵀ half h -> packed columns [16h, 16h + 16) of the buffer; the
+        // fp32 columns they overwrite were read above (half 1 reads 32..63).
+        tmem_st16(tSb + 16 * half, ppk);
+        tmem_st16(tDb + 16 * half, dpk);
       }
-      tmem_st32(tSb, ppk);
-      tmem_st32(tDb, dpk);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kDSFull + bf));
     }
-    bool good = ok;
-    if (good && n_iter > 0) good = warp_wait(bar(kAccDone), 0, ctl);
-    // K and V tiles are free once every MMA is done: they stage dK and dV.
-    uint8_t* stage_dk = smem + L::kOffK;
-    uint8_t* stage_dv = smem + L::kOffV;
-    if (good) {
-      tc_fence_after();
-      stage_tmem_row<D, BF16>(tmem + lane_base + L::kTmemDV, stage_dv, row, n_iter == 0);
-      stage_tmem_row<D, BF16>(tmem + lane_base + L::kTmemDK, stage_dk, row, n_iter == 0);
-      fence_async_shared();
-    }
-    if (lane == 0) warp_ok[wq] = good ? 1 : 0;
-    named_sync(1, 128);
-    if (wq == 0 && lane == 0 && warp_ok[0] && warp_ok[1] && warp_ok[2] && warp_ok[3]) {
-      for (int s = 0; s < L::kSub; ++s) {
-        tma_store_4d(&tmDV, smem_u32(stage_dv) + s * (kRows * 128), s * 64, c0, hkv, b);
-        tma_store_4d(&tmDK, smem_u32(stage_dk) + s * (kRows * 128), s * 64, c0, hkv, b);
+    // Warpgroup 0 runs the epilogue; warpgroup 1 goes straight to the exit.
+    if (eg == 0) {
+      bool good = ok;
+      if (good && n_iter > 0) good = warp_wait(bar(kAccDone), 0, ctl);
+      good = good && !*abort_flag;
+      // K and V tiles are free once every MMA is done: they stage dK and dV.
+      uint8_t* stage_dk = smem + L::kOffK;
+      uint8_t* stage_dv = smem + L::kOffV;
+      if (good) {
+        tc_fence_after();
+        stage_tmem_row<D, BF16>(tmem + lane_base + L::kTmemDV, stage_dv, row, n_iter == 0);
+        stage_tmem_row<D, BF16>(tmem + lane_base + L::kTmemDK, stage_dk, row, n_iter == 0);
+        fence_async_shared();
       }
-      tma_store_commit();
-      tma_store_wait_all();
+      if (lane == 0) warp_ok[wq] = good ? 1 : 0;
+      named_sync(1, 128);
+      if (wq == 0 && lane == 0 && warp_ok[0] && warp_ok[1] && warp_ok[2] && warp_ok[3]) {
+        for (int s = 0; s < L::kSub; ++s) {
+          tma_store_4d(&tmDV, smem_u32(stage_dv) + s * (kRows * 128), s * 64, c0, hkv, b);
+          tma_store_4d(&tmDK, smem_u32(stage_dk) + s * (kRows * 128), s * 64, c0, hkv, b);
+        }
+        tma_store_commit();
+        tma_store_wait_all();
+      }
     }
   }
 
@@ -537,6 +558,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       drain_wait(bar(kDrain), 0, p.timeout_ns);
     }
   } else if (warp >= 4) {
+    // Two warpgroups take alternate steps (step parity = TMEM buffer); each
+    // thread owns one query row and walks the 64 key columns in two halves.
+    const int eg = (warp - 4) >> 2;
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
     const int qi = q0 + row;
@@ -550,7 +574,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float lse2 = p.lse2[ridx];
     const float dlt = p.delta[ridx];
     bool ok = true;
-    for (int i = 0; i < n_iter; ++i) {
+    for (int i = eg; i < n_iter; i += 2) {
       const int bf = i & 1, k = i >> 1;
       const int j0 = (jt0 + i) * kInner;
       uint32_t wbar = bar(kSPFull + bf), wpar = (uint32_t)(k & 1);
@@ -562,59 +586,69 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t tSb = tmem + lane_base + L::kTmemS + 64 * bf;
       const uint32_t tDb = tmem + lane_base + L::kTmemDP + 64 * bf;
-      uint32_t sr[64], dr[64];
-      tmem_ld32(tSb, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-      tmem_ld32(tSb + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-      tmem_ld32(tDb, *reinterpret_cast<uint32_t(*)[32]>(&dr[0]));
-      tmem_ld32(tDb + 32, *reinterpret_cast<uint32_t(*)[32]>(&dr[32]));
-      tmem_ld_wait();
-
       const bool full = tile_full(p, q0, q0 + kRows, j0, j0 + kInner);
       const float abase = ALIBI ? slope2 * (float)(gi - (int64_t)j0 - p.k_off) : 0.f;
-      uint32_t dpk[32];
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        uint32_t sr[32], dr[32];
+        tmem_ld32(tSb + 32 * half, sr);
+        tmem_ld32(tDb + 32 * half, dr);
+        tmem_ld_wait();
+        uint32_t dpk[16];
 #pragma unroll
-      for (int c = 0; c < 64; c += 2) {
-        float ds2[2];
+        for (int c = 0; c < 32; c += 2) {
+          float ds2[2];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int cc = c + h;
-          float t;
-          float x = logit2<CAP>(__uint_as_float(sr[cc]), sl2, cap_in, cap_out, &t);
-          if (ALIBI) x = fmaf(-slope2, (float)cc, x + abase);
-          float pr = ex2(x - lse2);
-          if (!full) {
-            const int kj = j0 + cc;
-            const bool keep = (qi < p.Sq) && (kj < p.Sk) &&
-                              keep_pair(gi, (int64_t)kj + p.k_off, p.causal, p.window);
-            pr = keep ? pr : 0.f;
+          for (int h = 0; h < 2; ++h) {
+            const int cc = 32 * half + c + h;
+            const float raw = __uint_as_float(sr[c + h]);
+            float pr, t = 0.f;
+            if (CAP || ALIBI) {
+              float x = logit2<CAP>(raw, sl2, cap_in, cap_out, &t);
+              if (ALIBI) x = fmaf(-slope2, (float)cc, x + abase);
+              pr = ex2(x - lse2);
+            } else {
+              pr = ex2(fmaf(raw, sl2, -lse2));
+            }
+            if (!full) {
+              const int kj = j0 + cc;
+              const bool keep = (qi < p.Sq) && (kj < p.Sk) &&
+                                keep_pair(gi, (int64_t)kj + p.k_off, p.causal, p.window);
+              pr = keep ? pr : 0.f;
+            }
+            float ds = pr * (__uint_as_float(dr[c + h]) - dlt) * p.scale;
+            if (CAP) ds *= (1.f - t * t);
+            ds2[h] = ds;
           }
-          float ds = pr * (__uint_as_float(dr[cc]) - dlt) * p.scale;
-          if (CAP) ds *= (1.f - t * t);
-          ds2[h] = ds;
+          dpk[c / 2] = pack2<BF16>(ds2[0], ds2[1]);
         }
-        dpk[c / 2] = pack2<BF16>(ds2[0], ds2[1]);
+        // dS half h -> packed columns [16h, 16h + 16) of the dP buffer; the
+        // fp32 columns they overwrite were already read.
+        tmem_st16(tDb + 16 * half, dpk);
       }
-      tmem_st32(tDb, dpk);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kDSFull + bf));
     }
-    bool good = ok;
-    if (good && n_iter > 0) good = warp_wait(bar(kAccDone), 0, ctl);
-    uint8_t* stage_dq = smem + L::kOffQ;  // Q's tile is free once every MMA is done
-    if (good) {
-      tc_fence_after();
-      stage_tmem_row<D, BF16>(tmem + lane_base + L::kTmemDQ, stage_dq, row, n_iter == 0);
-      fence_async_shared();
-    }
-    if (lane == 0) warp_ok[wq] = good ? 1 : 0;
-    named_sync(1, 128);
-    if (wq == 0 && lane == 0 && warp_ok[0] && warp_ok[1] && warp_ok[2] && warp_ok[3]) {
-      for (int s = 0; s < L::kSub; ++s)
-        tma_store_4d(&tmDQ, smem_u32(stage_dq) + s * (kRows * 128), s * 64, q0, hq, b);
-      tma_store_commit();
-      tma_store_wait_all();
+    if (eg == 0) {
+      bool good = ok;
+      if (good && n_iter > 0) good = warp_wait(bar(kAccDone), 0, ctl);
+      good = good && !*abort_flag;
+      uint8_t* stage_dq = smem + L::kOffQ;  // Q's tile is free once every MMA is done
+      if (good) {
+        tc_fence_after();
+        stage_tmem_row<D, BF16>(tmem + lane_base + L::kTmemDQ, stage_dq, row, n_iter == 0);
+        fence_async_shared();
+      }
+      if (lane == 0) warp_ok[wq] = good ? 1 : 0;
+      named_sync(1, 128);
+      if (wq == 0 && lane == 0 && warp_ok[0] && warp_ok[1] && warp_ok[2] && warp_ok[3]) {
+        for (int s = 0; s < L::kSub; ++s)
+          tma_store_4d(&tmDQ, smem_u32(stage_dq) + s * (kRows * 128), s * 64, q0, hq, b);
+        tma_store_commit();
+        tma_store_wait_all();
+      }
     }
   }
 

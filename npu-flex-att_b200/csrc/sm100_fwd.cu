@@ -284,28 +284,52 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!(ok = warp_wait(wbar, wpar, ctl))) break;
       tc_fence_after();
-      uint32_t sr[kBN];
-#pragma unroll
-      for (int c = 0; c < kBN / 32; ++c)
-        tmem_ld32(tS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&sr[32 * c]));
-      tmem_ld_wait();
 
+      // Two passes over the S row in 32-column TMEM chunks keep the register
+      // footprint small (a whole 128-value row plus packed P does not fit the
+      // 168 registers a thread has at 384 threads without spilling).
+      // Pass 1: logits in base 2 (cap, ALiBi, mask) and their row max. When
+      // the logit is more than a scaled copy of S it is written back to TMEM.
+      // The chunk loops stay rolled (one 32-column body in the instruction
+      // cache); four independent max / sum accumulators break the dependency
+      // chains. A plain, fully kept tile only needs max(S) (the scale is > 0)
+      // and folds the scale into the exponent with one FMA.
       const bool full = tile_full(p, tr0, tr0 + kBM, c0, c0 + kBN);
+      const bool store_x = CAP || ALIBI || !full || !(sl2 > 0.f);
       const float abase = ALIBI ? slope2 * (float)(gi - (int64_t)c0 - p.k_off) : 0.f;
-      float mx = neg_inf();
+      float mx;
+      {
+        float m4[4] = {neg_inf(), neg_inf(), neg_inf(), neg_inf()};
+#pragma unroll 1
+        for (int ch = 0; ch < kBN / 32; ++ch) {
+          uint32_t r[32];
+          tmem_ld32(tS + 32 * ch, r);
+          tmem_ld_wait();
+          if (!store_x) {
 #pragma unroll
-      for (int c = 0; c < kBN; ++c) {
-        const float raw = __uint_as_float(sr[c]);
-        float x = CAP ? cap_out * tanh_exp(raw * cap_in) : raw * sl2;
-        if (ALIBI) x = fmaf(-slope2, (float)c, x + abase);
-        if (!full) {
-          const int64_t gj = (int64_t)c0 + c + p.k_off;
-          const bool keep = (c0 + c < p.Sk) && keep_pair(gi, gj, p.causal, p.window);
-          x = keep ? x : neg_inf();
+            for (int e = 0; e < 32; ++e) m4[e & 3] = fmaxf(m4[e & 3], __uint_as_float(r[e]));
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int c = 32 * ch + e;
+              const float raw = __uint_as_float(r[e]);
+              float x = CAP ? cap_out * tanh_exp(raw * cap_in) : raw * sl2;
+              if (ALIBI) x = fmaf(-slope2, (float)c, x + abase);
+              if (!full) {
+                const int64_t gj = (int64_t)c0 + c + p.k_off;
+                const bool keep = (c0 + c < p.Sk) && keep_pair(gi, gj, p.causal, p.window);
+                x = keep ? x : neg_inf();
+              }
+              r[e] = __float_as_uint(x);
+              m4[e & 3] = fmaxf(m4[e & 3], x);
+            }
+            tmem_st32(tS + 32 * ch, r);
+          }
         }
-        sr[c] = __float_as_uint(x);
-        mx = fmaxf(mx, x);
+        mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        if (!store_x) mx *= sl2;
       }
+      if (store_x) tmem_st_wait();
       // Raise the reference max only when it grows by more than the threshold
       // (or is still -inf); the decision is warp-uniform because the O rescale
       // uses warp-collective TMEM loads/stores.
@@ -315,15 +339,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (__any_sync(0xffffffffu, grow)) m_new = fmaxf(m, mx);
       const float m_use = (m_new == neg_inf()) ? 0.f : m_new;
       const float alpha = ex2(m - m_use);
-      float rs = 0.f;
-      uint32_t pk[kBN / 2];
+      // Pass 2: P = 2^(x - m) packed to 16 bits over the first 64 columns of
+      // the S region. Chunk ch writes packed columns [16ch, 16ch + 16), all
+      // of which were already read (by chunk ch or an earlier one).
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
+      const float xs = store_x ? 1.f : sl2;  // x = raw * xs
+#pragma unroll 1
+      for (int ch = 0; ch < kBN / 32; ++ch) {
+        uint32_t r[32];
+        tmem_ld32(tS + 32 * ch, r);
+        tmem_ld_wait();
+        uint32_t pk[16];
 #pragma unroll
-      for (int c = 0; c < kBN; c += 2) {
-        const float p0 = ex2(__uint_as_float(sr[c]) - m_use);
-        const float p1 = ex2(__uint_as_float(sr[c + 1]) - m_use);
-        rs += p0 + p1;
-        pk[c / 2] = pack2<BF16>(p0, p1);
+        for (int e = 0; e < 32; e += 2) {
+          const float p0 = ex2(fmaf(__uint_as_float(r[e]), xs, -m_use));
+          const float p1 = ex2(fmaf(__uint_as_float(r[e + 1]), xs, -m_use));
+          s4[(e >> 1) & 3] += p0 + p1;
+          pk[e / 2] = pack2<BF16>(p0, p1);
+        }
+        tmem_st16(tS + 16 * ch, pk);
       }
+      const float rs = (s4[0] + s4[1]) + (s4[2] + s4[3]);
       l = l * alpha + rs;
       m = m_new;
       if (it > 0) {
@@ -342,8 +378,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      tmem_st32(tS, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
-      tmem_st32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
