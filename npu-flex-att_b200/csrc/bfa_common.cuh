@@ -77,6 +77,36 @@ __device__ __forceinline__ float transform_logit(float dot, float scale, float c
   return s;
 }
 
+// Kept key columns [lo, hi) for one query row: the columns are local keys
+// j0 + c, c in [0, n). `row_ok` false (a padding row) gives an empty range.
+__device__ __forceinline__ void keys_for_query(const Params& p, int64_t gi, bool row_ok, int j0,
+                                               int n, int* lo, int* hi) {
+  int64_t l = 0, h = n;
+  h = min(h, (int64_t)p.Sk - j0);
+  if (p.causal) h = min(h, gi - p.k_off - j0 + 1);
+  if (p.window > 0) l = max(l, gi - p.window - p.k_off - j0);
+  if (!row_ok || h < l) h = l;
+  l = max((int64_t)0, min(l, (int64_t)n));
+  h = max(l, min(h, (int64_t)n));
+  *lo = (int)l;
+  *hi = (int)h;
+}
+
+// Kept query columns [lo, hi) for one key row: the columns are local queries
+// q0 + c, c in [0, n).
+__device__ __forceinline__ void queries_for_key(const Params& p, int64_t gj, bool row_ok, int q0,
+                                                int n, int* lo, int* hi) {
+  int64_t l = 0, h = n;
+  h = min(h, (int64_t)p.Sq - q0);
+  if (p.causal) l = max(l, gj - p.q_off - q0);
+  if (p.window > 0) h = min(h, gj + p.window - p.q_off - q0 + 1);
+  if (!row_ok || h < l) h = l;
+  l = max((int64_t)0, min(l, (int64_t)n));
+  h = max(l, min(h, (int64_t)n));
+  *lo = (int)l;
+  *hi = (int)h;
+}
+
 // Range of key indices [lo, hi) (local) that can be kept for local query
 // rows [r0, r1). Tiles outside it are fully masked and skipped.
 __device__ __forceinline__ void key_range(const Params& p, int r0, int r1, int* lo, int* hi) {

@@ -25,6 +25,7 @@
 #include <cuda_runtime.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "bfa_internal.h"
 #include "sm100_host.h"
@@ -38,22 +39,6 @@ using namespace sm100;
 constexpr int kThreads = 384;  // warps 0-3: TMA / MMA / TMEM alloc / idle; 4-11: two elementwise warpgroups
 constexpr int kRows = 128;  // TMEM lanes / rows owned by the elementwise warps
 constexpr int kInner = 64;  // columns of one S/dP step
-
-__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const WaitCtl& ctl) {
-  int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, ctl, BFA_ERR_DEVICE_TIMEOUT) ? 1 : 0;
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  __syncwarp();
-  return ok != 0;
-}
-
-__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, uint64_t timeout_ns) {
-  if (mbar_try_wait(bar, parity)) return;
-  const uint64_t t0 = globaltimer();
-  while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer() - t0 > timeout_ns) return;
-  }
-}
 
 __device__ __forceinline__ bool tile_full(const Params& p, int r0, int r1, int c0, int c1) {
   if (r1 > p.Sq || c1 > p.Sk) return false;
@@ -235,17 +220,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idSP = idesc_f16(kRows, kInner, BF16, false);
       constexpr uint32_t idAcc = idesc_f16(kRows, D, BF16, true);
       auto stage = [&](int i) -> uint32_t { return sbase + L::kOffStage + (i % NS) * L::kStageBytes; };
+      // Descriptors are built once; a K step only moves the start address
+      // (a compile-time offset added to the low field).
+      const uint64_t dK0 = desc_kmajor(sbase + L::kOffK), dV0 = desc_kmajor(sbase + L::kOffV);
       auto issue_sp = [&](int i) {
         const int bf = i & 1;
-        const uint32_t qa = stage(i), da = stage(i) + L::kQBytes;
+        const uint64_t dq = desc_kmajor(stage(i)), ddo = desc_kmajor(stage(i) + L::kQBytes);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t offkv = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
-          const uint32_t offq = (kk >> 2) * (kInner * 128) + (kk & 3) * 32;
-          mma_ss(tmem + L::kTmemS + 64 * bf, desc_kmajor(sbase + L::kOffK + offkv),
-                 desc_kmajor(qa + offq), idSP, kk > 0 ? 1u : 0u);
-          mma_ss(tmem + L::kTmemDP + 64 * bf, desc_kmajor(sbase + L::kOffV + offkv),
-                 desc_kmajor(da + offq), idSP, kk > 0 ? 1u : 0u);
+          const uint32_t offkv = ((kk >> 2) * (kRows * 128) + (kk & 3) * 32) >> 4;
+          const uint32_t offq = ((kk >> 2) * (kInner * 128) + (kk & 3) * 32) >> 4;
+          mma_ss(tmem + L::kTmemS + 64 * bf, dK0 + offkv, dq + offq, idSP, kk > 0 ? 1u : 0u);
+          mma_ss(tmem + L::kTmemDP + 64 * bf, dV0 + offkv, ddo + offq, idSP, kk > 0 ? 1u : 0u);
         }
         mma_commit(bar(kSPFull + bf));
       };
@@ -267,14 +253,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!(ok = mbar_wait(bar(kDSFull + bf), k & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
         tc_fence_after();
-        const uint32_t qa = stage(i), da = stage(i) + L::kQBytes;
+        const uint64_t mq = desc_mnmajor(stage(i), kInner * 128);
+        const uint64_t mdo = desc_mnmajor(stage(i) + L::kQBytes, kInner * 128);
 #pragma unroll
         for (int kk = 0; kk < kInner / 16; ++kk) {
           const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-          mma_ts(tmem + L::kTmemDV, tmem + L::kTmemS + 64 * bf + kk * 8,
-                 desc_mnmajor(da + kk * 2048, kInner * 128), idAcc, acc);
-          mma_ts(tmem + L::kTmemDK, tmem + L::kTmemDP + 64 * bf + kk * 8,
-                 desc_mnmajor(qa + kk * 2048, kInner * 128), idAcc, acc);
+          mma_ts(tmem + L::kTmemDV, tmem + L::kTmemS + 64 * bf + kk * 8, mdo + ((kk * 2048) >> 4),
+                 idAcc, acc);
+          mma_ts(tmem + L::kTmemDK, tmem + L::kTmemDP + 64 * bf + kk * 8, mq + ((kk * 2048) >> 4),
+                 idAcc, acc);
         }
         mma_commit(bar(kQEmpty + i % NS));
       }
@@ -316,53 +303,57 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool full = tile_full(p, q0, q0 + kInner, c0, c0 + kRows);
       const float slope2 = ALIBI ? p.alibi[hq] * kLog2e : 0.f;
       const float abase = ALIBI ? slope2 * (float)((int64_t)q0 + p.q_off - gj) : 0.f;
+      int clo, chi;  // kept query columns [clo, chi) of this key row
+      queries_for_key(p, gj, kj < p.Sk, q0, kInner, &clo, &chi);
+      // One body per case (mask or not), chosen once per step: no branches
+      // inside the unrolled column loop.
+      auto step = [&](auto masked) {
+        constexpr bool MASKED = decltype(masked)::value;
 #pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        uint32_t sr[32], dr[32];
-        tmem_ld32(tSb + 32 * half, sr);
-        tmem_ld32(tDb + 32 * half, dr);
-        tmem_ld_wait();
-        uint32_t ppk[16], dpk[16];
+        for (int half = 0; half < 2; ++half) {
+          uint32_t sr[32], dr[32];
+          tmem_ld32(tSb + 32 * half, sr);
+          tmem_ld32(tDb + 32 * half, dr);
+          tmem_ld_wait();
+          uint32_t ppk[16], dpk[16];
 #pragma unroll
-        for (int c = 0; c < 32; c += 4) {
-          const float4 l4 = *reinterpret_cast<const float4*>(rowv + 32 * half + c);
-          const float4 d4 = *reinterpret_cast<const float4*>(rowv + 64 + 32 * half + c);
-          const float lse_c[4] = {l4.x, l4.y, l4.z, l4.w};
-          const float dl_c[4] = {d4.x, d4.y, d4.z, d4.w};
-          float pr4[4], ds4[4];
+          for (int c = 0; c < 32; c += 4) {
+            const float4 l4 = *reinterpret_cast<const float4*>(rowv + 32 * half + c);
+            const float4 d4 = *reinterpret_cast<const float4*>(rowv + 64 + 32 * half + c);
+            const float lse_c[4] = {l4.x, l4.y, l4.z, l4.w};
+            const float dl_c[4] = {d4.x, d4.y, d4.z, d4.w};
+            float pr4[4], ds4[4];
 #pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            const int cc = 32 * half + c + h;
-            const float raw = __uint_as_float(sr[c + h]);
-            float pr, t = 0.f;
-            if (CAP || ALIBI) {
-              float x = logit2<CAP>(raw, sl2, cap_in, cap_out, &t);
-              if (ALIBI) x = fmaf(slope2, (float)cc, x + abase);
-              pr = ex2(x - lse_c[h]);
-            } else {
-              pr = ex2(fmaf(raw, sl2, -lse_c[h]));
+            for (int h = 0; h < 4; ++h) {
+              const int cc = 32 * half + c + h;
+              const float raw = __uint_as_float(sr[c + h]);
+              float pr, t = 0.f;
+              if (CAP || ALIBI) {
+                float x = logit2<CAP>(raw, sl2, cap_in, cap_out, &t);
+                if (ALIBI) x = fmaf(slope2, (float)cc, x + abase);
+                pr = ex2(x - lse_c[h]);
+              } else {
+                pr = ex2(fmaf(raw, sl2, -lse_c[h]));
+              }
+              if (MASKED) pr = ((unsigned)(cc - clo) < (unsigned)(chi - clo)) ? pr : 0.f;
+              float ds = pr * (__uint_as_float(dr[c + h]) - dl_c[h]) * p.scale;
+              if (CAP) ds *= (1.f - t * t);
+              pr4[h] = pr;
+              ds4[h] = ds;
             }
-            if (!full) {
-              const int qi = q0 + cc;
-              const bool keep = (qi < p.Sq) && (kj < p.Sk) &&
-                                keep_pair((int64_t)qi + p.q_off, gj, p.causal, p.window);
-              pr = keep ? pr : 0.f;
-            }
-            float ds = pr * (__uint_as_float(dr[c + h]) - dl_c[h]) * p.scale;
-            if (CAP) ds *= (1.f - t * t);
-            pr4[h] = pr;
-            ds4[h] = ds;
+            ppk[c / 2] = pack2<BF16>(pr4[0], pr4[1]);
+            ppk[c / 2 + 1] = pack2<BF16>(pr4[2], pr4[3]);
+            dpk[c / 2] = pack2<BF16>(ds4[0], ds4[1]);
+            dpk[c / 2 + 1] = pack2<BF16>(ds4[2], ds4[3]);
           }
-          ppk[c / 2] = pack2<BF16>(pr4[0], pr4[1]);
-          ppk[c / 2 + 1] = pack2<BF16>(pr4[2], pr4[3]);
-          dpk[c / 2] = pack2<BF16>(ds4[0], ds4[1]);
-          dpk[c / 2 + 1] = pack2<BF16>(ds4[2], ds4[3]);
+          // Pᵀ / dSᵀ half h -> packed columns [16h, 16h + 16) of the buffer; the
+          // fp32 columns they overwrite were read above (half 1 reads 32..63).
+          tmem_st16(tSb + 16 * half, ppk);
+          tmem_st16(tDb + 16 * half, dpk);
         }
-        // Pᵀ / dSᵀ half h -> packed columns [16h, 16h + 16) of the buffer; the
-        // fp32 columns they overwrite were read above (half 1 reads 32..63).
-        tmem_st16(tSb + 16 * half, ppk);
-        tmem_st16(tDb + 16 * half, dpk);
-      }
+      };
+      if (full) step(std::false_type{});
+      else step(std::true_type{});
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
@@ -513,17 +504,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idSP = idesc_f16(kRows, kInner, BF16, false);
       constexpr uint32_t idAcc = idesc_f16(kRows, D, BF16, true);
       auto stage = [&](int i) -> uint32_t { return sbase + L::kOffStage + (i % NS) * L::kStageBytes; };
+      const uint64_t dQ0 = desc_kmajor(sbase + L::kOffQ), dDO0 = desc_kmajor(sbase + L::kOffDO);
       auto issue_sp = [&](int i) {
         const int bf = i & 1;
-        const uint32_t ka = stage(i), va = stage(i) + L::kKVBytes;
+        const uint64_t dk = desc_kmajor(stage(i)), dv = desc_kmajor(stage(i) + L::kKVBytes);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t offq = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
-          const uint32_t offk = (kk >> 2) * (kInner * 128) + (kk & 3) * 32;
-          mma_ss(tmem + L::kTmemS + 64 * bf, desc_kmajor(sbase + L::kOffQ + offq),
-                 desc_kmajor(ka + offk), idSP, kk > 0 ? 1u : 0u);
-          mma_ss(tmem + L::kTmemDP + 64 * bf, desc_kmajor(sbase + L::kOffDO + offq),
-                 desc_kmajor(va + offk), idSP, kk > 0 ? 1u : 0u);
+          const uint32_t offq = ((kk >> 2) * (kRows * 128) + (kk & 3) * 32) >> 4;
+          const uint32_t offk = ((kk >> 2) * (kInner * 128) + (kk & 3) * 32) >> 4;
+          mma_ss(tmem + L::kTmemS + 64 * bf, dQ0 + offq, dk + offk, idSP, kk > 0 ? 1u : 0u);
+          mma_ss(tmem + L::kTmemDP + 64 * bf, dDO0 + offq, dv + offk, idSP, kk > 0 ? 1u : 0u);
         }
         mma_commit(bar(kSPFull + bf));
       };
@@ -545,11 +535,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!(ok = mbar_wait(bar(kDSFull + bf), k & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
         tc_fence_after();
-        const uint32_t ka = stage(i);
+        const uint64_t mk = desc_mnmajor(stage(i), kInner * 128);
 #pragma unroll
         for (int kk = 0; kk < kInner / 16; ++kk) {
-          mma_ts(tmem + L::kTmemDQ, tmem + L::kTmemDP + 64 * bf + kk * 8,
-                 desc_mnmajor(ka + kk * 2048, kInner * 128), idAcc, (i > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(tmem + L::kTmemDQ, tmem + L::kTmemDP + 64 * bf + kk * 8, mk + ((kk * 2048) >> 4),
+                 idAcc, (i > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(bar(kKVEmpty + i % NS));
       }
@@ -588,44 +578,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tDb = tmem + lane_base + L::kTmemDP + 64 * bf;
       const bool full = tile_full(p, q0, q0 + kRows, j0, j0 + kInner);
       const float abase = ALIBI ? slope2 * (float)(gi - (int64_t)j0 - p.k_off) : 0.f;
+      int clo, chi;  // kept key columns [clo, chi) of this query row
+      keys_for_query(p, gi, qi < p.Sq, j0, kInner, &clo, &chi);
+      auto step = [&](auto masked) {
+        constexpr bool MASKED = decltype(masked)::value;
 #pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        uint32_t sr[32], dr[32];
-        tmem_ld32(tSb + 32 * half, sr);
-        tmem_ld32(tDb + 32 * half, dr);
-        tmem_ld_wait();
-        uint32_t dpk[16];
+        for (int half = 0; half < 2; ++half) {
+          uint32_t sr[32], dr[32];
+          tmem_ld32(tSb + 32 * half, sr);
+          tmem_ld32(tDb + 32 * half, dr);
+          tmem_ld_wait();
+          uint32_t dpk[16];
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          float ds2[2];
+          for (int c = 0; c < 32; c += 2) {
+            float ds2[2];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int cc = 32 * half + c + h;
-            const float raw = __uint_as_float(sr[c + h]);
-            float pr, t = 0.f;
-            if (CAP || ALIBI) {
-              float x = logit2<CAP>(raw, sl2, cap_in, cap_out, &t);
-              if (ALIBI) x = fmaf(-slope2, (float)cc, x + abase);
-              pr = ex2(x - lse2);
-            } else {
-              pr = ex2(fmaf(raw, sl2, -lse2));
+            for (int h = 0; h < 2; ++h) {
+              const int cc = 32 * half + c + h;
+              const float raw = __uint_as_float(sr[c + h]);
+              float pr, t = 0.f;
+              if (CAP || ALIBI) {
+                float x = logit2<CAP>(raw, sl2, cap_in, cap_out, &t);
+                if (ALIBI) x = fmaf(-slope2, (float)cc, x + abase);
+                pr = ex2(x - lse2);
+              } else {
+                pr = ex2(fmaf(raw, sl2, -lse2));
+              }
+              if (MASKED) pr = ((unsigned)(cc - clo) < (unsigned)(chi - clo)) ? pr : 0.f;
+              float ds = pr * (__uint_as_float(dr[c + h]) - dlt) * p.scale;
+              if (CAP) ds *= (1.f - t * t);
+              ds2[h] = ds;
             }
-            if (!full) {
-              const int kj = j0 + cc;
-              const bool keep = (qi < p.Sq) && (kj < p.Sk) &&
-                                keep_pair(gi, (int64_t)kj + p.k_off, p.causal, p.window);
-              pr = keep ? pr : 0.f;
-            }
-            float ds = pr * (__uint_as_float(dr[c + h]) - dlt) * p.scale;
-            if (CAP) ds *= (1.f - t * t);
-            ds2[h] = ds;
+            dpk[c / 2] = pack2<BF16>(ds2[0], ds2[1]);
           }
-          dpk[c / 2] = pack2<BF16>(ds2[0], ds2[1]);
+          // dS half h -> packed columns [16h, 16h + 16) of the dP buffer; the
+          // fp32 columns they overwrite were already read.
+          tmem_st16(tDb + 16 * half, dpk);
         }
-        // dS half h -> packed columns [16h, 16h + 16) of the dP buffer; the
-        // fp32 columns they overwrite were already read.
-        tmem_st16(tDb + 16 * half, dpk);
-      }
+      };
+      if (full) step(std::false_type{});
+      else step(std::true_type{});
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();

@@ -60,26 +60,6 @@ struct FwdLayout {
   static_assert(kSmemBytes <= 232448, "smem budget");
 };
 
-// Bounded wait by lane 0 of the warp, result shared with the whole warp so
-// that warp-collective tcgen05 instructions stay converged.
-__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const WaitCtl& ctl) {
-  int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, ctl, BFA_ERR_DEVICE_TIMEOUT) ? 1 : 0;
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  __syncwarp();
-  return ok != 0;
-}
-
-// Drain wait (ignores the abort flag, still bounded): used before exit so
-// that no async copy or MMA is in flight when the CTA retires.
-__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, uint64_t timeout_ns) {
-  if (mbar_try_wait(bar, parity)) return;
-  const uint64_t t0 = globaltimer();
-  while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer() - t0 > timeout_ns) return;
-  }
-}
-
 // True when every (row, key) pair of the tile is kept and inside Sk.
 __device__ __forceinline__ bool tile_full(const Params& p, int r0, int r1, int c0, int c1) {
   if (c1 > p.Sk) return false;
@@ -199,24 +179,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto kv_addr = [&](int idx) -> uint32_t {
         return sbase + L::kOffKV + (uint32_t)(idx % NS) * L::kKVBytes;
       };
+      // Descriptors are built once per tile; a K step only moves the start
+      // address (a compile-time offset added to the low field).
       auto issue_s = [&](int t, int idx) {
-        const uint32_t qa = sbase + L::kOffQ + t * L::kQBytes;
-        const uint32_t ka = kv_addr(idx);
+        const uint64_t dq = desc_kmajor(sbase + L::kOffQ + t * L::kQBytes);
+        const uint64_t dk = desc_kmajor(kv_addr(idx));
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t offq = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
           const uint32_t offk = (kk >> 2) * (kBN * 128) + (kk & 3) * 32;
-          mma_ss(tmem + L::kTmemS + t * kBN, desc_kmajor(qa + offq), desc_kmajor(ka + offk), idS,
+          mma_ss(tmem + L::kTmemS + t * kBN, dq + (offq >> 4), dk + (offk >> 4), idS,
                  kk > 0 ? 1u : 0u);
         }
         mma_commit(bar(kSFull + t));
       };
       auto issue_pv = [&](int t, int idx, bool acc) {
-        const uint32_t va = kv_addr(idx);
+        const uint64_t dv = desc_mnmajor(kv_addr(idx), kBN * 128);
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
           mma_ts(tmem + L::kTmemO + t * D, tmem + L::kTmemS + t * kBN + kk * 8,
-                 desc_mnmajor(va + kk * 16 * 128, kBN * 128), idO, (acc || kk > 0) ? 1u : 0u);
+                 dv + ((kk * 16 * 128) >> 4), idO, (acc || kk > 0) ? 1u : 0u);
         }
         mma_commit(bar(kODone + t));
       };
@@ -297,6 +279,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool full = tile_full(p, tr0, tr0 + kBM, c0, c0 + kBN);
       const bool store_x = CAP || ALIBI || !full || !(sl2 > 0.f);
       const float abase = ALIBI ? slope2 * (float)(gi - (int64_t)c0 - p.k_off) : 0.f;
+      int clo, chi;  // kept key columns [clo, chi) of this row (all of them on a full tile)
+      keys_for_query(p, gi, r_local < p.Sq, c0, kBN, &clo, &chi);
+      if (full) {
+        clo = 0;
+        chi = kBN;
+      }
       float mx;
       {
         float m4[4] = {neg_inf(), neg_inf(), neg_inf(), neg_inf()};
@@ -315,11 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float raw = __uint_as_float(r[e]);
               float x = CAP ? cap_out * tanh_exp(raw * cap_in) : raw * sl2;
               if (ALIBI) x = fmaf(-slope2, (float)c, x + abase);
-              if (!full) {
-                const int64_t gj = (int64_t)c0 + c + p.k_off;
-                const bool keep = (c0 + c < p.Sk) && keep_pair(gi, gj, p.causal, p.window);
-                x = keep ? x : neg_inf();
-              }
+              x = ((unsigned)(c - clo) < (unsigned)(chi - clo)) ? x : neg_inf();
               r[e] = __float_as_uint(x);
               m4[e & 3] = fmaxf(m4[e & 3], x);
             }

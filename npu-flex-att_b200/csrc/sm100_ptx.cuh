@@ -26,6 +26,8 @@
 
 #include <stdint.h>
 
+#include "bfa.h"
+
 namespace bfa {
 namespace sm100 {
 
@@ -71,6 +73,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes (or the hint, in ns, runs out) instead of spinning.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Shared abort state of one CTA: once any role gives up on a wait, every
 // other bounded wait in the CTA returns false at once.
 struct WaitCtl {
@@ -85,20 +101,41 @@ struct WaitCtl {
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtl& ctl,
                                           int code) {
   if (mbar_try_wait(bar, parity)) return true;
-  // Slow path: the abort flag and the clock are checked every 32 polls only
-  // (try_wait itself suspends the thread for a short while), which keeps a
-  // waiting thread from stealing issue slots from the warps doing the work.
+  // Slow path: sleep in try_wait (woken when the phase completes, at most
+  // kSleepNs per call) so a waiting thread takes no issue slots from the
+  // warps doing the work; check the abort flag and the clock between calls.
+  constexpr uint32_t kSleepNs = 1000000;  // 1 ms
   const uint64_t t0 = globaltimer();
-  for (uint32_t n = 1;; ++n) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((n & 31u) == 0) {
-      if (*ctl.abort) return false;
-      if (globaltimer() - t0 > ctl.timeout_ns) {
-        *ctl.abort = 1;
-        if (ctl.status) atomicExch(ctl.status, code);
-        return false;
-      }
+  while (true) {
+    if (mbar_try_wait_sleep(bar, parity, kSleepNs)) return true;
+    if (*ctl.abort) return false;
+    if (globaltimer() - t0 > ctl.timeout_ns) {
+      *ctl.abort = 1;
+      if (ctl.status) atomicExch(ctl.status, code);
+      return false;
     }
+  }
+}
+
+// Bounded wait for a whole warp. Fast path: every lane polls once and the
+// warp stays converged. Otherwise lane 0 runs the bounded wait and shares the
+// result, so warp-collective tcgen05 instructions that follow stay converged.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const WaitCtl& ctl) {
+  if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, ctl, BFA_ERR_DEVICE_TIMEOUT) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
+
+// Drain wait (ignores the abort flag, still bounded): used before exit so
+// that no async copy or MMA is in flight when the CTA retires.
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, uint64_t timeout_ns) {
+  if (mbar_try_wait(bar, parity)) return;
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait_sleep(bar, parity, 1000000)) {
+    if (globaltimer() - t0 > timeout_ns) return;
   }
 }
 
