@@ -58,6 +58,16 @@ def peaks():
         return 1590.0, 6650.0, "fallback"
 
 
+def committed_traffic(phase: str):
+    """DRAM bytes per launch of a kernel from the committed ncu capture, or None."""
+    kernel = {"fwd": "fwd_kernel", "dkdv": "dkdv_kernel", "dq": "dq_kernel"}.get(phase)
+    try:
+        with open(os.path.join(ROOT, "profiles", "c3_dram_traffic.json")) as f:
+            return json.load(f)["kernels"][kernel]["dram_bytes_per_launch"]
+    except Exception:
+        return None
+
+
 def dist_env():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -274,7 +284,10 @@ def run_ours(args):
     achieved = kern_flops[names[dom]] / (phase_ms[dom] * 1e-3) / 1e12
     roofline = {"bound": "tensor", "kernel": names[dom], "achieved": round(achieved, 2),
                 "peak": peak_tf, "unit": "TFLOP/s", "frac": round(achieved / peak_tf, 4),
-                "peak_kind": f"bf16 dense burst, {peak_kind}", "traffic": None,
+                "peak_kind": f"bf16 dense burst, {peak_kind}",
+                "traffic": committed_traffic(names[dom]),
+                "traffic_unit": "DRAM bytes per launch (ncu capture, profiles/c3_dram_traffic.json)",
+                "algorithmic_flop_per_launch": kern_flops[names[dom]],
                 "phase_ms": {n: round(x, 4) for n, x in zip(names, phase_ms)}}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
