@@ -45,7 +45,7 @@
 extern "C" {
 #endif
 
-#define BFA_ABI_VERSION 1
+#define BFA_ABI_VERSION 2
 
 typedef enum bfa_dtype {
   BFA_DTYPE_F32 = 0,
@@ -118,6 +118,10 @@ typedef struct bfa_bwd_args {
   uint32_t debug_flags;    /* 0 in production; BFA_DEBUG_* for tests */
   uint32_t phases;         /* 0 = all; else a mask of BFA_BWD_PHASE_* (same workspace
                               across the calls, Δ first) -- lets a caller time each kernel */
+  uint32_t accumulate;     /* 0: dq/dk/dv have the input dtype and are overwritten.
+                              1: dq/dk/dv are fp32 accumulators and the gradients are
+                              added to them (blockwise / context-parallel backward: no
+                              16-bit rounding of partial gradients) */
 } bfa_bwd_args;
 
 #define BFA_BWD_PHASE_DELTA 1u  /* Δ = rowsum(O∘dO) into the workspace */

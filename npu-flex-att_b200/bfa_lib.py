@@ -14,7 +14,7 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libbfa.so")
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 DEBUG_INJECT_STALL = 1
@@ -56,7 +56,7 @@ class BwdArgs(ctypes.Structure):
                 ("dout", Tensor), ("lse", ctypes.c_void_p), ("dq", Tensor),
                 ("dk", Tensor), ("dv", Tensor), ("status", ctypes.c_void_p),
                 ("wait_timeout_ns", ctypes.c_int64), ("debug_flags", ctypes.c_uint32),
-                ("phases", ctypes.c_uint32)]
+                ("phases", ctypes.c_uint32), ("accumulate", ctypes.c_uint32)]
 
 
 _lib = None

@@ -1,0 +1,358 @@
+"""Context-parallel attention: a K/V ring over ranks with LSE merging.
+
+The reference runs one sequence on one device. This module shards a long
+sequence across ranks (one process per GPU) and keeps each rank's kernels
+exactly the single-GPU ones (``bfa_fwd`` / ``bfa_bwd`` with absolute
+position offsets), so masks, ALiBi and the soft-cap see true positions.
+
+Layout (zigzag). The sequence of length S is cut into 2N chunks of C = S/(2N)
+rows; rank r holds chunks r and 2N-1-r of Q, K and V. Under a causal mask
+every rank then owns the same amount of work.
+
+Forward. At step t = 0..N-1 rank r holds the K/V shard of rank (r - t) mod N;
+for each of its two query chunks and each visiting key chunk that the mask
+does not hide entirely it runs one attention call and folds the partial
+(O, LSE) into fp32 accumulators with ``bfa_merge_partial``:
+    lse' = logaddexp(lse_acc, lse_p),  o' = o_acc e^(lse_acc-lse') + o_p e^(lse_p-lse').
+The next K/V shard is in flight (NCCL send/recv) while the current one is used.
+
+Backward. dK/dV accumulators travel with their K/V shard around the ring and
+arrive home after N hops; dQ stays local. Each visible block runs the single-
+GPU backward against the FINAL O and LSE (which is what makes the blockwise
+gradients exact) and adds its gradients into fp32 accumulators in place
+(``bfa_bwd_args.accumulate``), so partial gradients are never rounded to
+16 bits. Δ = rowsum(O∘dO) is computed once per query chunk.
+
+The ring algorithm is written as per-rank generators that yield their
+communication steps, so the same code runs over ``torch.distributed``
+(``run_dist``: NCCL on GPUs, gloo in CPU tests) and in one process over a list
+of simulated ranks (``run_simulated``).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+import bfa_lib as _bfa
+import npu_flash_attention as _nfa
+
+
+# ---------------------------------------------------------------- layout
+class ZigzagLayout:
+    """Chunks {r, 2N-1-r} of the sequence on rank r (N = world size)."""
+
+    def __init__(self, seqlen: int, world: int):
+        if world < 1 or seqlen % (2 * world) != 0:
+            raise ValueError(f"seqlen {seqlen} must be a multiple of 2*world ({2 * world})")
+        self.seqlen, self.world = seqlen, world
+        self.chunk = seqlen // (2 * world)
+
+    def chunks(self, rank: int) -> tuple[int, int]:
+        return rank, 2 * self.world - 1 - rank
+
+    def shard(self, x: torch.Tensor, rank: int, dim: int = 2) -> torch.Tensor:
+        """This rank's rows of a full-sequence tensor, contiguous."""
+        a, b = self.chunks(rank)
+        c = self.chunk
+        return torch.cat([x.narrow(dim, a * c, c), x.narrow(dim, b * c, c)], dim=dim).contiguous()
+
+    def unshard(self, shards: list[torch.Tensor], dim: int = 2) -> torch.Tensor:
+        """Inverse of ``shard`` over all ranks' shards."""
+        c = self.chunk
+        parts: list[Optional[torch.Tensor]] = [None] * (2 * self.world)
+        for r, s in enumerate(shards):
+            a, b = self.chunks(r)
+            parts[a] = s.narrow(dim, 0, c)
+            parts[b] = s.narrow(dim, c, c)
+        return torch.cat(parts, dim=dim)
+
+
+@dataclass
+class MaskArgs:
+    causal: bool = False
+    sliding_window: int = 0
+    alibi_slope: Optional[torch.Tensor] = None
+    scale: Optional[float] = None
+    soft_cap: float = 0.0
+
+
+def block_visible(qa: int, kb: int, chunk: int, m: MaskArgs) -> bool:
+    """False when the mask hides every (i, j) of query chunk qa x key chunk kb."""
+    q_lo, q_hi = qa * chunk, qa * chunk + chunk - 1
+    k_lo, k_hi = kb * chunk, kb * chunk + chunk - 1
+    if m.causal and k_lo > q_hi:
+        return False
+    if m.sliding_window > 0 and q_lo - k_hi > m.sliding_window:
+        return False
+    return True
+
+
+# ---------------------------------------------------------------- block ops (CUDA)
+class CudaBlockOps:
+    """One block of the ring on this rank's GPU through libbfa."""
+
+    def fwd(self, q, k, v, q_off, k_off, m: MaskArgs):
+        return _nfa.npu_flash_attention_forward(
+            q, k, v, causal=m.causal, sliding_window=m.sliding_window,
+            alibi_slope=m.alibi_slope, scale=m.scale, soft_cap=m.soft_cap,
+            return_lse=True, q_pos_offset=q_off, k_pos_offset=k_off)
+
+    def merge(self, o_acc, lse_acc, o_part, lse_part):
+        """In place: (o_acc, lse_acc) <- LSE merge with (o_part, lse_part)."""
+        B, H, S, D = o_acc.shape
+        lib = _bfa.load()
+        lse_p = lse_part.contiguous()
+        dev = o_acc.device
+        with torch.cuda.device(dev):
+            _bfa.check(lib.bfa_merge_partial(
+                B, H, S, D, _bfa.tensor(o_acc), _bfa.bfa_dtype(o_acc.dtype),
+                ctypes.c_void_p(lse_acc.data_ptr()), _bfa.tensor(o_part),
+                _bfa.bfa_dtype(o_part.dtype), ctypes.c_void_p(lse_p.data_ptr()),
+                ctypes.c_void_p(_bfa.stream_ptr(dev))))
+
+    def bwd_rows(self, q, k, o, do, lse, m: MaskArgs):
+        """Per-query-chunk state: Δ and the scaled LSE, computed once."""
+        lib = _bfa.load()
+        D = q.shape[-1]
+        scale = m.scale if m.scale is not None else 1.0 / math.sqrt(D)
+        pr = _nfa._problem(q, k, m.causal, m.sliding_window, None, scale, m.soft_cap)
+        ws = torch.empty(max(lib.bfa_bwd_workspace_bytes(pr), 1), dtype=torch.uint8,
+                         device=q.device)
+        # Δ reads only o, dout and lse; the gradient buffers are not touched.
+        z = torch.zeros(1, 1, 1, 1, device=q.device, dtype=torch.float32)
+        _nfa.npu_flash_attention_backward(
+            q, k, k, o, lse, do, causal=m.causal, sliding_window=m.sliding_window,
+            alibi_slope=m.alibi_slope, scale=m.scale, soft_cap=m.soft_cap,
+            _phases=_bfa.PHASE_DELTA, _workspace=ws, _outputs=(z, z, z))
+        return ws
+
+    def bwd_into(self, state, q, k, v, o, lse, do, q_off, k_off, m: MaskArgs,
+                 dq_acc, dk_acc, dv_acc):
+        """Add this block's dQ, dK, dV to the fp32 accumulators."""
+        _nfa.npu_flash_attention_backward(
+            q, k, v, o, lse, do, causal=m.causal, sliding_window=m.sliding_window,
+            alibi_slope=m.alibi_slope, scale=m.scale, soft_cap=m.soft_cap,
+            q_pos_offset=q_off, k_pos_offset=k_off,
+            _phases=_bfa.PHASE_DKDV | _bfa.PHASE_DQ, _workspace=state,
+            _outputs=(dq_acc, dk_acc, dv_acc), _accumulate=True)
+
+
+# ---------------------------------------------------------------- ring (per rank)
+def ring_forward(q, k, v, rank: int, world: int, m: MaskArgs, ops):
+    """Generator for one rank's forward. Yields ("start", kv) to post the send
+    of ``kv`` to rank+1 and the receive from rank-1, ("finish",) to complete
+    them (sent back: the received K/V). Returns (O, LSE) of this rank's rows.
+    """
+    S2 = q.shape[2]
+    C = S2 // 2
+    lay = ZigzagLayout(S2 * world, world)
+    my = lay.chunks(rank)
+    B, H, _, D = q.shape
+    o_acc = [torch.zeros(B, H, C, D, device=q.device, dtype=torch.float32) for _ in range(2)]
+    lse_acc = [torch.full((B, H, C), float("-inf"), device=q.device, dtype=torch.float32)
+               for _ in range(2)]
+    kv = (k, v)
+    for t in range(world):
+        src = (rank - t) % world
+        if t + 1 < world:
+            yield ("start", kv)
+        kc, vc = kv
+        for ia, qa in enumerate(my):
+            for ib, kb in enumerate(lay.chunks(src)):
+                if not block_visible(qa, kb, C, m):
+                    continue
+                o_p, lse_p = ops.fwd(q.narrow(2, ia * C, C), kc.narrow(2, ib * C, C),
+                                     vc.narrow(2, ib * C, C), qa * C, kb * C, m)
+                ops.merge(o_acc[ia], lse_acc[ia], o_p, lse_p)
+        if t + 1 < world:
+            kv = yield ("finish",)
+    return torch.cat(o_acc, dim=2).to(q.dtype), torch.cat(lse_acc, dim=2)
+
+
+def ring_backward(q, k, v, o, lse, do, rank: int, world: int, m: MaskArgs, ops):
+    """Generator for one rank's backward. K/V move as in the forward; the
+    fp32 dK/dV accumulators follow with ("swap", (dk, dv)) after every step,
+    so after N steps each rank holds the gradients of its own K/V shard.
+    Returns (dQ, dK, dV) in the input dtypes.
+    """
+    S2 = q.shape[2]
+    C = S2 // 2
+    lay = ZigzagLayout(S2 * world, world)
+    my = lay.chunks(rank)
+    dq_acc = torch.zeros(q.shape, device=q.device, dtype=torch.float32)
+    dkv = (torch.zeros(k.shape, device=k.device, dtype=torch.float32),
+           torch.zeros(v.shape, device=v.device, dtype=torch.float32))
+    rows = []
+    for ia in range(2):
+        sl = slice(ia * C, ia * C + C)
+        rows.append(ops.bwd_rows(q[:, :, sl], k, o[:, :, sl], do[:, :, sl],
+                                 lse[:, :, sl].contiguous(), m))
+    kv = (k, v)
+    for t in range(world):
+        src = (rank - t) % world
+        if t + 1 < world:
+            yield ("start", kv)
+        kc, vc = kv
+        dk_acc, dv_acc = dkv
+        for ia, qa in enumerate(my):
+            qs = slice(ia * C, ia * C + C)
+            for ib, kb in enumerate(lay.chunks(src)):
+                if not block_visible(qa, kb, C, m):
+                    continue
+                ks = slice(ib * C, ib * C + C)
+                ops.bwd_into(rows[ia], q[:, :, qs], kc[:, :, ks], vc[:, :, ks], o[:, :, qs],
+                             lse[:, :, qs].contiguous(), do[:, :, qs], qa * C, kb * C, m,
+                             dq_acc[:, :, qs], dk_acc[:, :, ks], dv_acc[:, :, ks])
+        if t + 1 < world:
+            kv = yield ("finish",)
+        if world > 1:
+            dkv = yield ("swap", dkv)
+    dk_acc, dv_acc = dkv
+    return dq_acc.to(q.dtype), dk_acc.to(k.dtype), dv_acc.to(v.dtype)
+
+
+# ---------------------------------------------------------------- drivers
+class DistRing:
+    """Ring transfers over torch.distributed point-to-point (NCCL or gloo)."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        self.dist, self.group = dist, group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self._pending = None
+
+    def _peer(self, r: int) -> int:
+        r %= self.world
+        return r if self.group is None else self.dist.get_global_rank(self.group, r)
+
+    def _post(self, payload):
+        dist = self.dist
+        recv = tuple(torch.empty_like(t) for t in payload)
+        ops = []
+        for t, rb in zip(payload, recv):
+            ops.append(dist.P2POp(dist.isend, t.contiguous(), self._peer(self.rank + 1), self.group))
+            ops.append(dist.P2POp(dist.irecv, rb, self._peer(self.rank - 1), self.group))
+        reqs = dist.batch_isend_irecv(ops)
+        # The send buffers stay referenced until the requests complete.
+        return reqs, recv, payload
+
+    def start(self, payload):
+        assert self._pending is None, "ring transfer already in flight"
+        self._pending = self._post(payload)
+
+    def finish(self):
+        reqs, recv, _ = self._pending
+        for r in reqs:
+            r.wait()
+        self._pending = None
+        return recv
+
+    def swap(self, payload):
+        reqs, recv, _ = self._post(payload)
+        for r in reqs:
+            r.wait()
+        return recv
+
+
+def run_dist(gen, group=None):
+    """Drive one rank's ring generator over torch.distributed."""
+    ring = DistRing(group)
+    try:
+        step = next(gen)
+        while True:
+            kind = step[0]
+            if kind == "start":
+                ring.start(step[1])
+                step = gen.send(None)
+            elif kind == "finish":
+                step = gen.send(ring.finish())
+            elif kind == "swap":
+                step = gen.send(ring.swap(step[1]))
+            else:
+                raise RuntimeError(f"unknown ring step {kind!r}")
+    except StopIteration as stop:
+        return stop.value
+
+
+def run_simulated(gens):
+    """Drive all ranks' generators in one process, in lockstep: every rank
+    yields the same step kinds in the same order; rank r receives what rank
+    r-1 sent."""
+    n = len(gens)
+    results = [None] * n
+    steps = [None] * n
+    done = 0
+    for r, g in enumerate(gens):
+        try:
+            steps[r] = next(g)
+        except StopIteration as stop:  # a ring of one rank never communicates
+            results[r] = stop.value
+            done += 1
+    if done == n:
+        return results
+    if done:
+        raise RuntimeError("ranks finished at different steps")
+    inflight = None
+    while True:
+        kinds = {s[0] for s in steps}
+        if len(kinds) != 1:
+            raise RuntimeError(f"ranks out of step: {kinds}")
+        kind = kinds.pop()
+        if kind == "start":
+            inflight = [s[1] for s in steps]
+            sends = [None] * n
+        elif kind == "finish":
+            sends = [inflight[(r - 1) % n] for r in range(n)]
+            inflight = None
+        elif kind == "swap":
+            sends = [steps[(r - 1) % n][1] for r in range(n)]
+        else:
+            raise RuntimeError(f"unknown ring step {kind!r}")
+        done = 0
+        for r, g in enumerate(gens):
+            try:
+                steps[r] = g.send(sends[r])
+            except StopIteration as stop:
+                results[r] = stop.value
+                done += 1
+        if done == n:
+            return results
+        if done:
+            raise RuntimeError("ranks finished at different steps")
+
+
+# ---------------------------------------------------------------- public API
+class RingFlexAttention(torch.autograd.Function):
+    """Autograd over the ring: inputs and outputs are this rank's zigzag shard."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, causal, sliding_window, alibi_slope, scale, soft_cap, group):
+        import torch.distributed as dist
+        m = MaskArgs(causal, int(sliding_window), alibi_slope, scale, float(soft_cap))
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        o, lse = run_dist(ring_forward(q, k, v, rank, world, m, CudaBlockOps()), group)
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.m, ctx.group, ctx.rank, ctx.world = m, group, rank, world
+        return o
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        q, k, v, o, lse = ctx.saved_tensors
+        do = grad_out.to(q.dtype).contiguous()
+        dq, dk, dv = run_dist(ring_backward(q, k, v, o, lse, do, ctx.rank, ctx.world, ctx.m,
+                                            CudaBlockOps()), ctx.group)
+        return dq, dk, dv, None, None, None, None, None, None
+
+
+def context_parallel_attention(q, k, v, causal=False, sliding_window=0, alibi_slope=None,
+                               scale=None, soft_cap=0.0, group=None):
+    """Attention over a sequence sharded across the ranks of ``group`` in the
+    zigzag layout (``ZigzagLayout.shard``): q [B, Hq, 2C, D], k/v [B, Hkv, 2C, D]
+    on this rank's GPU. Returns this rank's rows of O; differentiable."""
+    return RingFlexAttention.apply(q, k, v, causal, sliding_window, alibi_slope, scale,
+                                   soft_cap, group)

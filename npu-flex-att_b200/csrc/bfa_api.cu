@@ -136,6 +136,8 @@ static int fill_bwd(const bfa_problem* pr, const bfa_bwd_args* a, Params* p) {
   p->debug_flags = a->debug_flags;
   p->phases = a->phases ? a->phases
                         : (BFA_BWD_PHASE_DELTA | BFA_BWD_PHASE_DKDV | BFA_BWD_PHASE_DQ);
+  if (a->accumulate > 1) return BFA_ERR_INVALID_ARGUMENT;
+  p->grad_acc = a->accumulate;
   return BFA_OK;
 }
 

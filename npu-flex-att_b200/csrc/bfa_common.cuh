@@ -42,6 +42,7 @@ struct Params {
   uint64_t timeout_ns;
   uint32_t debug_flags;
   uint32_t phases;  // backward: mask of BFA_BWD_PHASE_* (never 0 here)
+  uint32_t grad_acc;  // backward: dq/dk/dv are fp32 accumulators (add, don't store)
 };
 
 template <typename T> __device__ __forceinline__ float to_f32(T x);

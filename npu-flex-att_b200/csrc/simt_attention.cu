@@ -198,11 +198,14 @@ __global__ void __launch_bounds__(NT) simt_bwd_dq_kernel(Params p) {
     }
   }
   if (r < rows) {
-    T* DQ = (T*)p.dq + (int64_t)b * p.sdq_[0] + (int64_t)hq * p.sdq_[1] + (int64_t)(r0 + r) * p.sdq_[2];
+    const int64_t base = (int64_t)b * p.sdq_[0] + (int64_t)hq * p.sdq_[1] + (int64_t)(r0 + r) * p.sdq_[2];
 #pragma unroll
     for (int e = 0; e < DP / 4; ++e) {
       const int d = c + 4 * e;
-      if (d < p.D) DQ[(int64_t)d * p.sdq_[3]] = from_f32<T>(acc[e]);
+      if (d >= p.D) continue;
+      const int64_t at = base + (int64_t)d * p.sdq_[3];
+      if (p.grad_acc) ((float*)p.dq)[at] += acc[e];
+      else ((T*)p.dq)[at] = from_f32<T>(acc[e]);
     }
   }
 }
@@ -282,14 +285,19 @@ __global__ void __launch_bounds__(NT) simt_bwd_dkdv_kernel(Params p) {
     }
   }
   if (r < cols) {
-    T* DK = (T*)p.dk + (int64_t)b * p.sdk_[0] + (int64_t)hkv * p.sdk_[1] + (int64_t)(c0 + r) * p.sdk_[2];
-    T* DV = (T*)p.dv + (int64_t)b * p.sdv_[0] + (int64_t)hkv * p.sdv_[1] + (int64_t)(c0 + r) * p.sdv_[2];
+    const int64_t bk = (int64_t)b * p.sdk_[0] + (int64_t)hkv * p.sdk_[1] + (int64_t)(c0 + r) * p.sdk_[2];
+    const int64_t bv = (int64_t)b * p.sdv_[0] + (int64_t)hkv * p.sdv_[1] + (int64_t)(c0 + r) * p.sdv_[2];
 #pragma unroll
     for (int e = 0; e < DP / 4; ++e) {
       const int d = c + 4 * e;
-      if (d < p.D) {
-        DK[(int64_t)d * p.sdk_[3]] = from_f32<T>(adk[e]);
-        DV[(int64_t)d * p.sdv_[3]] = from_f32<T>(adv[e]);
+      if (d >= p.D) continue;
+      const int64_t ak = bk + (int64_t)d * p.sdk_[3], av = bv + (int64_t)d * p.sdv_[3];
+      if (p.grad_acc) {
+        ((float*)p.dk)[ak] += adk[e];
+        ((float*)p.dv)[av] += adv[e];
+      } else {
+        ((T*)p.dk)[ak] = from_f32<T>(adk[e]);
+        ((T*)p.dv)[av] = from_f32<T>(adv[e]);
       }
     }
   }

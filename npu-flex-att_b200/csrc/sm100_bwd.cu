@@ -21,6 +21,8 @@
 // issuer, warp 2 TMEM allocator, warps 4-7 elementwise (one row per thread).
 // S/dP are double-buffered in TMEM so the MMAs of step i+1 overlap the
 // elementwise work of step i.
+// Accumulate mode (Params::grad_acc): dq/dk/dv are fp32 and the epilogues
+// TMA reduce-add their fp32 tiles into them instead of storing 16-bit tiles.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -94,6 +96,22 @@ __device__ __forceinline__ void stage_tmem_row(uint32_t taddr, uint8_t* stage, i
   }
 }
 
+// Accumulate mode: the same row in fp32, D/32 swizzled sub-tiles of 128 rows
+// x 32 floats, for a TMA reduce-add into the caller's fp32 gradient.
+template <int D>
+__device__ __forceinline__ void stage_tmem_row_f32(uint32_t taddr, uint8_t* stage, int row) {
+#pragma unroll 1
+  for (int c = 0; c < D / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld32(taddr + 32 * c, r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      *reinterpret_cast<uint4*>(stage + c * (kRows * 128) + sw128_offset(row, q)) =
+          make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+  }
+}
+
 // ============================================================== dK / dV
 // TMEM: Sᵀ(b) at 64·b, dPᵀ(b) at 128 + 64·b (b = step parity, fp32, 64
 // columns each); the elementwise warps overwrite the first 32 columns of each
@@ -116,6 +134,7 @@ struct DkdvLayout {
   static_assert(kTmemDK + D <= 512, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "smem budget");
   static_assert((2 * kQBytes) % 1024 == 0, "stage alignment");
+  static_assert(kStages * kStageBytes >= 2u * kRows * D * 4, "fp32 dK/dV staging");
 };
 
 template <int D, bool BF16, bool CAP, bool ALIBI>
@@ -365,20 +384,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (good && n_iter > 0) good = warp_wait(bar(kAccDone), 0, ctl);
       good = good && !*abort_flag;
       // K and V tiles are free once every MMA is done: they stage dK and dV.
-      uint8_t* stage_dk = smem + L::kOffK;
-      uint8_t* stage_dv = smem + L::kOffV;
-      if (good) {
+      // In accumulate mode the fp32 tiles (2 x 128 x D x 4 bytes) go to the
+      // Q/dO stages instead, which are free too; a key tile no query sees
+      // adds nothing and skips the epilogue.
+      const bool acc = p.grad_acc != 0;
+      uint8_t* stage_dk = acc ? smem + L::kOffStage + kRows * D * 4 : smem + L::kOffK;
+      uint8_t* stage_dv = acc ? smem + L::kOffStage : smem + L::kOffV;
+      if (good && !(acc && n_iter == 0)) {
         tc_fence_after();
-        stage_tmem_row<D, BF16>(tmem + lane_base + L::kTmemDV, stage_dv, row, n_iter == 0);
-        stage_tmem_row<D, BF16>(tmem + lane_base + L::kTmemDK, stage_dk, row, n_iter == 0);
+        if (acc) {
+          stage_tmem_row_f32<D>(tmem + lane_base + L::kTmemDV, stage_dv, row);
+          stage_tmem_row_f32<D>(tmem + lane_base + L::kTmemDK, stage_dk, row);
+        } else {
+          stage_tmem_row<D, BF16>(tmem + lane_base + L::kTmemDV, stage_dv, row, n_iter == 0);
+          stage_tmem_row<D, BF16>(tmem + lane_base + L::kTmemDK, stage_dk, row, n_iter == 0);
+        }
         fence_async_shared();
       }
       if (lane == 0) warp_ok[wq] = good ? 1 : 0;
       named_sync(1, 128);
       if (wq == 0 && lane == 0 && warp_ok[0] && warp_ok[1] && warp_ok[2] && warp_ok[3]) {
-        for (int s = 0; s < L::kSub; ++s) {
-          tma_store_4d(&tmDV, smem_u32(stage_dv) + s * (kRows * 128), s * 64, c0, hkv, b);
-          tma_store_4d(&tmDK, smem_u32(stage_dk) + s * (kRows * 128), s * 64, c0, hkv, b);
+        if (!acc) {
+          for (int s = 0; s < L::kSub; ++s) {
+            tma_store_4d(&tmDV, smem_u32(stage_dv) + s * (kRows * 128), s * 64, c0, hkv, b);
+            tma_store_4d(&tmDK, smem_u32(stage_dk) + s * (kRows * 128), s * 64, c0, hkv, b);
+          }
+        } else if (n_iter > 0) {
+          for (int s = 0; s < D / 32; ++s) {
+            tma_reduce_add_4d(&tmDV, smem_u32(stage_dv) + s * (kRows * 128), s * 32, c0, hkv, b);
+            tma_reduce_add_4d(&tmDK, smem_u32(stage_dk) + s * (kRows * 128), s * 32, c0, hkv, b);
+          }
         }
         tma_store_commit();
         tma_store_wait_all();
@@ -412,6 +447,7 @@ struct DqLayout {
   static constexpr uint32_t kTmemS = 0, kTmemDP = 128, kTmemDQ = 256;
   static_assert(kTmemDQ + D <= 512, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "smem budget");
+  static_assert(kOffDO == kOffQ + kQBytes && 2 * kQBytes >= kRows * D * 4, "fp32 dQ staging");
 };
 
 template <int D, bool BF16, bool CAP, bool ALIBI>
@@ -627,17 +663,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool good = ok;
       if (good && n_iter > 0) good = warp_wait(bar(kAccDone), 0, ctl);
       good = good && !*abort_flag;
-      uint8_t* stage_dq = smem + L::kOffQ;  // Q's tile is free once every MMA is done
-      if (good) {
+      // Q's tile (and dO's after it, for the fp32 tile of accumulate mode)
+      // is free once every MMA is done.
+      uint8_t* stage_dq = smem + L::kOffQ;
+      const bool acc = p.grad_acc != 0;
+      if (good && !(acc && n_iter == 0)) {
         tc_fence_after();
-        stage_tmem_row<D, BF16>(tmem + lane_base + L::kTmemDQ, stage_dq, row, n_iter == 0);
+        if (acc) stage_tmem_row_f32<D>(tmem + lane_base + L::kTmemDQ, stage_dq, row);
+        else stage_tmem_row<D, BF16>(tmem + lane_base + L::kTmemDQ, stage_dq, row, n_iter == 0);
         fence_async_shared();
       }
       if (lane == 0) warp_ok[wq] = good ? 1 : 0;
       named_sync(1, 128);
       if (wq == 0 && lane == 0 && warp_ok[0] && warp_ok[1] && warp_ok[2] && warp_ok[3]) {
-        for (int s = 0; s < L::kSub; ++s)
-          tma_store_4d(&tmDQ, smem_u32(stage_dq) + s * (kRows * 128), s * 64, q0, hq, b);
+        if (!acc) {
+          for (int s = 0; s < L::kSub; ++s)
+            tma_store_4d(&tmDQ, smem_u32(stage_dq) + s * (kRows * 128), s * 64, q0, hq, b);
+        } else if (n_iter > 0) {
+          for (int s = 0; s < D / 32; ++s)
+            tma_reduce_add_4d(&tmDQ, smem_u32(stage_dq) + s * (kRows * 128), s * 32, q0, hq, b);
+        }
         tma_store_commit();
         tma_store_wait_all();
       }
@@ -660,6 +705,7 @@ bool set_smem(K kern, uint32_t bytes) {
 
 template <int D, bool BF16, bool CAP, bool ALIBI>
 int launch_bwd(const Params& p, int dtype, cudaStream_t st) {
+  const int gdt = p.grad_acc ? BFA_DTYPE_F32 : dtype;  // dtype of dq/dk/dv
   if (p.phases & BFA_BWD_PHASE_DKDV) {
     using L = DkdvLayout<D>;
     auto kern = dkdv_kernel<D, BF16, CAP, ALIBI>;
@@ -672,8 +718,8 @@ int launch_bwd(const Params& p, int dtype, cudaStream_t st) {
         !make_tmap_bhsd(&m[1], p.v, dtype, D, p.Sk, p.Hkv, p.B, p.sv_, kRows) ||
         !make_tmap_bhsd(&m[2], p.q, dtype, D, p.Sq, p.Hq, p.B, p.sq_, kInner) ||
         !make_tmap_bhsd(&m[3], p.dout, dtype, D, p.Sq, p.Hq, p.B, p.sdo_, kInner) ||
-        !make_tmap_bhsd(&m[4], p.dk, dtype, D, p.Sk, p.Hkv, p.B, p.sdk_, kRows) ||
-        !make_tmap_bhsd(&m[5], p.dv, dtype, D, p.Sk, p.Hkv, p.B, p.sdv_, kRows))
+        !make_tmap_bhsd(&m[4], p.dk, gdt, D, p.Sk, p.Hkv, p.B, p.sdk_, kRows) ||
+        !make_tmap_bhsd(&m[5], p.dv, gdt, D, p.Sk, p.Hkv, p.B, p.sdv_, kRows))
       return BFA_ERR_CUDA;
     const unsigned grid = (unsigned)((p.Sk + kRows - 1) / kRows) * p.Hkv * p.B;
     kern<<<grid, kThreads, L::kSmemBytes, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], p);
@@ -692,7 +738,7 @@ int launch_bwd(const Params& p, int dtype, cudaStream_t st) {
         !make_tmap_bhsd(&m[1], p.dout, dtype, D, p.Sq, p.Hq, p.B, p.sdo_, kRows) ||
         !make_tmap_bhsd(&m[2], p.k, dtype, D, p.Sk, p.Hkv, p.B, p.sk_, kInner) ||
         !make_tmap_bhsd(&m[3], p.v, dtype, D, p.Sk, p.Hkv, p.B, p.sv_, kInner) ||
-        !make_tmap_bhsd(&m[4], p.dq, dtype, D, p.Sq, p.Hq, p.B, p.sdq_, kRows))
+        !make_tmap_bhsd(&m[4], p.dq, gdt, D, p.Sq, p.Hq, p.B, p.sdq_, kRows))
       return BFA_ERR_CUDA;
     const unsigned grid = (unsigned)((p.Sq + kRows - 1) / kRows) * p.Hq * p.B;
     kern<<<grid, kThreads, L::kSmemBytes, st>>>(m[0], m[1], m[2], m[3], m[4], p);
@@ -718,10 +764,11 @@ bool sm100_bwd_eligible(const Params& p, int dtype) {
   if (p.D != 64 && p.D != 128) return false;
   if (p.Sq < 1 || p.Sk < 1 || p.B < 1 || p.Hq < 1) return false;
   if (!device_is_sm100()) return false;
+  const int ges = p.grad_acc ? 4 : 2;
   return tma_layout_ok(p.q, p.sq_, 2) && tma_layout_ok(p.k, p.sk_, 2) &&
          tma_layout_ok(p.v, p.sv_, 2) && tma_layout_ok(p.dout, p.sdo_, 2) &&
-         tma_layout_ok(p.dq, p.sdq_, 2) && tma_layout_ok(p.dk, p.sdk_, 2) &&
-         tma_layout_ok(p.dv, p.sdv_, 2);
+         tma_layout_ok(p.dq, p.sdq_, ges) && tma_layout_ok(p.dk, p.sdk_, ges) &&
+         tma_layout_ok(p.dv, p.sdv_, ges);
 }
 
 int sm100_bwd(const Params& p, int dtype, cudaStream_t st) {

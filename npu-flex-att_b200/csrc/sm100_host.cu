@@ -69,14 +69,15 @@ bool make_tmap_bhsd(CUtensorMap* map, const void* ptr, int dtype, int D, int S, 
                     const int64_t* stride, int box_rows) {
   EncodeFn fn = encode_fn();
   if (!fn) return false;
-  const int es = 2;
+  const int es = dtype == BFA_DTYPE_F32 ? 4 : 2;
   cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
   cuuint64_t gstr[3] = {(cuuint64_t)(stride[2] * es), (cuuint64_t)(stride[1] * es),
                         (cuuint64_t)(stride[0] * es)};
-  cuuint32_t box[4] = {64u, (cuuint32_t)box_rows, 1u, 1u};
+  cuuint32_t box[4] = {(cuuint32_t)(128 / es), (cuuint32_t)box_rows, 1u, 1u};
   cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
-  const CUtensorMapDataType dt = dtype == BFA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUtensorMapDataType dt = dtype == BFA_DTYPE_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == BFA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const CUresult r = fn(map, dt, 4, const_cast<void*>(ptr), dims, gstr, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);

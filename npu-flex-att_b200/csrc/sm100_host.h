@@ -17,8 +17,9 @@ bool device_is_sm100();
 // TMA: unit innermost stride, 16-byte aligned base and outer strides.
 bool tma_layout_ok(const void* ptr, const int64_t* stride, int elem_bytes);
 
-// 4-D tensor map over a [B, H, S, D] 16-bit tensor: box = 64 elements of D
-// (128 bytes, 128-byte swizzle) x `box_rows` rows of S x 1 x 1. Rows past S
+// 4-D tensor map over a [B, H, S, D] tensor (fp16/bf16, or fp32 for the
+// backward's accumulate mode): box = 128 bytes of D (64 16-bit or 32 fp32
+// elements, 128-byte swizzle) x `box_rows` rows of S x 1 x 1. Rows past S
 // read as zero and are not written. Returns false if the driver rejects it.
 bool make_tmap_bhsd(CUtensorMap* map, const void* ptr, int dtype, int D, int S, int H, int B,
                     const int64_t* stride, int box_rows);

@@ -173,6 +173,18 @@ __device__ __forceinline__ void tma_store_4d(const void* tmap, uint32_t src, int
       : "memory");
 }
 
+// Element-wise add of a shared-memory tile into global memory (fp32 here):
+// the reduction happens in L2, so CTAs adding into the same tile need no
+// other synchronisation. Completes with the store bulk-group.
+__device__ __forceinline__ void tma_reduce_add_4d(const void* tmap, uint32_t src, int c0, int c1,
+                                                  int c2, int c3) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4, %5}], "
+      "[%1];" ::"l"(tmap),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_store_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }

@@ -175,12 +175,16 @@ def npu_flash_attention_backward(
     _phases=0,
     _workspace=None,
     _outputs=None,
+    _accumulate=False,
 ):
     """Attention backward: (dQ, dK, dV), dK/dV summed over each GQA group.
 
     ``_phases`` / ``_workspace`` / ``_outputs`` (internal) let a benchmark
     launch Δ, dK/dV and dQ as separate calls on one workspace and reuse the
     gradient buffers, so each kernel can be timed on its own.
+    ``_accumulate`` (internal) adds the gradients into ``_outputs``, which must
+    then be fp32: a blockwise (context-parallel) backward sums its partial
+    gradients without rounding each one to 16 bits.
 
     Mirrors npu_flash_attention.py:659-739; Δ, both gradient kernels and the
     GQA reduction run on the device in one library call.
@@ -200,6 +204,10 @@ def npu_flash_attention_backward(
     lse_c = lse.to(torch.float32).contiguous()
     if _outputs is not None:
         DQ, DK, DV = _outputs
+        if _accumulate and not all(t.dtype == torch.float32 for t in _outputs):
+            raise ValueError("_accumulate needs fp32 gradient buffers")
+    elif _accumulate:
+        raise ValueError("_accumulate needs _outputs")
     else:
         DQ = torch.empty_like(query)
         DK = torch.empty(B, Hkv, Sk, D, device=dev, dtype=key.dtype)
@@ -216,6 +224,7 @@ def npu_flash_attention_backward(
     args.wait_timeout_ns = int(_wait_timeout_ns)
     args.debug_flags = int(_debug_flags)
     args.phases = int(_phases)
+    args.accumulate = 1 if _accumulate else 0
     ws_bytes = lib.bfa_bwd_workspace_bytes(pr)
     ws = _workspace if _workspace is not None else torch.empty(
         max(ws_bytes, 1), dtype=torch.uint8, device=dev)

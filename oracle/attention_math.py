@@ -148,7 +148,8 @@ def attention_forward(q, k, v, *, causal=False, sliding_window=0,
 def attention_backward(q, k, v, grad_out, *, causal=False, sliding_window=0,
                        alibi_slope=None, scale=None, soft_cap=0.0,
                        q_offset=0, k_offset=0, alibi_in_backward=True,
-                       out=None, lse=None, dtype=torch.float64):
+                       out=None, lse=None, dtype=torch.float64,
+                       operand_dtype=None):
     """Backward oracle: returns ``(dQ, dK, dV)`` with dK/dV per KV head.
 
     Restates npu_flash_attention.py:659-739 and the two kernels :298-560.
@@ -156,6 +157,11 @@ def attention_backward(q, k, v, grad_out, *, causal=False, sliding_window=0,
     ``rowsum(out∘grad_out)`` (:685). With ``alibi_in_backward=False`` the
     probabilities are recomputed without the ALiBi bias against the given
     ``lse``, exactly as the reference kernels do.
+
+    ``operand_dtype`` (fp16/bf16) rounds P and dS to that type before they
+    enter the dV, dK and dQ products, as the reference kernels do
+    (``p.to(v.dtype)`` :506/:545, ``ds.to(k.dtype)`` :516/:555,
+    ``ds.to(q.dtype)`` :399); the products themselves stay in ``dtype``.
     """
     d = q.shape[-1]
     if scale is None:
@@ -188,6 +194,9 @@ def attention_backward(q, k, v, grad_out, *, causal=False, sliding_window=0,
     if t is not None:
         ds = ds * (1.0 - t * t)
     ds = ds * scale
+    if operand_dtype is not None:
+        p = p.to(operand_dtype).to(dtype)
+        ds = ds.to(operand_dtype).to(dtype)
     dq = torch.matmul(ds, kx)
     dk_h = torch.matmul(ds.transpose(-2, -1), qf)
     dv_h = torch.matmul(p.transpose(-2, -1), dof)
@@ -195,6 +204,18 @@ def attention_backward(q, k, v, grad_out, *, causal=False, sliding_window=0,
     dk = dk_h.view(b, hkv, g, sk, d).sum(2)
     dv = dv_h.view(b, hkv, g, sk, d).sum(2)
     return dq, dk, dv
+
+
+def reference_backward(q, k, v, grad_out, *, dtype=torch.float64, **mask):
+    """Gradients of the operator as a caller sees it: the forward's output is
+    rounded to the input dtype before Δ = rowsum(O∘dO) is formed, as the
+    autograd wrapper saves the stored ``out`` (npu_flash_attention.py:760, :772-777),
+    and P / dS enter the gradient products in the input dtype (16-bit inputs).
+    """
+    o, lse = attention_forward(q, k, v, dtype=dtype, **mask)
+    op = q.dtype if q.dtype in (torch.float16, torch.bfloat16) else None
+    return attention_backward(q, k, v, grad_out, out=o.to(q.dtype), lse=lse,
+                              dtype=dtype, operand_dtype=op, **mask)
 
 
 def attention_forward_reference_tiles(q, k, v, *, causal=False, sliding_window=0,

@@ -51,9 +51,9 @@ def test_injected_stall_in_backward_kernels():
                                      _debug_flags=bfa_lib.DEBUG_INJECT_STALL)
     torch.cuda.synchronize()
     assert bfa_lib.read_and_clear_status(torch.device(DEV)) == bfa_lib.ERR_DEVICE_TIMEOUT
-    from oracle.attention_math import attention_backward
+    from oracle.attention_math import reference_backward
     dq, dk, dv = nfa.npu_flash_attention_backward(qd, kd, vd, o, lse, god, causal=True)
-    rq, rk, rv = attention_backward(q, k, v, go, causal=True)
+    rq, rk, rv = reference_backward(q, k, v, go, causal=True)
     for a, r in ((dq, rq), (dk, rk), (dv, rv)):
         assert ((a.cpu().double() - r).abs() / (1 + r.abs())).max().item() < 2e-2
     nfa.check_device_status(DEV)

@@ -98,3 +98,28 @@ def test_oracle_backward_is_autograd_of_forward():
     dq, dk, dv = attention_backward(q, k, v, go, **kw)
     for a, b_ in ((dq, qr.grad), (dk, kr.grad), (dv, vr.grad)):
         assert (a - b_).abs().max().item() < 1e-10
+
+
+FP16_BWD = [c for c in CASES if "dq" in c[1] and _dtype_class(c[0]) == "fp16"
+            and "ref_bwd_ignores_alibi" not in c[0]["flags"]]
+
+
+@pytest.mark.parametrize("meta,rec", FP16_BWD, ids=[m["name"] for m, _ in FP16_BWD])
+def test_operand_casts_restate_reference_kernels(meta, rec):
+    """With P and dS rounded to fp16 before the gradient products (as the
+    reference kernels round them) the oracle lands closer to the reference's
+    own fp16 gradients than the all-fp64 oracle does."""
+    kw = _kwargs(meta, rec)
+    args = (rec["q"], rec["k"], rec["v"], rec["grad_out"])
+    plain = attention_backward(*args, out=rec["o"], lse=rec["lse"], **kw)
+    cast = attention_backward(*args, out=rec["o"], lse=rec["lse"],
+                              operand_dtype=torch.float16, **kw)
+    for name, a, c in zip(("dq", "dk", "dv"), plain, cast):
+        r = rec[name].double()
+        rel_plain = ((a - r).abs() / (1 + r.abs())).max().item()
+        rel_cast = ((c - r).abs() / (1 + r.abs())).max().item()
+        rms_plain = (a - r).pow(2).mean().sqrt().item()
+        rms_cast = (c - r).pow(2).mean().sqrt().item()
+        assert rel_cast <= rel_plain + 1e-9, (name, rel_cast, rel_plain)
+        assert rms_cast <= rms_plain + 1e-9, (name, rms_cast, rms_plain)
+        assert rel_cast < 1e-3, (name, rel_cast)

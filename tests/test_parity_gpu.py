@@ -12,7 +12,7 @@ import torch
 
 import npu_flash_attention as nfa
 from golden_cases import load_cases
-from oracle.attention_math import attention_backward, attention_forward
+from oracle.attention_math import attention_backward, attention_forward, reference_backward
 
 pytestmark = pytest.mark.gpu
 
@@ -73,7 +73,15 @@ def check_case(q, k, v, go, *, tol=None, bwd=True, **kw):
     if not bwd:
         return
     dq, dk, dv = nfa.npu_flash_attention_backward(qd, kd, vd, o, lse, god, **kw_dev)
-    dq_r, dk_r, dv_r = attention_backward(q, k, v, go, **kw)
+    # The backward is checked as the operator it is: a function of
+    # (q, k, v, out, lse, dout), given the same out the kernels got and the
+    # exact LSE, with P and dS rounded to the input dtype before the gradient
+    # products as the reference kernels round them. (The exact LSE rather than
+    # the kernel's fp32 one: at logits near 1e4 an fp32 ulp of the LSE is
+    # 1e-3, which the fp64 logits here would not share.)
+    op_dt = dtype if dtype in (torch.float16, torch.bfloat16) else None
+    dq_r, dk_r, dv_r = attention_backward(q, k, v, go, out=o.cpu(), lse=lse_ref,
+                                          operand_dtype=op_dt, **kw)
     assert dq.shape == q.shape and dk.shape == k.shape and dv.shape == v.shape
     for name, a, r in (("dq", dq, dq_r), ("dk", dk, dk_r), ("dv", dv, dv_r)):
         e = _err(a, r)
@@ -230,7 +238,7 @@ def test_autograd_through_flex_attention():
     out = nfa.flex_attention(qd, kd, vd, config=cfg)
     out.backward(go.to(DEV))
     o_r, _ = attention_forward(q, k, v, causal=True, sliding_window=64, soft_cap=30.0)
-    dq, dk, dv = attention_backward(q, k, v, go, causal=True, sliding_window=64, soft_cap=30.0)
+    dq, dk, dv = reference_backward(q, k, v, go, causal=True, sliding_window=64, soft_cap=30.0)
     assert _err(out, o_r) < 2e-2
     assert _err(qd.grad, dq) < 2e-2 and _err(kd.grad, dk) < 2e-2 and _err(vd.grad, dv) < 2e-2
 
