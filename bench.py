@@ -5,7 +5,8 @@ Llama-3-8B-style GQA layer, B=4 per GPU, Hq=32, Hkv=8, D=128, S=4096, causal,
 scale 1/sqrt(128); q, k, v, grad_out ~ N(0,1) seeded, synthetic.
 
 One step = one forward + one backward of that layer through the library's
-C ABI (bfa_fwd, then Δ, dK/dV, dQ). FLOPs count only unmasked (i, j) pairs,
+C ABI (bfa_fwd, then Δ, dK/dV, dQ as three calls on one workspace so each
+kernel is timed on its own). FLOPs count only unmasked (i, j) pairs,
 element-exact: 4·D per pair forward, 10·D backward.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
@@ -203,11 +204,12 @@ def run_ours(args):
     import npu_flash_attention as nfa
 
     rank, world, local = dist_env()
-    if world > 1:
-        import datetime
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=dev)
     lib = bfa_lib.load()
     q, k, v, do = make_inputs(1234 + rank, dev)
     B, Hq, Hkv, S, D = CFG["B"], CFG["Hq"], CFG["Hkv"], CFG["S"], CFG["D"]
@@ -274,7 +276,7 @@ def run_ours(args):
     value = world * flops / (ms_step * 1e-3) / 1e12
 
     # ---- e2e: public autograd API, host (pinned) buffers, copies inside the timed region
-    e2e = run_e2e(nfa, dev, args, world)
+    e2e = None if args.profile else run_e2e(nfa, dev, args, world)
 
     peak_tf, _, peak_kind = peaks()
     pairs = causal_pairs(S) * B * Hq
@@ -290,7 +292,7 @@ def run_ours(args):
                 "algorithmic_flop_per_launch": kern_flops[names[dom]],
                 "phase_ms": {n: round(x, 4) for n, x in zip(names, phase_ms)}}
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.profile):
         tf, threads, n = cpu_baseline_sample(budget_s=args.cpu_budget)
         cpu = {"value": round(tf, 6), "unit": "TFLOPS", "cores": threads, "kind": "port",
                "sample": f"{n} whole (b, q-head) slices of the workload (S=4096, D=128, causal, "
@@ -368,6 +370,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="for ncu: only the warm-up and timed steps (no e2e, no CPU baseline)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

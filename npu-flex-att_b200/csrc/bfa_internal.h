@@ -18,6 +18,11 @@ bool sm100_fwd_eligible(const Params& p, int dtype);
 int sm100_fwd(const Params& p, int dtype, cudaStream_t st);
 bool sm100_bwd_eligible(const Params& p, int dtype);
 int sm100_bwd(const Params& p, int dtype, cudaStream_t st);
+// One-kernel backward (sm100_bwd_fused.cu): `order` holds one counter per
+// 64-row query tile (B·Hq·Sq_pad/64), `dq_acc` an fp32 [B, Hq, Sq, D]
+// buffer (unused in accumulate mode).
+bool sm100_bwd_fused_eligible(const Params& p, int dtype);
+int sm100_bwd_fused(const Params& p, int dtype, uint32_t* order, float* dq_acc, cudaStream_t st);
 
 // Partial-result merge (merge.cu).
 int launch_merge(int B, int H, int S, int D, const bfa_tensor& oa, int adt, float* lse_a,
