@@ -16,11 +16,12 @@
 //   MMAs (M = 128 keys): Sᵀ = K Qᵢᵀ, dPᵀ = V dOᵢᵀ (N = 64), then
 //   dV += Pᵀ dOᵢ and dK += dSᵀ Qᵢ (N = D, B operand MN-major).
 // dq_kernel: one CTA per (batch, q-head, 128-row query tile); loops over
-//   64-key tiles: S = Q Kⱼᵀ, dP = dO Vⱼᵀ, dQ += dS Kⱼ.
+//   128-key tiles: S = Q Kⱼᵀ, dP = dO Vⱼᵀ (Q, dO held in TMEM), dQ += dS Kⱼ.
 // Warp roles in both: warp 0 TMA producer (+ LSE/Δ staging), warp 1 MMA
-// issuer, warp 2 TMEM allocator, warps 4-7 elementwise (one row per thread).
-// S/dP are double-buffered in TMEM so the MMAs of step i+1 overlap the
-// elementwise work of step i.
+// issuer, warp 2 TMEM allocator, warps 4-11 elementwise: two warpgroups, one
+// row per thread, each taking half of every step's 64 columns. S/dP are
+// double-buffered in TMEM so the MMAs of step i+1 overlap the elementwise
+// work of step i.
 // Accumulate mode (Params::grad_acc): dq/dk/dv are fp32 and the epilogues
 // TMA reduce-add their fp32 tiles into them instead of storing 16-bit tiles.
 #include <cuda.h>
@@ -42,9 +43,9 @@ using namespace bwd;
 
 // ============================================================== dK / dV
 // TMEM: Sᵀ(b) at 64·b, dPᵀ(b) at 128 + 64·b (b = step parity, fp32, 64
-// columns each); the elementwise warps overwrite the first 32 columns of each
-// with Pᵀ / dSᵀ (16-bit, two per column), the A operands of the dV / dK MMAs.
-// dV at 256, dK at 256 + D.
+// columns each); the elementwise warps overwrite columns [0, 16) and
+// [32, 48) of each with Pᵀ / dSᵀ (16-bit, two per column; query columns 0-31
+// and 32-63), the A operands of the dV / dK MMAs. dV at 256, dK at 256 + D.
 template <int D>
 struct DkdvLayout {
   static constexpr int kSub = D / 64;
@@ -110,7 +111,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; ++i)
-      mbar_init(bar(i), (i >= kDSFull && i < kDSFull + 2) ? 4u : 1u);
+      mbar_init(bar(i), (i >= kDSFull && i < kDSFull + 2) ? 8u : 1u);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -205,9 +206,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < kInner / 16; ++kk) {
           const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-          mma_ts(tmem + L::kTmemDV, tmem + L::kTmemS + 64 * bf + kk * 8, mdo + ((kk * 2048) >> 4),
+          mma_ts(tmem + L::kTmemDV, tmem + L::kTmemS + 64 * bf + 32 * (kk >> 1) + 8 * (kk & 1), mdo + ((kk * 2048) >> 4),
                  idAcc, acc);
-          mma_ts(tmem + L::kTmemDK, tmem + L::kTmemDP + 64 * bf + kk * 8, mq + ((kk * 2048) >> 4),
+          mma_ts(tmem + L::kTmemDK, tmem + L::kTmemDP + 64 * bf + 32 * (kk >> 1) + 8 * (kk & 1), mq + ((kk * 2048) >> 4),
                  idAcc, acc);
         }
         mma_commit(bar(kQEmpty + i % NS));
@@ -218,9 +219,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ elementwise
-    // Two warpgroups take alternate steps (step parity = TMEM buffer), so the
-    // exp / scale work of consecutive steps overlaps. Each thread owns one key
-    // row (TMEM lane) and walks the 64 query columns in two halves of 32.
+    // Both warpgroups work on every step: warpgroup h takes query columns
+    // [32h, 32h + 32) of it, so a step's elementwise latency is that of 32
+    // columns. Each thread owns one key row (TMEM lane).
     const int eg = (warp - 4) >> 2;
     const int wq = warp & 3;
     const int row = wq * 32 + lane;  // key row within the tile
@@ -231,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float cap_in = CAP ? p.scale / p.soft_cap : 0.f;
     const float cap_out = CAP ? p.soft_cap * kLog2e : 0.f;
     bool ok = true;
-    for (int i = eg; i < n_iter; i += 2) {
+    for (int i = 0; i < n_iter; ++i) {
       const int bf = i & 1, k = i >> 1, st = i % NS;
       const int hq = hkv * p.G + i / n_qt;
       const int q0 = (qt0 + i % n_qt) * kInner;
@@ -256,8 +257,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // inside the unrolled column loop.
       auto step = [&](auto masked) {
         constexpr bool MASKED = decltype(masked)::value;
-#pragma unroll 1
-        for (int half = 0; half < 2; ++half) {
+        {
+          const int half = eg;
           uint32_t sr[32], dr[32];
           tmem_ld32(tSb + 32 * half, sr);
           tmem_ld32(tDb + 32 * half, dr);
@@ -293,10 +294,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             dpk[c / 2] = pack2<BF16>(ds4[0], ds4[1]);
             dpk[c / 2 + 1] = pack2<BF16>(ds4[2], ds4[3]);
           }
-          // Pᵀ / dSᵀ half h -> packed columns [16h, 16h + 16) of the buffer; the
-          // fp32 columns they overwrite were read above (half 1 reads 32..63).
-          tmem_st16(tSb + 16 * half, ppk);
-          tmem_st16(tDb + 16 * half, dpk);
+          // Pᵀ / dSᵀ of half h -> packed columns [32h, 32h + 16) of the
+          // buffer: inside this half's own fp32 columns, read above.
+          tmem_st16(tSb + 32 * half, ppk);
+          tmem_st16(tDb + 32 * half, dpk);
         }
       };
       if (full) step(std::false_type{});
@@ -358,23 +359,44 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ============================================================== dQ
-// TMEM: S(b) at 64·b, dP(b) at 128 + 64·b; dS (16-bit) overwrites the first
-// 32 columns of dP(b) and is the A operand of dQ += dS·K. dQ at 256.
+// One CTA per (batch, q-head, 128-row query tile) loops over 128-key tiles:
+//   S = Q Kⱼᵀ, dP = dO Vⱼᵀ, dS (elementwise), dQ += dS Kⱼ.
+// Every MMA has N = 128: on B200 a tcgen05.mma with N = 64 costs about 1.4x
+// its nominal time (a fixed per-instruction cost), with N >= 128 it runs at
+// the nominal rate.
+// TMEM: S at 0 and dP at 128 (128 fp32 columns each), dQ at 256, Q and dO at
+// 256 + D and 256 + 3D/2 (16-bit, two per column). Q and dO are the A
+// operands of S and dP and constant for the CTA, so they are moved into TMEM
+// once and those MMAs read only K / V from shared memory. dS (16-bit)
+// overwrites dP in place: warpgroup h's keys [64h, 64h + 64) pack into
+// columns [128 + 64h, 128 + 64h + 32), the A operand of dQ += dS·K.
+// Per step i the MMA warp issues S(i+1) as soon as the elementwise warps have
+// read S(i) into registers, then dQ(i) once dS(i) is in TMEM, then dP(i+1),
+// which overwrites dS(i) after dQ(i) has read it (one thread's MMAs run in
+// order). The elementwise work of step i overlaps S(i+1).
+// Shared memory: Q, dO, then K/V stages; once Q and dO are in TMEM their
+// tile is the last K/V stage.
 template <int D>
 struct DqLayout {
+  static constexpr int kKeys = 128;  // keys per step
   static constexpr int kSub = D / 64;
-  static constexpr int kStages = (D <= 64) ? 10 : 5;
-  static constexpr uint32_t kQBytes = kRows * D * 2;     // Q or dO tile (128 rows)
-  static constexpr uint32_t kKVBytes = kInner * D * 2;   // K or V tile (64 keys)
+  static constexpr uint32_t kQBytes = kRows * D * 2;    // Q or dO tile (128 rows)
+  static constexpr uint32_t kKVBytes = kKeys * D * 2;   // K or V tile (128 keys)
+  static constexpr uint32_t kStageBytes = 2 * kKVBytes;
+  static constexpr int kStages = (D <= 64) ? 5 : 3;     // the last one is the Q/dO tile
   static constexpr uint32_t kOffQ = 0;
   static constexpr uint32_t kOffDO = kOffQ + kQBytes;
   static constexpr uint32_t kOffStage = kOffDO + kQBytes;
-  static constexpr uint32_t kStageBytes = 2 * kKVBytes;
-  static constexpr uint32_t kOffBar = kOffStage + kStages * kStageBytes;
+  static constexpr uint32_t kOffBar = kOffStage + (kStages - 1) * kStageBytes;
   static constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
   static constexpr uint32_t kTmemS = 0, kTmemDP = 128, kTmemDQ = 256;
-  static_assert(kTmemDQ + D <= 512, "TMEM budget");
+  static constexpr uint32_t kTmemQ = kTmemDQ + D, kTmemDO = kTmemQ + D / 2;
+  static __host__ __device__ constexpr uint32_t stage_off(int st) {
+    return st < kStages - 1 ? kOffStage + st * kStageBytes : kOffQ;
+  }
+  static_assert(kTmemDO + D / 2 <= 512, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "smem budget");
+  static_assert(2 * kQBytes == kStageBytes, "the Q/dO tile doubles as a K/V stage");
   static_assert(kOffDO == kOffQ + kQBytes && 2 * kQBytes >= kRows * D * 4, "fp32 dQ staging");
 };
 
@@ -385,13 +407,16 @@ __global__ void __launch_bounds__(kThreads, 1)
               const __grid_constant__ CUtensorMap tmDQ, const Params p) {
   using L = DqLayout<D>;
   constexpr int NS = L::kStages;
+  constexpr int NK = L::kKeys;
   enum {
     kQFull = 0,
     kKVFull = 1,
     kKVEmpty = 1 + NS,
-    kSPFull = 1 + 2 * NS,
-    kDSFull = kSPFull + 2,
-    kAccDone = kDSFull + 2,
+    kSPFull = 1 + 2 * NS,  // MMA -> elementwise: S(i) and dP(i) are in TMEM
+    kSRead = kSPFull + 1,  // elementwise -> MMA: S(i) is in registers (8 warps)
+    kDSFull = kSRead + 1,  // elementwise -> MMA: dS(i) is in TMEM (8 warps)
+    kOpsReady = kDSFull + 1,  // Q and dO are in TMEM (8 warps)
+    kAccDone = kOpsReady + 1,
     kDrain = kAccDone + 1,
     kNever = kDrain + 1,
     kNumBars = kNever + 1
@@ -415,14 +440,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int q0 = qt * kRows;
   int klo, khi;
   key_range(p, q0, min(q0 + kRows, p.Sq), &klo, &khi);
-  const int jt0 = klo / kInner;
-  const int n_iter = (khi > klo) ? (khi + kInner - 1) / kInner - jt0 : 0;
+  const int jt0 = klo / NK;
+  const int n_iter = (khi > klo) ? (khi + NK - 1) / NK - jt0 : 0;
 
   WaitCtl ctl{abort_flag, p.status, p.timeout_ns};
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; ++i)
-      mbar_init(bar(i), (i >= kDSFull && i < kDSFull + 2) ? 4u : 1u);
+      mbar_init(bar(i), (i >= kSRead && i <= kOpsReady) ? 8u : 1u);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -447,15 +472,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       int n = 0;
-      for (int i = 0; i < n_iter; ++i) {
+      bool ok = true;
+      for (int i = 0; i < n_iter && ok; ++i) {
         const int st = i % NS;
-        if (i >= NS && !mbar_wait(bar(kKVEmpty + st), ((i / NS) & 1) ^ 1, ctl, BFA_ERR_DEVICE_TIMEOUT)) break;
-        const int j0 = (jt0 + i) * kInner;
-        const uint32_t ks = sbase + L::kOffStage + st * L::kStageBytes;
+        if (i >= NS) ok = mbar_wait(bar(kKVEmpty + st), ((i / NS) & 1) ^ 1, ctl, BFA_ERR_DEVICE_TIMEOUT);
+        else if (st == NS - 1) ok = mbar_wait(bar(kOpsReady), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
+        if (!ok) break;
+        const int j0 = (jt0 + i) * NK;
+        const uint32_t ks = sbase + L::stage_off(st);
         mbar_arrive_expect_tx(bar(kKVFull + st), L::kStageBytes);
         for (int s = 0; s < L::kSub; ++s) {
-          tma_load_4d(ks + s * (kInner * 128), &tmK, bar(kKVFull + st), s * 64, j0, hkv, b);
-          tma_load_4d(ks + L::kKVBytes + s * (kInner * 128), &tmV, bar(kKVFull + st), s * 64, j0, hkv, b);
+          tma_load_4d(ks + s * (NK * 128), &tmK, bar(kKVFull + st), s * 64, j0, hkv, b);
+          tma_load_4d(ks + L::kKVBytes + s * (NK * 128), &tmV, bar(kKVFull + st), s * 64, j0, hkv, b);
         }
         n = i + 1;
       }
@@ -465,55 +493,61 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idSP = idesc_f16(kRows, kInner, BF16, false);
+      constexpr uint32_t idSP = idesc_f16(kRows, NK, BF16, false);
       constexpr uint32_t idAcc = idesc_f16(kRows, D, BF16, true);
-      auto stage = [&](int i) -> uint32_t { return sbase + L::kOffStage + (i % NS) * L::kStageBytes; };
-      const uint64_t dQ0 = desc_kmajor(sbase + L::kOffQ), dDO0 = desc_kmajor(sbase + L::kOffDO);
-      auto issue_sp = [&](int i) {
-        const int bf = i & 1;
-        const uint64_t dk = desc_kmajor(stage(i)), dv = desc_kmajor(stage(i) + L::kKVBytes);
+      auto stage = [&](int i) -> uint32_t { return sbase + L::stage_off(i % NS); };
+      auto issue_s = [&](int i) {
+        const uint64_t dk = desc_kmajor(stage(i));
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t offq = ((kk >> 2) * (kRows * 128) + (kk & 3) * 32) >> 4;
-          const uint32_t offk = ((kk >> 2) * (kInner * 128) + (kk & 3) * 32) >> 4;
-          mma_ss(tmem + L::kTmemS + 64 * bf, dQ0 + offq, dk + offk, idSP, kk > 0 ? 1u : 0u);
-          mma_ss(tmem + L::kTmemDP + 64 * bf, dDO0 + offq, dv + offk, idSP, kk > 0 ? 1u : 0u);
+          const uint32_t offk = ((kk >> 2) * (NK * 128) + (kk & 3) * 32) >> 4;
+          mma_ts(tmem + L::kTmemS, tmem + L::kTmemQ + 8 * kk, dk + offk, idSP, kk > 0 ? 1u : 0u);
         }
-        mma_commit(bar(kSPFull + bf));
       };
-      bool ok = n_iter == 0 || mbar_wait(bar(kQFull), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
+      auto issue_dp = [&](int i) {
+        const uint64_t dv = desc_kmajor(stage(i) + L::kKVBytes);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t offk = ((kk >> 2) * (NK * 128) + (kk & 3) * 32) >> 4;
+          mma_ts(tmem + L::kTmemDP, tmem + L::kTmemDO + 8 * kk, dv + offk, idSP, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(bar(kSPFull));
+      };
+      bool ok = n_iter == 0 || mbar_wait(bar(kOpsReady), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
       if (ok && n_iter > 0) {
         ok = mbar_wait(bar(kKVFull), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
         if (ok) {
           tc_fence_after();
-          issue_sp(0);
+          issue_s(0);
+          issue_dp(0);
         }
       }
       for (int i = 0; i < n_iter && ok; ++i) {
-        const int bf = i & 1, k = i >> 1;
-        if (i + 1 < n_iter) {
-          const int n1 = i + 1;
+        const int n1 = i + 1;
+        if (n1 < n_iter) {
           if (!(ok = mbar_wait(bar(kKVFull + n1 % NS), (n1 / NS) & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
+          if (!(ok = mbar_wait(bar(kSRead), i & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
           tc_fence_after();
-          issue_sp(n1);
+          issue_s(n1);
         }
-        if (!(ok = mbar_wait(bar(kDSFull + bf), k & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
+        if (!(ok = mbar_wait(bar(kDSFull), i & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
         tc_fence_after();
-        const uint64_t mk = desc_mnmajor(stage(i), kInner * 128);
+        const uint64_t mk = desc_mnmajor(stage(i), NK * 128);
 #pragma unroll
-        for (int kk = 0; kk < kInner / 16; ++kk) {
-          mma_ts(tmem + L::kTmemDQ, tmem + L::kTmemDP + 64 * bf + kk * 8, mk + ((kk * 2048) >> 4),
-                 idAcc, (i > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < NK / 16; ++kk) {
+          mma_ts(tmem + L::kTmemDQ, tmem + L::kTmemDP + 64 * (kk >> 2) + 8 * (kk & 3),
+                 mk + ((kk * 2048) >> 4), idAcc, (i > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(bar(kKVEmpty + i % NS));
+        if (n1 < n_iter) issue_dp(n1);
       }
       mma_commit(bar(kAccDone));
       mma_commit(bar(kDrain));
       drain_wait(bar(kDrain), 0, p.timeout_ns);
     }
   } else if (warp >= 4) {
-    // Two warpgroups take alternate steps (step parity = TMEM buffer); each
-    // thread owns one query row and walks the 64 key columns in two halves.
+    // Both warpgroups work on every step: warpgroup h takes key columns
+    // [64h, 64h + 64) of it. Each thread owns one query row.
     const int eg = (warp - 4) >> 2;
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
@@ -528,28 +562,57 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float lse2 = p.lse2[ridx];
     const float dlt = p.delta[ridx];
     bool ok = true;
-    for (int i = eg; i < n_iter; i += 2) {
-      const int bf = i & 1, k = i >> 1;
-      const int j0 = (jt0 + i) * kInner;
-      uint32_t wbar = bar(kSPFull + bf), wpar = (uint32_t)(k & 1);
+    // Warpgroup 0 moves this thread's Q row, warpgroup 1 its dO row, from the
+    // swizzled shared tile into TMEM (lane = row, two elements per column).
+    if (n_iter > 0) {
+      ok = warp_wait(bar(kQFull), 0, ctl);
+      if (ok) {
+        const uint8_t* tile = smem + (eg == 0 ? L::kOffQ : L::kOffDO);
+        const uint32_t tcol = tmem + lane_base + (eg == 0 ? L::kTmemQ : L::kTmemDO);
+#pragma unroll 1
+        for (int s = 0; s < L::kSub; ++s) {
+          uint32_t r[32];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const uint4 w = *reinterpret_cast<const uint4*>(tile + s * (kRows * 128) + sw128_offset(row, c));
+            r[4 * c] = w.x; r[4 * c + 1] = w.y; r[4 * c + 2] = w.z; r[4 * c + 3] = w.w;
+          }
+          tmem_st32(tcol + 32 * s, r);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(kOpsReady));
+      }
+    }
+    for (int i = 0; i < n_iter && ok; ++i) {
+      const int j0 = (jt0 + i) * NK;
+      uint32_t wbar = bar(kSPFull), wpar = (uint32_t)(i & 1);
       if ((p.debug_flags & BFA_DEBUG_INJECT_STALL) && i == 0) {
         wbar = bar(kNever);
         wpar = 0;
       }
       if (!(ok = warp_wait(wbar, wpar, ctl))) break;
       tc_fence_after();
-      const uint32_t tSb = tmem + lane_base + L::kTmemS + 64 * bf;
-      const uint32_t tDb = tmem + lane_base + L::kTmemDP + 64 * bf;
-      const bool full = tile_full(p, q0, q0 + kRows, j0, j0 + kInner);
+      const uint32_t tSb = tmem + lane_base + L::kTmemS + 64 * eg;
+      const uint32_t tDb = tmem + lane_base + L::kTmemDP + 64 * eg;
+      // This warpgroup's 64 S columns into registers; S(i+1) may then start.
+      uint32_t sr[64];
+      tmem_ld32(tSb, *reinterpret_cast<uint32_t(*)[32]>(sr));
+      tmem_ld32(tSb + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kSRead));
+      const bool full = tile_full(p, q0, q0 + kRows, j0, j0 + NK);
       const float abase = ALIBI ? slope2 * (float)(gi - (int64_t)j0 - p.k_off) : 0.f;
       int clo, chi;  // kept key columns [clo, chi) of this query row
-      keys_for_query(p, gi, qi < p.Sq, j0, kInner, &clo, &chi);
+      keys_for_query(p, gi, qi < p.Sq, j0, NK, &clo, &chi);
       auto step = [&](auto masked) {
         constexpr bool MASKED = decltype(masked)::value;
-#pragma unroll 1
+#pragma unroll
         for (int half = 0; half < 2; ++half) {
-          uint32_t sr[32], dr[32];
-          tmem_ld32(tSb + 32 * half, sr);
+          uint32_t dr[32];
           tmem_ld32(tDb + 32 * half, dr);
           tmem_ld_wait();
           uint32_t dpk[16];
@@ -558,8 +621,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             float ds2[2];
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const int cc = 32 * half + c + h;
-              const float raw = __uint_as_float(sr[c + h]);
+              const int cc = 64 * eg + 32 * half + c + h;
+              const float raw = __uint_as_float(sr[32 * half + c + h]);
               float pr, t = 0.f;
               if (CAP || ALIBI) {
                 float x = logit2<CAP>(raw, sl2, cap_in, cap_out, &t);
@@ -575,8 +638,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             dpk[c / 2] = pack2<BF16>(ds2[0], ds2[1]);
           }
-          // dS half h -> packed columns [16h, 16h + 16) of the dP buffer; the
-          // fp32 columns they overwrite were already read.
+          // dS of this 32-key half -> packed columns [16·half, 16·half + 16)
+          // of this warpgroup's dP columns (all read by then: half 0 wrote
+          // over its own, half 1 writes over half 0's).
           tmem_st16(tDb + 16 * half, dpk);
         }
       };
@@ -585,7 +649,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kDSFull + bf));
+      if (lane == 0) mbar_arrive(bar(kDSFull));
     }
     if (eg == 0) {
       bool good = ok;
@@ -664,8 +728,8 @@ int launch_bwd(const Params& p, int dtype, cudaStream_t st) {
     CUtensorMap m[5];
     if (!make_tmap_bhsd(&m[0], p.q, dtype, D, p.Sq, p.Hq, p.B, p.sq_, kRows) ||
         !make_tmap_bhsd(&m[1], p.dout, dtype, D, p.Sq, p.Hq, p.B, p.sdo_, kRows) ||
-        !make_tmap_bhsd(&m[2], p.k, dtype, D, p.Sk, p.Hkv, p.B, p.sk_, kInner) ||
-        !make_tmap_bhsd(&m[3], p.v, dtype, D, p.Sk, p.Hkv, p.B, p.sv_, kInner) ||
+        !make_tmap_bhsd(&m[2], p.k, dtype, D, p.Sk, p.Hkv, p.B, p.sk_, L::kKeys) ||
+        !make_tmap_bhsd(&m[3], p.v, dtype, D, p.Sk, p.Hkv, p.B, p.sv_, L::kKeys) ||
         !make_tmap_bhsd(&m[4], p.dq, gdt, D, p.Sq, p.Hq, p.B, p.sdq_, kRows))
       return BFA_ERR_CUDA;
     const unsigned grid = (unsigned)((p.Sq + kRows - 1) / kRows) * p.Hq * p.B;
