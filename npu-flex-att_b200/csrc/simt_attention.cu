@@ -337,6 +337,54 @@ __global__ void __launch_bounds__(256) delta_kernel(Params p) {
   }
 }
 
+// Δ for 16-bit rows with unit inner stride and 16-byte aligned rows: G = D/8
+// threads per row, each loading 8 elements of O and dO with one 16-byte load
+// apiece (the kernel is HBM-bound: 4·D bytes read per row), reduced with
+// shuffles inside the group. Same outputs as delta_kernel.
+template <typename T, int G>
+__global__ void __launch_bounds__(256) delta_vec_kernel(Params p) {
+  const int64_t row = (int64_t)blockIdx.x * (256 / G) + (threadIdx.x / G);
+  const int g = threadIdx.x % G;
+  const int64_t nrows = (int64_t)p.B * p.Hq * p.Sq_pad;
+  if (row >= nrows) return;  // whole groups leave together (256 is a multiple of G)
+  const int i = (int)(row % p.Sq_pad);
+  const int hq = (int)((row / p.Sq_pad) % p.Hq);
+  const int b = (int)(row / ((int64_t)p.Sq_pad * p.Hq));
+  float acc = 0.f;
+  if (i < p.Sq) {
+    const T* O = (const T*)p.o + (int64_t)b * p.so_[0] + (int64_t)hq * p.so_[1] + (int64_t)i * p.so_[2];
+    const T* DO = (const T*)p.dout + (int64_t)b * p.sdo_[0] + (int64_t)hq * p.sdo_[1] + (int64_t)i * p.sdo_[2];
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(O) + g);
+    const uint4 c = __ldg(reinterpret_cast<const uint4*>(DO) + g);
+    const T* ae = reinterpret_cast<const T*>(&a);
+    const T* ce = reinterpret_cast<const T*>(&c);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc = fmaf(to_f32<T>(ae[e]), to_f32<T>(ce[e]), acc);
+  }
+#pragma unroll
+  for (int off = G / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (g == 0) {
+    p.delta[row] = acc;
+    if (p.lse2) {
+      float l2 = __int_as_float(0x7f800000);
+      if (i < p.Sq) {
+        const float lse = p.lse[((int64_t)b * p.Hq + hq) * p.Sq + i];
+        if (lse != neg_inf()) l2 = lse * kLog2e;
+      }
+      p.lse2[row] = l2;
+    }
+  }
+}
+
+// Rows of a [B, H, S, D] 16-bit tensor start on 16-byte boundaries and are
+// contiguous in D.
+static bool rows_vec_ok(const void* ptr, const int64_t* st, int D) {
+  if (((uintptr_t)ptr & 15u) != 0 || st[3] != 1 || (D % 8) != 0) return false;
+  for (int k = 0; k < 3; ++k)
+    if ((st[k] * 2) % 16 != 0) return false;
+  return true;
+}
+
 template <typename T, int DP>
 int launch_fwd_t(const Params& p, cudaStream_t st) {
   const size_t smem = (size_t)(TM + 2 * TN) * (DP + 1) * 4 + (size_t)TM * (TN + 1) * 4;
@@ -418,6 +466,21 @@ int simt_bwd(const Params& p, int dtype, cudaStream_t st) {
 int launch_delta(const Params& p, int dtype, cudaStream_t st) {
   const int64_t rows = (int64_t)p.B * p.Hq * p.Sq_pad;
   if (rows == 0) return BFA_OK;
+  if ((dtype == BFA_DTYPE_BF16 || dtype == BFA_DTYPE_F16) && (p.D == 64 || p.D == 128) &&
+      rows_vec_ok(p.o, p.so_, p.D) && rows_vec_ok(p.dout, p.sdo_, p.D)) {
+    const int G = p.D / 8, per_block = 256 / G;
+    const unsigned vblocks = (unsigned)((rows + per_block - 1) / per_block);
+    const bool bf = dtype == BFA_DTYPE_BF16;
+    if (G == 16) {
+      if (bf) delta_vec_kernel<__nv_bfloat16, 16><<<vblocks, 256, 0, st>>>(p);
+      else delta_vec_kernel<__half, 16><<<vblocks, 256, 0, st>>>(p);
+    } else {
+      if (bf) delta_vec_kernel<__nv_bfloat16, 8><<<vblocks, 256, 0, st>>>(p);
+      else delta_vec_kernel<__half, 8><<<vblocks, 256, 0, st>>>(p);
+    }
+    note_launch();
+    return cudaGetLastError() == cudaSuccess ? BFA_OK : BFA_ERR_CUDA;
+  }
   const unsigned blocks = (unsigned)((rows + 7) / 8);
   switch (dtype) {
     case BFA_DTYPE_F32: delta_kernel<float><<<blocks, 256, 0, st>>>(p); break;

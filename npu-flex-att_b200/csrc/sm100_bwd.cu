@@ -367,15 +367,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 // TMEM: S at 0 and dP at 128 (128 fp32 columns each), dQ at 256, Q and dO at
 // 256 + D and 256 + 3D/2 (16-bit, two per column). Q and dO are the A
 // operands of S and dP and constant for the CTA, so they are moved into TMEM
-// once and those MMAs read only K / V from shared memory. dS (16-bit)
-// overwrites dP in place: warpgroup h's keys [64h, 64h + 64) pack into
-// columns [128 + 64h, 128 + 64h + 32), the A operand of dQ += dS·K.
-// Per step i the MMA warp issues S(i+1) as soon as the elementwise warps have
-// read S(i) into registers, then dQ(i) once dS(i) is in TMEM, then dP(i+1),
-// which overwrites dS(i) after dQ(i) has read it (one thread's MMAs run in
-// order). The elementwise work of step i overlaps S(i+1).
-// Shared memory: Q, dO, then K/V stages; once Q and dO are in TMEM their
-// tile is the last K/V stage.
+// once and those MMAs read only K / V from shared memory. dS (16-bit) goes to
+// a 128-byte-swizzled shared tile [128 rows][128 keys], the A operand of
+// dQ += dS·K.
+// The elementwise warps release S(i) as soon as it is in registers and dP(i)
+// as soon as its second half is, so the MMA warp issues S(i+1) and dP(i+1)
+// while they compute dS(i); dQ(i) follows once dS(i) is in shared memory.
+// Shared memory: Q, dO, then K/V stages, then the dS tile; once Q and dO are
+// in TMEM their tile is the last K/V stage.
 template <int D>
 struct DqLayout {
   static constexpr int kKeys = 128;  // keys per step
@@ -384,10 +383,12 @@ struct DqLayout {
   static constexpr uint32_t kKVBytes = kKeys * D * 2;   // K or V tile (128 keys)
   static constexpr uint32_t kStageBytes = 2 * kKVBytes;
   static constexpr int kStages = (D <= 64) ? 5 : 3;     // the last one is the Q/dO tile
+  static constexpr uint32_t kDSBytes = kRows * kKeys * 2;  // dS [128 rows][128 keys]
   static constexpr uint32_t kOffQ = 0;
   static constexpr uint32_t kOffDO = kOffQ + kQBytes;
   static constexpr uint32_t kOffStage = kOffDO + kQBytes;
-  static constexpr uint32_t kOffBar = kOffStage + (kStages - 1) * kStageBytes;
+  static constexpr uint32_t kOffDS = kOffStage + (kStages - 1) * kStageBytes;
+  static constexpr uint32_t kOffBar = kOffDS + kDSBytes;
   static constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
   static constexpr uint32_t kTmemS = 0, kTmemDP = 128, kTmemDQ = 256;
   static constexpr uint32_t kTmemQ = kTmemDQ + D, kTmemDO = kTmemQ + D / 2;
@@ -414,9 +415,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     kKVEmpty = 1 + NS,
     kSPFull = 1 + 2 * NS,  // MMA -> elementwise: S(i) and dP(i) are in TMEM
     kSRead = kSPFull + 1,  // elementwise -> MMA: S(i) is in registers (8 warps)
-    kDSFull = kSRead + 1,  // elementwise -> MMA: dS(i) is in TMEM (8 warps)
+    kDPRead = kSRead + 1,  // elementwise -> MMA: dP(i) is in registers (8 warps)
+    kDSFull = kDPRead + 1,  // elementwise -> MMA: dS(i) is in shared memory (8 warps)
     kOpsReady = kDSFull + 1,  // Q and dO are in TMEM (8 warps)
-    kAccDone = kOpsReady + 1,
+    kDSFree = kOpsReady + 1,  // MMA -> elementwise: dQ(i) has read the dS tile
+    kAccDone = kDSFree + 1,
     kDrain = kAccDone + 1,
     kNever = kDrain + 1,
     kNumBars = kNever + 1
@@ -522,6 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           issue_dp(0);
         }
       }
+      const uint64_t dS0 = desc_kmajor(sbase + L::kOffDS);
       for (int i = 0; i < n_iter && ok; ++i) {
         const int n1 = i + 1;
         if (n1 < n_iter) {
@@ -529,17 +533,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!(ok = mbar_wait(bar(kSRead), i & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
           tc_fence_after();
           issue_s(n1);
+          if (!(ok = mbar_wait(bar(kDPRead), i & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
+          tc_fence_after();
+          issue_dp(n1);
         }
         if (!(ok = mbar_wait(bar(kDSFull), i & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
         tc_fence_after();
         const uint64_t mk = desc_mnmajor(stage(i), NK * 128);
 #pragma unroll
         for (int kk = 0; kk < NK / 16; ++kk) {
-          mma_ts(tmem + L::kTmemDQ, tmem + L::kTmemDP + 64 * (kk >> 2) + 8 * (kk & 3),
-                 mk + ((kk * 2048) >> 4), idAcc, (i > 0 || kk > 0) ? 1u : 0u);
+          const uint32_t offs = ((kk >> 2) * (kRows * 128) + (kk & 3) * 32) >> 4;
+          mma_ss(tmem + L::kTmemDQ, dS0 + offs, mk + ((kk * 2048) >> 4), idAcc,
+                 (i > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(bar(kKVEmpty + i % NS));
-        if (n1 < n_iter) issue_dp(n1);
+        mma_commit(bar(kDSFree));
       }
       mma_commit(bar(kAccDone));
       mma_commit(bar(kDrain));
@@ -608,6 +616,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float abase = ALIBI ? slope2 * (float)(gi - (int64_t)j0 - p.k_off) : 0.f;
       int clo, chi;  // kept key columns [clo, chi) of this query row
       keys_for_query(p, gi, qi < p.Sq, j0, NK, &clo, &chi);
+      uint8_t* ds_row = smem + L::kOffDS + eg * (kRows * 128);  // this warpgroup's 64 keys
       auto step = [&](auto masked) {
         constexpr bool MASKED = decltype(masked)::value;
 #pragma unroll
@@ -615,6 +624,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t dr[32];
           tmem_ld32(tDb + 32 * half, dr);
           tmem_ld_wait();
+          if (half == 1) {  // all of dP(i) is in registers: dP(i+1) may start
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kDPRead));
+          }
           uint32_t dpk[16];
 #pragma unroll
           for (int c = 0; c < 32; c += 2) {
@@ -638,16 +652,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             dpk[c / 2] = pack2<BF16>(ds2[0], ds2[1]);
           }
-          // dS of this 32-key half -> packed columns [16·half, 16·half + 16)
-          // of this warpgroup's dP columns (all read by then: half 0 wrote
-          // over its own, half 1 writes over half 0's).
-          tmem_st16(tDb + 16 * half, dpk);
+          // dS of this 32-key half -> 16-byte chunks [4·half, 4·half + 4) of
+          // this row of the warpgroup's swizzled sub-tile; dQ(i-1) has read
+          // the tile by then.
+          if (half == 0 && i > 0 && !warp_wait(bar(kDSFree), (uint32_t)((i - 1) & 1), ctl)) return false;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<uint4*>(ds_row + sw128_offset(row, 4 * half + j)) =
+                make_uint4(dpk[4 * j], dpk[4 * j + 1], dpk[4 * j + 2], dpk[4 * j + 3]);
         }
+        return true;
       };
-      if (full) step(std::false_type{});
-      else step(std::true_type{});
-      tmem_st_wait();
-      tc_fence_before();
+      if (!(ok = full ? step(std::false_type{}) : step(std::true_type{}))) break;
+      fence_async_shared();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kDSFull));
     }
