@@ -638,13 +638,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int cc = 64 * eg + 32 * half + c + h;
               const float raw = __uint_as_float(sr[32 * half + c + h]);
               float pr, t = 0.f;
+              float x;
               if (CAP || ALIBI) {
-                float x = logit2<CAP>(raw, sl2, cap_in, cap_out, &t);
+                x = logit2<CAP>(raw, sl2, cap_in, cap_out, &t);
                 if (ALIBI) x = fmaf(-slope2, (float)cc, x + abase);
-                pr = ex2(x - lse2);
+                x -= lse2;
               } else {
-                pr = ex2(fmaf(raw, sl2, -lse2));
+                x = fmaf(raw, sl2, -lse2);
               }
+              pr = ex2(x);
               if (MASKED) pr = ((unsigned)(cc - clo) < (unsigned)(chi - clo)) ? pr : 0.f;
               float ds = pr * (__uint_as_float(dr[c + h]) - dlt) * p.scale;
               if (CAP) ds *= (1.f - t * t);

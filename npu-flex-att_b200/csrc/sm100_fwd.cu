@@ -24,6 +24,7 @@
 #include <cuda_runtime.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "bfa_internal.h"
 #include "sm100_host.h"
@@ -328,21 +329,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       // of which were already read (by chunk ch or an earlier one).
       float s4[4] = {0.f, 0.f, 0.f, 0.f};
       const float xs = store_x ? 1.f : sl2;  // x = raw * xs
+      // On a fully kept tile (no -inf logits) every fourth exponential runs
+      // on the FMA pipe (ex2_poly), the rest on the MUFU unit.
+      auto pass2 = [&](auto split) {
+        constexpr bool SPLIT = decltype(split)::value;
 #pragma unroll 1
-      for (int ch = 0; ch < kBN / 32; ++ch) {
-        uint32_t r[32];
-        tmem_ld32(tS + 32 * ch, r);
-        tmem_ld_wait();
-        uint32_t pk[16];
+        for (int ch = 0; ch < kBN / 32; ++ch) {
+          uint32_t r[32];
+          tmem_ld32(tS + 32 * ch, r);
+          tmem_ld_wait();
+          uint32_t pk[16];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float p0 = ex2(fmaf(__uint_as_float(r[e]), xs, -m_use));
-          const float p1 = ex2(fmaf(__uint_as_float(r[e + 1]), xs, -m_use));
-          s4[(e >> 1) & 3] += p0 + p1;
-          pk[e / 2] = pack2<BF16>(p0, p1);
+          for (int e = 0; e < 32; e += 2) {
+            const float x0 = fmaf(__uint_as_float(r[e]), xs, -m_use);
+            const float x1 = fmaf(__uint_as_float(r[e + 1]), xs, -m_use);
+            const float p0 = ex2(x0);
+            const float p1 = (SPLIT && (e & 3) == 2) ? ex2_poly(x1) : ex2(x1);
+            s4[(e >> 1) & 3] += p0 + p1;
+            pk[e / 2] = pack2<BF16>(p0, p1);
+          }
+          tmem_st16(tS + 16 * ch, pk);
         }
-        tmem_st16(tS + 16 * ch, pk);
-      }
+      };
+      if (full) pass2(std::true_type{});
+      else pass2(std::false_type{});
       const float rs = (s4[0] + s4[1]) + (s4[2] + s4[3]);
       l = l * alpha + rs;
       m = m_new;

@@ -401,6 +401,22 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// 2^x on the FMA pipe instead of the MUFU unit, to split the exponentials of
+// a softmax between the two (the MUFU unit alone is a bottleneck on B200).
+// Cody-Waite style reduction x = j + f, j = rint(x) taken from the low
+// mantissa bits of x + 1.5·2^23, f in [-0.5, 0.5]; 2^f by a cubic fitted for
+// this code by relative least squares on Chebyshev nodes (max relative error
+// 7.8e-5, ample for 16-bit P); 2^j is added to the exponent bits. x is
+// clamped to >= -126, so the result is never exactly 0: callers use it only
+// where no element is masked to -inf (or zero masked elements themselves).
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.05508868f, f, 0.24260405f), f, 0.69327623f), f, 0.99992895f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 __device__ __forceinline__ float lg2(float x) {
   float y;
   asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
