@@ -362,6 +362,70 @@ def run_e2e(nfa, dev, args, world):
             "steps": steps}
 
 
+C5 = dict(B=1, Hq=64, Hkv=8, S=65536, D=128)
+C5_WORKLOAD = "c5: bf16 B=1 Hq=64 Hkv=8 D=128 S=65536 causal + ALiBi, context-parallel K/V ring"
+
+
+def run_c5(args):
+    """Config 5 through the context-parallel ring (one process per GPU): each
+    rank holds its zigzag shard (2 chunks of S/(2N) rows) of Q, K, V and runs
+    forward + backward with context_parallel_attention. FLOPs count the
+    unmasked pairs of the whole causal sequence (14·D per pair per q-head)."""
+    import datetime
+    import context_parallel as cp
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29517")
+    torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev,
+                                         rank=rank, world_size=world)
+    B, Hq, Hkv, S, D = C5["B"], C5["Hq"], C5["Hkv"], C5["S"], C5["D"]
+    rows = S // world
+    gd = torch.Generator(device=dev).manual_seed(4321 + rank)
+    q = torch.randn(B, Hq, rows, D, generator=gd, device=dev, dtype=torch.bfloat16).requires_grad_(True)
+    k = torch.randn(B, Hkv, rows, D, generator=gd, device=dev, dtype=torch.bfloat16).requires_grad_(True)
+    v = torch.randn(B, Hkv, rows, D, generator=gd, device=dev, dtype=torch.bfloat16).requires_grad_(True)
+    do = torch.randn(B, Hq, rows, D, generator=gd, device=dev, dtype=torch.bfloat16)
+    slopes = torch.tensor([2.0 ** (-8.0 * (i + 1) / Hq) for i in range(Hq)], device=dev)
+
+    def step():
+        q.grad = k.grad = v.grad = None
+        o = cp.context_parallel_attention(q, k, v, causal=True, alibi_slope=slopes)
+        o.backward(do)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    torch.distributed.barrier()
+    s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_.record()
+    for _ in range(args.steps):
+        step()
+    e_.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([s_.elapsed_time(e_) / args.steps], device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    flops = 14.0 * D * causal_pairs(S) * B * Hq
+    peak_tf, _, peak_kind = peaks()
+    if rank == 0:
+        value = flops / (ms * 1e-3) / 1e12
+        print(json.dumps({
+            "metric": METRIC, "value": round(value, 3), "unit": "TFLOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1), generated on device)",
+            "config": {"workload": C5_WORKLOAD, "global_batch": B, "seq_len": S,
+                       "parallelism": f"context-parallel zigzag K/V ring over {world} GPU(s), NCCL"},
+            "pct_of_peak": round(100.0 * value / world / peak_tf, 2),
+            "gpu_launches": None, "roofline": None, "cpu_baseline": None, "e2e": None,
+            "note": "auxiliary measurement of the P-2 ring; the headline line is the default c3 run"}),
+            flush=True)
+    torch.distributed.barrier()
+    torch.distributed.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -370,6 +434,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["c3", "c5"], default="c3",
+                    help="c3 (default, the headline) or c5 (context-parallel ring)")
     ap.add_argument("--profile", action="store_true",
                     help="for ncu: only the warm-up and timed steps (no e2e, no CPU baseline)")
     args = ap.parse_args()
@@ -377,6 +443,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "c5":
+        run_c5(args)
     else:
         run_ours(args)
 
