@@ -96,9 +96,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* warp_ok = (int*)(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_kt = (p.Sk + kRows - 1) / kRows;
-  const int kt = blockIdx.x % n_kt;
-  const int bh = blockIdx.x / n_kt;
+  // Key tiles are the slow index, so all (batch, kv-head) units' first key
+  // tiles -- the longest under a causal mask -- are dispatched first
+  // (longest-first over the whole grid).
+  const int kt = (int)(blockIdx.x / (p.B * p.Hkv));
+  const int bh = (int)(blockIdx.x % (p.B * p.Hkv));
   const int hkv = bh % p.Hkv, b = bh / p.Hkv;
   const int c0 = kt * kRows;
   int qlo, qhi;
