@@ -273,6 +273,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float lse_c[4] = {l4.x, l4.y, l4.z, l4.w};
             const float dl_c[4] = {d4.x, d4.y, d4.z, d4.w};
             float pr4[4], ds4[4];
+            if (!CAP && !ALIBI) {
+              // Plain logits: two keys per packed instruction (fma / add /
+              // mul .f32x2), which leaves issue slots to the MMA thread on
+              // the same sub-partition.
+#pragma unroll
+              for (int h = 0; h < 4; h += 2) {
+                const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[c + h]), __uint_as_float(sr[c + h + 1])),
+                                            make_float2(sl2, sl2), make_float2(-lse_c[h], -lse_c[h + 1]));
+                float pr0 = ex2(x.x), pr1 = ex2(x.y);
+                if (MASKED) {
+                  const int cc = 32 * half + c + h;
+                  pr0 = ((unsigned)(cc - clo) < (unsigned)(chi - clo)) ? pr0 : 0.f;
+                  pr1 = ((unsigned)(cc + 1 - clo) < (unsigned)(chi - clo)) ? pr1 : 0.f;
+                }
+                const float2 dd = __fadd2_rn(make_float2(__uint_as_float(dr[c + h]), __uint_as_float(dr[c + h + 1])),
+                                             make_float2(-dl_c[h], -dl_c[h + 1]));
+                const float2 ds = __fmul2_rn(__fmul2_rn(make_float2(pr0, pr1), dd), make_float2(p.scale, p.scale));
+                pr4[h] = pr0;
+                pr4[h + 1] = pr1;
+                ds4[h] = ds.x;
+                ds4[h + 1] = ds.y;
+              }
+            } else {
 #pragma unroll
             for (int h = 0; h < 4; ++h) {
               const int cc = 32 * half + c + h;
@@ -290,6 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (CAP) ds *= (1.f - t * t);
               pr4[h] = pr;
               ds4[h] = ds;
+            }
             }
             ppk[c / 2] = pack2<BF16>(pr4[0], pr4[1]);
             ppk[c / 2 + 1] = pack2<BF16>(pr4[2], pr4[3]);
@@ -632,6 +656,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive(bar(kDPRead));
           }
           uint32_t dpk[16];
+          if (!CAP && !ALIBI) {
+            // Plain logits: two keys per packed instruction (fma / mul
+            // .f32x2), which leaves issue slots to the MMA thread on the same
+            // sub-partition; dS = P (dP·scale - Δ·scale).
+            const float2 sl22 = make_float2(sl2, sl2), nl2 = make_float2(-lse2, -lse2);
+            const float2 sc2 = make_float2(p.scale, p.scale), nds2 = make_float2(-dlt * p.scale, -dlt * p.scale);
+#pragma unroll
+            for (int c = 0; c < 32; c += 2) {
+              const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[32 * half + c]),
+                                                      __uint_as_float(sr[32 * half + c + 1])), sl22, nl2);
+              float pr0 = ex2(x.x), pr1 = ex2(x.y);
+              if (MASKED) {
+                const int cc = 64 * eg + 32 * half + c;
+                pr0 = ((unsigned)(cc - clo) < (unsigned)(chi - clo)) ? pr0 : 0.f;
+                pr1 = ((unsigned)(cc + 1 - clo) < (unsigned)(chi - clo)) ? pr1 : 0.f;
+              }
+              const float2 ds = __fmul2_rn(make_float2(pr0, pr1),
+                                           __ffma2_rn(make_float2(__uint_as_float(dr[c]), __uint_as_float(dr[c + 1])), sc2, nds2));
+              dpk[c / 2] = pack2<BF16>(ds.x, ds.y);
+            }
+          } else
 #pragma unroll
           for (int c = 0; c < 32; c += 2) {
             float ds2[2];

@@ -42,6 +42,9 @@ constexpr int kThreads = 384;
 // units). Until then P is computed against the stale max, so P <= 2^8; the
 // final O/l and LSE are exact either way.
 constexpr float kRescaleThreshold = 8.0f;
+// Every kPolyEvery-th exponential of a fully kept tile runs on the FMA pipe
+// (ex2_poly) instead of the MUFU unit.
+constexpr int kPolyEvery = 4;
 
 template <int D>
 struct FwdLayout {
@@ -274,9 +277,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Pass 1: logits in base 2 (cap, ALiBi, mask) and their row max. When
       // the logit is more than a scaled copy of S it is written back to TMEM.
       // The chunk loops stay rolled (one 32-column body in the instruction
-      // cache); four independent max / sum accumulators break the dependency
-      // chains. A plain, fully kept tile only needs max(S) (the scale is > 0)
-      // and folds the scale into the exponent with one FMA.
+      // cache); four independent max accumulators (three-input max) and two
+      // packed sum accumulators break the dependency chains. A plain, fully
+      // kept tile only needs max(S) (the scale is > 0) and folds the scale
+      // into the exponent with one FMA.
       const bool full = tile_full(p, tr0, tr0 + kBM, c0, c0 + kBN);
       const bool store_x = CAP || ALIBI || !full || !(sl2 > 0.f);
       const float abase = ALIBI ? slope2 * (float)(gi - (int64_t)c0 - p.k_off) : 0.f;
@@ -296,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_wait();
           if (!store_x) {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) m4[e & 3] = fmaxf(m4[e & 3], __uint_as_float(r[e]));
+            for (int e = 0; e < 32; e += 2) m4[(e >> 1) & 3] = fmax3(m4[(e >> 1) & 3], __uint_as_float(r[e]), __uint_as_float(r[e + 1]));
           } else {
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
@@ -327,12 +331,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Pass 2: P = 2^(x - m) packed to 16 bits over the first 64 columns of
       // the S region. Chunk ch writes packed columns [16ch, 16ch + 16), all
       // of which were already read (by chunk ch or an earlier one).
-      float s4[4] = {0.f, 0.f, 0.f, 0.f};
-      const float xs = store_x ? 1.f : sl2;  // x = raw * xs
-      // On a fully kept tile (no -inf logits) every fourth exponential runs
-      // on the FMA pipe (ex2_poly), the rest on the MUFU unit.
+      // The softmax warps share each sub-partition's issue slots with the
+      // single thread that issues the MMAs, and a warp with a long run of
+      // ready FMA-pipe instructions starves it (measured: MMA steps up to 3x
+      // slower). So x and the row sums are formed in packed pairs (one
+      // fma.f32x2 / add.f32x2 per two keys); on a fully kept tile every
+      // kPolyEvery-th exponential runs on the FMA pipe (ex2_poly) to unload
+      // the MUFU unit.
+      float2 s2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      const float2 xs2 = make_float2(store_x ? 1.f : sl2, store_x ? 1.f : sl2);
+      const float2 nm2 = make_float2(-m_use, -m_use);
       auto pass2 = [&](auto split) {
-        constexpr bool SPLIT = decltype(split)::value;
+        constexpr bool SPLIT = decltype(split)::value && kPolyEvery > 0;
 #pragma unroll 1
         for (int ch = 0; ch < kBN / 32; ++ch) {
           uint32_t r[32];
@@ -341,11 +351,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
-            const float x0 = fmaf(__uint_as_float(r[e]), xs, -m_use);
-            const float x1 = fmaf(__uint_as_float(r[e + 1]), xs, -m_use);
-            const float p0 = ex2(x0);
-            const float p1 = (SPLIT && (e & 3) == 2) ? ex2_poly(x1) : ex2(x1);
-            s4[(e >> 1) & 3] += p0 + p1;
+            const float2 x = __ffma2_rn(make_float2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), xs2, nm2);
+            const float p0 = ex2(x.x);
+            const float p1 = (SPLIT && e % kPolyEvery == kPolyEvery - 2) ? ex2_poly(x.y) : ex2(x.y);
+            s2[(e >> 1) & 1] = __fadd2_rn(s2[(e >> 1) & 1], make_float2(p0, p1));
             pk[e / 2] = pack2<BF16>(p0, p1);
           }
           tmem_st16(tS + 16 * ch, pk);
@@ -353,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       if (full) pass2(std::true_type{});
       else pass2(std::false_type{});
-      const float rs = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+      const float rs = (s2[0].x + s2[0].y) + (s2[1].x + s2[1].y);
       l = l * alpha + rs;
       m = m_new;
       if (it > 0) {

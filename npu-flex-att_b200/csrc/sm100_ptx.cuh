@@ -401,6 +401,13 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// max(a, b, c) in one instruction (three-input max.f32, sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // 2^x on the FMA pipe instead of the MUFU unit, to split the exponentials of
 // a softmax between the two (the MUFU unit alone is a bottleneck on B200).
 // Cody-Waite style reduction x = j + f, j = rint(x) taken from the low
