@@ -196,9 +196,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < n_iter && ok; ++i) {
         const int bf = i & 1, k = i >> 1;
         if (i + 1 < n_iter) {
+          // Q/dO come by TMA (ordered by the mbarrier). The S/dP buffer being
+          // overwritten was last read by the elementwise warps of step i - 1,
+          // ordered by the DSFull wait and fence of that step.
           const int n1 = i + 1;
           if (!(ok = mbar_wait(bar(kQFull + n1 % NS), (n1 / NS) & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
-          tc_fence_after();
           issue_sp(n1);
         }
         if (!(ok = mbar_wait(bar(kDSFull + bf), k & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;

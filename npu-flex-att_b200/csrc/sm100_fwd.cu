@@ -12,10 +12,10 @@
 //   warp 2      TMEM allocator (512 columns)
 //   warps 4-7   softmax for query tile 0, warps 8-11 for tile 1: each thread
 //               owns one query row (one TMEM lane), reads its S row with
-//               tcgen05.ld, writes P (16-bit) into a 128B-swizzled smem tile
-//               that the next MMA reads as its A operand, rescales its O row
-//               in TMEM when the running max grows, and finally writes O via
-//               smem + TMA store and the LSE.
+//               tcgen05.ld, writes P (16-bit) over the first 64 columns of its
+//               S in TMEM, the A operand of the PV MMA (TS form), rescales its
+//               O row in TMEM when the running max grows, and finally writes O
+//               via smem + TMA store and the LSE.
 // The MMA order S_0(j), S_1(j), then per step PV_0(j), S_0(j+1), PV_1(j),
 // S_1(j+1) lets one tile's softmax run while the tensor core works on the
 // other tile. K/V are read with the GQA head map hkv = hq / G
@@ -44,7 +44,7 @@ constexpr int kThreads = 384;
 constexpr float kRescaleThreshold = 8.0f;
 // Every kPolyEvery-th exponential of a fully kept tile runs on the FMA pipe
 // (ex2_poly) instead of the MUFU unit.
-constexpr int kPolyEvery = 4;
+constexpr int kPolyEvery = 8;
 
 template <int D>
 struct FwdLayout {
@@ -226,8 +226,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           issue_pv(0, iv, it > 0);
           if (more) {
+            // K comes by TMA (ordered by the mbarrier); the softmax reads of
+            // S_0 were ordered by the PFull wait and fence above.
             if (!(ok = wait_load(ik))) break;
-            tc_fence_after();
             issue_s(0, ik);
           }
           if (!(ok = mbar_wait(bar(kPFull + 1), it & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
@@ -271,18 +272,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!(ok = warp_wait(wbar, wpar, ctl))) break;
       tc_fence_after();
 
-      // Two passes over the S row in 32-column TMEM chunks keep the register
-      // footprint small (a whole 128-value row plus packed P does not fit the
-      // 168 registers a thread has at 384 threads without spilling).
-      // Pass 1: logits in base 2 (cap, ALiBi, mask) and their row max. When
-      // the logit is more than a scaled copy of S it is written back to TMEM.
-      // The chunk loops stay rolled (one 32-column body in the instruction
-      // cache); four independent max accumulators (three-input max) and two
-      // packed sum accumulators break the dependency chains. A plain, fully
-      // kept tile only needs max(S) (the scale is > 0) and folds the scale
-      // into the exponent with one FMA.
+      // The whole 128-column S row comes into registers with four TMEM loads
+      // and one wait: one TMEM round trip per step instead of one per
+      // 32-column chunk and pass. Logits in base 2 (cap, ALiBi, mask) are
+      // formed in place; a plain, fully kept tile only needs max(S) (the
+      // scale is > 0) and folds the scale into the exponent with one FMA.
+      // Four independent max accumulators (three-input max) and two packed
+      // sum accumulators break the dependency chains.
       const bool full = tile_full(p, tr0, tr0 + kBM, c0, c0 + kBN);
-      const bool store_x = CAP || ALIBI || !full || !(sl2 > 0.f);
+      const bool store_x = CAP || ALIBI || !full || !(sl2 > 0.f);  // x != S * sl2
       const float abase = ALIBI ? slope2 * (float)(gi - (int64_t)c0 - p.k_off) : 0.f;
       int clo, chi;  // kept key columns [clo, chi) of this row (all of them on a full tile)
       keys_for_query(p, gi, r_local < p.Sq, c0, kBN, &clo, &chi);
@@ -290,35 +288,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         clo = 0;
         chi = kBN;
       }
+      uint32_t r[kBN / 32][32];
+#pragma unroll
+      for (int ch = 0; ch < kBN / 32; ++ch) tmem_ld32(tS + 32 * ch, r[ch]);
+      tmem_ld_wait();
       float mx;
       {
         float m4[4] = {neg_inf(), neg_inf(), neg_inf(), neg_inf()};
-#pragma unroll 1
-        for (int ch = 0; ch < kBN / 32; ++ch) {
-          uint32_t r[32];
-          tmem_ld32(tS + 32 * ch, r);
-          tmem_ld_wait();
-          if (!store_x) {
+        if (!store_x) {
 #pragma unroll
-            for (int e = 0; e < 32; e += 2) m4[(e >> 1) & 3] = fmax3(m4[(e >> 1) & 3], __uint_as_float(r[e]), __uint_as_float(r[e + 1]));
-          } else {
+          for (int ch = 0; ch < kBN / 32; ++ch)
+#pragma unroll
+            for (int e = 0; e < 32; e += 2)
+              m4[(e >> 1) & 3] = fmax3(m4[(e >> 1) & 3], __uint_as_float(r[ch][e]), __uint_as_float(r[ch][e + 1]));
+        } else {
+#pragma unroll
+          for (int ch = 0; ch < kBN / 32; ++ch) {
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
               const int c = 32 * ch + e;
-              const float raw = __uint_as_float(r[e]);
+              const float raw = __uint_as_float(r[ch][e]);
               float x = CAP ? cap_out * tanh_exp(raw * cap_in) : raw * sl2;
               if (ALIBI) x = fmaf(-slope2, (float)c, x + abase);
               x = ((unsigned)(c - clo) < (unsigned)(chi - clo)) ? x : neg_inf();
-              r[e] = __float_as_uint(x);
+              r[ch][e] = __float_as_uint(x);
               m4[e & 3] = fmaxf(m4[e & 3], x);
             }
-            tmem_st32(tS + 32 * ch, r);
           }
         }
         mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
         if (!store_x) mx *= sl2;
       }
-      if (store_x) tmem_st_wait();
       // Raise the reference max only when it grows by more than the threshold
       // (or is still -inf); the decision is warp-uniform because the O rescale
       // uses warp-collective TMEM loads/stores.
@@ -328,30 +328,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (__any_sync(0xffffffffu, grow)) m_new = fmaxf(m, mx);
       const float m_use = (m_new == neg_inf()) ? 0.f : m_new;
       const float alpha = ex2(m - m_use);
-      // Pass 2: P = 2^(x - m) packed to 16 bits over the first 64 columns of
-      // the S region. Chunk ch writes packed columns [16ch, 16ch + 16), all
-      // of which were already read (by chunk ch or an earlier one).
-      // The softmax warps share each sub-partition's issue slots with the
-      // single thread that issues the MMAs, and a warp with a long run of
-      // ready FMA-pipe instructions starves it (measured: MMA steps up to 3x
-      // slower). So x and the row sums are formed in packed pairs (one
-      // fma.f32x2 / add.f32x2 per two keys); on a fully kept tile every
-      // kPolyEvery-th exponential runs on the FMA pipe (ex2_poly) to unload
-      // the MUFU unit.
+      // P = 2^(x - m) packed to 16 bits over the first 64 columns of the S
+      // region (the row is already in registers). The softmax warps share
+      // each sub-partition's issue slots with the single thread that issues
+      // the MMAs, and a warp with a long run of ready FMA-pipe instructions
+      // starves it (measured: MMA steps up to 3x slower). So x and the row
+      // sums are formed in packed pairs (one fma.f32x2 / add.f32x2 per two
+      // keys); on a fully kept tile every kPolyEvery-th exponential runs on
+      // the FMA pipe (ex2_poly) to unload the MUFU unit.
       float2 s2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
       const float2 xs2 = make_float2(store_x ? 1.f : sl2, store_x ? 1.f : sl2);
       const float2 nm2 = make_float2(-m_use, -m_use);
-      auto pass2 = [&](auto split) {
+      auto exps = [&](auto split) {
         constexpr bool SPLIT = decltype(split)::value && kPolyEvery > 0;
-#pragma unroll 1
+#pragma unroll
         for (int ch = 0; ch < kBN / 32; ++ch) {
-          uint32_t r[32];
-          tmem_ld32(tS + 32 * ch, r);
-          tmem_ld_wait();
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
-            const float2 x = __ffma2_rn(make_float2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), xs2, nm2);
+            const float2 x = __ffma2_rn(make_float2(__uint_as_float(r[ch][e]), __uint_as_float(r[ch][e + 1])), xs2, nm2);
             const float p0 = ex2(x.x);
             const float p1 = (SPLIT && e % kPolyEvery == kPolyEvery - 2) ? ex2_poly(x.y) : ex2(x.y);
             s2[(e >> 1) & 1] = __fadd2_rn(s2[(e >> 1) & 1], make_float2(p0, p1));
@@ -360,8 +355,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st16(tS + 16 * ch, pk);
         }
       };
-      if (full) pass2(std::true_type{});
-      else pass2(std::false_type{});
+      if (full) exps(std::true_type{});
+      else exps(std::false_type{});
       const float rs = (s2[0].x + s2[0].y) + (s2[1].x + s2[1].y);
       l = l * alpha + rs;
       m = m_new;
