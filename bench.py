@@ -459,6 +459,78 @@ def run_c5(args):
     torch.distributed.destroy_process_group()
 
 
+DEC = dict(B=8, Hq=32, Hkv=8, Sq=1, Sk=32768, D=128)
+DEC_WORKLOAD = ("decode: bf16 B=8 Hq=32 Hkv=8 D=128, 1 query per head, 32768 keys, causal with "
+                "the query at the end of the keys (split-KV path)")
+
+
+def run_decode(args):
+    """Decoding forward (one query per q-head, long K/V) through the split-KV
+    path on one GPU. The metric is the K/V read bandwidth, bounded by HBM:
+    K and V (1.07 GB, larger than L2) are read once per step. The regular
+    forward (BFA_FWD_DECODE=0) is timed on the same inputs beside it."""
+    import bfa_lib
+    import npu_flash_attention as nfa
+    _, _, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    lib = bfa_lib.load()
+    B, Hq, Hkv, Sq, Sk, D = DEC["B"], DEC["Hq"], DEC["Hkv"], DEC["Sq"], DEC["Sk"], DEC["D"]
+    g = torch.Generator(device=dev).manual_seed(777)
+    q = torch.randn(B, Hq, Sq, D, generator=g, device=dev, dtype=torch.bfloat16)
+    k = torch.randn(B, Hkv, Sk, D, generator=g, device=dev, dtype=torch.bfloat16)
+    v = torch.randn(B, Hkv, Sk, D, generator=g, device=dev, dtype=torch.bfloat16)
+    kv_bytes = 2 * k.numel() * k.element_size()
+
+    def step():
+        return nfa.npu_flash_attention_forward(q, k, v, causal=True, q_pos_offset=Sk - Sq, return_lse=True)
+
+    def timed(steps, sample_clocks):
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        nfa.check_device_status(dev)
+        sampler = ClockSampler(local) if sample_clocks else None
+        if sampler:
+            sampler.start()
+            time.sleep(0.3)
+        n0 = lib.bfa_launch_count()
+        s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s_.record()
+        for _ in range(steps):
+            step()
+        e_.record()
+        torch.cuda.synchronize()
+        clocks = sampler.stop() if sampler else None
+        nfa.check_device_status(dev)
+        return s_.elapsed_time(e_) / steps, lib.bfa_launch_count() - n0, clocks
+
+    steps = max(args.steps, 20)
+    os.environ.pop("BFA_FWD_DECODE", None)
+    ms, launches, clocks = timed(steps, True)
+    os.environ["BFA_FWD_DECODE"] = "0"
+    ms_regular, _, _ = timed(max(3, steps // 4), False)
+    os.environ.pop("BFA_FWD_DECODE", None)
+    _, hbm, peak_kind = peaks()
+    gbs = kv_bytes / (ms * 1e-3) / 1e9
+    print(json.dumps({
+        "metric": "decode forward K/V read bandwidth", "value": round(gbs, 1), "unit": "GB/s",
+        "n_gpus": 1, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1), generated on device)",
+        "config": {"workload": DEC_WORKLOAD, "global_batch": B, "seq_len": Sk,
+                   "parallelism": "1 GPU", "l2": "K/V 1.07 GB, larger than L2"},
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(gbs / hbm, 4), "peak_kind": f"HBM copy, {peak_kind}",
+                     "traffic": None, "algorithmic_bytes_per_launch": kv_bytes},
+        "regular_path_ms": round(ms_regular, 5),
+        "cpu_baseline": None, "e2e": None, "clocks": clocks,
+        "note": "auxiliary measurement of the split-KV decoding path; the headline line is the default c3 run"}),
+        flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -467,8 +539,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["c3", "c5"], default="c3",
-                    help="c3 (default, the headline) or c5 (context-parallel ring)")
+    ap.add_argument("--workload", choices=["c3", "c5", "decode"], default="c3",
+                    help="c3 (default, the headline), c5 (context-parallel ring) or decode "
+                         "(split-KV decoding forward)")
     ap.add_argument("--profile", action="store_true",
                     help="for ncu: only the warm-up and timed steps (no e2e, no CPU baseline)")
     args = ap.parse_args()
@@ -478,6 +551,8 @@ def main():
         run_reference(args)
     elif args.workload == "c5":
         run_c5(args)
+    elif args.workload == "decode":
+        run_decode(args)
     else:
         run_ours(args)
 

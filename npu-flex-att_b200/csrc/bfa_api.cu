@@ -102,6 +102,13 @@ int bfa_fwd(const bfa_problem* pr, const bfa_fwd_args* a, void* stream) {
   p.timeout_ns = a->wait_timeout_ns > 0 ? (uint64_t)a->wait_timeout_ns : 1000000000ull;
   p.debug_flags = a->debug_flags;
   cudaStream_t st = (cudaStream_t)stream;
+  // Few query rows per KV head (decoding): the split-KV path streams K/V once
+  // per KV head across the whole GPU. The fault-injection flags exercise the
+  // tcgen05 kernels' bounded waits, so they keep the regular path.
+  if (p.debug_flags == 0 && bfa::decode_eligible(p, pr->dtype)) {
+    const int rc = bfa::decode_fwd(p, pr->dtype, st);
+    if (rc != -1) return rc;
+  }
   if (bfa::sm100_fwd_eligible(p, pr->dtype)) return bfa::sm100_fwd(p, pr->dtype, st);
   return bfa::simt_fwd(p, pr->dtype, st);
 }
