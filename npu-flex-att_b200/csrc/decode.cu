@@ -13,12 +13,13 @@
 //   - one CTA per (batch, KV head, key split) serves all G·Sq rows of that KV
 //     head, so K/V cross HBM once however large G is;
 //   - K/V stream through a cp.async double buffer in 64-key chunks (rows
-//     padded by 16 bytes so the 16-byte shared-memory reads are conflict-free);
-//   - S = q·k, the online softmax and P·V run on the CUDA cores in fp32: at
-//     <= 16 rows they take less time per chunk than the chunk's HBM transfer;
-//   - the keys are split into about eight CTAs per resident CTA slot (two
-//     per SM), so the GPU stays full to the last wave, and a merge kernel
-//     combines the splits' partial (O, LSE) per row.
+//     padded by 16 bytes so the shared-memory reads are conflict-free);
+//   - for bf16 / fp16 the two small GEMMs (S = q·kᵀ and P·V, all rows in one
+//     M = 16 tile) run on the tensor cores with mma.sync m16n8k16, the online
+//     softmax on the CUDA cores; fp32 inputs run S, softmax and P·V on the
+//     CUDA cores;
+//   - the keys are split so that the CTAs fill the GPU in about one wave, and
+//     a merge kernel combines the splits' partial (O, LSE) per row.
 // The math per row is the forward's: S·scale, cap, ALiBi, mask on absolute
 // positions (q_off, k_off), base-2 online softmax, O = PV/l and
 // LSE = m + ln(l) (natural log), -inf with O = 0 for a row that sees no key.
@@ -31,6 +32,7 @@
 #include <type_traits>
 
 #include "bfa_internal.h"
+#include "sm100_ptx.cuh"
 
 namespace bfa {
 namespace {
@@ -66,28 +68,10 @@ __device__ __forceinline__ float fast_ex2(float x) {
   return y;
 }
 
-// 16 bytes of T -> fp32 values.
+// 16 bytes / two consecutive elements of T -> fp32 (the CUDA-core kernel runs
+// only for fp32 inputs; 16-bit inputs take the tensor-core kernel below).
 template <typename T>
 __device__ __forceinline__ void unpack16(const uint4& u, float* f);
-template <>
-__device__ __forceinline__ void unpack16<__nv_bfloat16>(const uint4& u, float* f) {
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    f[2 * i] = __uint_as_float(w[i] << 16);
-    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-  }
-}
-template <>
-__device__ __forceinline__ void unpack16<__half>(const uint4& u, float* f) {
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-    f[2 * i] = t.x;
-    f[2 * i + 1] = t.y;
-  }
-}
 template <>
 __device__ __forceinline__ void unpack16<float>(const uint4& u, float* f) {
   f[0] = __uint_as_float(u.x);
@@ -95,19 +79,8 @@ __device__ __forceinline__ void unpack16<float>(const uint4& u, float* f) {
   f[2] = __uint_as_float(u.z);
   f[3] = __uint_as_float(u.w);
 }
-
-// Two consecutive T at p -> fp32.
 template <typename T>
 __device__ __forceinline__ float2 load2(const uint8_t* p);
-template <>
-__device__ __forceinline__ float2 load2<__nv_bfloat16>(const uint8_t* p) {
-  const uint32_t w = *reinterpret_cast<const uint32_t*>(p);
-  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
-}
-template <>
-__device__ __forceinline__ float2 load2<__half>(const uint8_t* p) {
-  return __half22float2(*reinterpret_cast<const __half2*>(p));
-}
 template <>
 __device__ __forceinline__ float2 load2<float>(const uint8_t* p) {
   return *reinterpret_cast<const float2*>(p);
@@ -320,6 +293,287 @@ __global__ void __launch_bounds__(kDecThreads)
   }
 }
 
+// ------------------------------------------------------------------ 16-bit
+// The same split kernel for bf16 / fp16 with the two small GEMMs on the
+// tensor cores (mma.sync m16n8k16, fp32 accumulate): all <= 16 rows are one
+// M = 16 tile. Per 64-key chunk:
+//   S:   warp w computes keys [8w, 8w + 8) for all rows: A = q (fragments held
+//        in registers for the whole CTA), B = K rows from shared memory;
+//   softmax as in the CUDA-core kernel, on an fp32 P tile in shared memory;
+//   P·V: warp w owns O columns [w·D/8, (w+1)·D/8): A = P rounded to the input
+//        type (as the tcgen05 forward and the reference, p.to(v.dtype)), B = V
+//        via ldmatrix.trans.
+// This takes about a quarter of the instructions of the CUDA-core version,
+// whose issue rate bounds it, so the kernel can run at HBM speed.
+constexpr int kPRow = kChunk + 8;  // P row pitch (floats): conflict-free float2 reads
+// K/V chunks per CTA in the cp.async ring. Two stages (three CTAs per SM at
+// D = 128) measured faster than three (two CTAs per SM) on every decode shape
+// tried: more CTAs per SM keep more loads in flight than a deeper ring.
+constexpr int kStagesM = 2;
+
+template <typename T, int D>
+struct DecLayoutM {
+  static constexpr int kRowBytes = D * 2 + 16;
+  static constexpr int kTileBytes = kChunk * kRowBytes;
+  static constexpr int kOffK = 0;
+  static constexpr int kOffV = kStagesM * kTileBytes;
+  static constexpr int kOffP = 2 * kStagesM * kTileBytes;      // fp32 [16][kPRow]
+  static constexpr int kOffRow = kOffP + kMaxRows * kPRow * 4;   // m, l, alpha per row
+  static constexpr int kSmemBytes = kOffRow + 3 * kMaxRows * 4;
+  static constexpr int kNT = D / 64;                           // 8-column n-tiles per warp in P·V
+  static_assert(sizeof(T) == 2 && D % 64 == 0, "16-bit, D multiple of 64");
+  static_assert(kSmemBytes <= 232448, "smem budget");
+};
+
+template <bool BF16>
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (BF16)
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  else
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                              uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2_trans(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
+               : "=r"(r0), "=r"(r1)
+               : "r"(addr));
+}
+
+template <typename T, int D, bool PLAIN>
+__global__ void __launch_bounds__(kDecThreads)
+    decode_mma_kernel(const Params p, int n_split, int kvis_lo, int split_len, float* __restrict__ part_o,
+                      float* __restrict__ part_lse) {
+  using L = DecLayoutM<T, D>;
+  constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr int NT = L::kNT;
+  extern __shared__ __align__(16) uint8_t smem[];
+  float* ps = reinterpret_cast<float*>(smem + L::kOffP);
+  float* row_m = reinterpret_cast<float*>(smem + L::kOffRow);
+  float* row_l = row_m + kMaxRows;
+  float* row_a = row_l + kMaxRows;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int R = p.G * p.Sq;
+  const int split = (int)(blockIdx.x % n_split);
+  const int bkv = (int)(blockIdx.x / n_split);
+  const int hkv = bkv % p.Hkv, b = bkv / p.Hkv;
+  int klo, khi;
+  key_range(p, 0, p.Sq, &klo, &khi);
+  const int kb = max(kvis_lo + split * split_len, klo);
+  const int ke = min(kvis_lo + (split + 1) * split_len, khi);
+  const int n_chunks = (ke > kb) ? (ke - kb + kChunk - 1) / kChunk : 0;
+  const T* kg = static_cast<const T*>(p.k);
+  const T* vg = static_cast<const T*>(p.v);
+  const float sl2 = p.scale * kLog2e;
+
+  auto load_chunk = [&](int c, int stage) {
+    constexpr int kPieces = D * 2 / 16;
+    const int key0 = kb + c * kChunk;
+    for (int idx = tid; idx < 2 * kChunk * kPieces; idx += kDecThreads) {
+      const int which = idx / (kChunk * kPieces);  // 0: K, 1: V
+      const int rem = idx - which * (kChunk * kPieces);
+      const int n = rem / kPieces, pc = rem - n * kPieces;
+      const int key = key0 + n;
+      uint8_t* dst = smem + (which ? L::kOffV : L::kOffK) + stage * L::kTileBytes + n * L::kRowBytes + pc * 16;
+      if (key < ke) {
+        const T* src = which ? vg + (int64_t)b * p.sv_[0] + (int64_t)hkv * p.sv_[1] + (int64_t)key * p.sv_[2]
+                             : kg + (int64_t)b * p.sk_[0] + (int64_t)hkv * p.sk_[1] + (int64_t)key * p.sk_[2];
+        cp_async16(dst, src + pc * 8);
+      } else {
+        *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    cp_async_commit();
+  };
+  // The first kStagesM - 1 chunks; one commit group per chunk slot (empty
+  // past the end) keeps the group count that cp.async.wait_group relies on.
+  for (int i = 0; i < kStagesM - 1; ++i) {
+    if (i < n_chunks) load_chunk(i, i);
+    else cp_async_commit();
+  }
+
+  // q as A fragments: rows g and g + 8, columns 16ks + 2t (+1) and
+  // 16ks + 8 + 2t (+1); raw 16-bit pairs, low half = lower column.
+  uint32_t qa[D / 16][4];
+  {
+    const uint16_t* qg = static_cast<const uint16_t*>(p.q);
+    auto qpair = [&](int r, int c) -> uint32_t {
+      if (r >= R) return 0u;
+      const int gg = r / p.Sq, s = r - gg * p.Sq;
+      const uint16_t* base = qg + (int64_t)b * p.sq_[0] + (int64_t)(hkv * p.G + gg) * p.sq_[1] + (int64_t)s * p.sq_[2];
+      return (uint32_t)base[(int64_t)c * p.sq_[3]] | ((uint32_t)base[(int64_t)(c + 1) * p.sq_[3]] << 16);
+    };
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      qa[ks][0] = qpair(g, 16 * ks + 2 * t);
+      qa[ks][1] = qpair(g + 8, 16 * ks + 2 * t);
+      qa[ks][2] = qpair(g, 16 * ks + 8 + 2 * t);
+      qa[ks][3] = qpair(g + 8, 16 * ks + 8 + 2 * t);
+    }
+  }
+  if (tid < kMaxRows) {
+    row_m[tid] = neg_inf();
+    row_l[tid] = 0.f;
+    row_a[tid] = 1.f;
+  }
+  // Rows R..15 keep P = 0 (the S phase writes only rows < R).
+  for (int idx = tid; idx < kMaxRows * kPRow; idx += kDecThreads) ps[idx] = 0.f;
+
+  const int col0 = warp * (D / 8);  // this warp's O columns in P·V
+  float o[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+
+  for (int c = 0; c < n_chunks; ++c) {
+    const int stage = c % kStagesM;
+    // Chunk c + kStagesM - 1 goes into the slot chunk c - 1 used (read by
+    // every thread before the last barrier of the previous chunk).
+    const int nxt = c + kStagesM - 1;
+    if (nxt < n_chunks) load_chunk(nxt, nxt % kStagesM);
+    else cp_async_commit();
+    cp_async_wait<kStagesM - 1>();
+    __syncthreads();  // chunk c (and, at c = 0, the row state and P tile) visible
+
+    // S for keys [8w, 8w + 8) of the chunk.
+    {
+      const uint8_t* krow = smem + L::kOffK + stage * L::kTileBytes + (8 * warp + g) * L::kRowBytes;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow + (16 * ks + 2 * t) * 2);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(krow + (16 * ks + 8 + 2 * t) * 2);
+        mma16816<BF16>(acc, qa[ks], b0, b1);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = g + 8 * (e >> 1);
+        const int n = 8 * warp + 2 * t + (e & 1);
+        if (r < R) {
+          const int key = kb + c * kChunk + n;
+          const int gg = r / p.Sq, s = r - gg * p.Sq;
+          const int64_t gi = (int64_t)s + p.q_off, gj = (int64_t)key + p.k_off;
+          const bool keep = key < ke && keep_pair(gi, gj, p.causal, p.window);
+          float x;
+          if (PLAIN) {
+            x = acc[e] * sl2;
+          } else {
+            const float slope = p.alibi ? p.alibi[hkv * p.G + gg] : 0.f;
+            x = transform_logit(acc[e], p.scale, p.soft_cap, slope, gi, gj, nullptr) * kLog2e;
+          }
+          ps[r * kPRow + n] = keep ? x : neg_inf();
+        }
+      }
+    }
+    __syncthreads();
+
+    // Online softmax: one warp per row, two keys per lane.
+    for (int r = warp; r < R; r += kDecThreads / 32) {
+      const float x0 = ps[r * kPRow + lane], x1 = ps[r * kPRow + lane + 32];
+      const float mx = warp_max(fmaxf(x0, x1));
+      const float m_old = row_m[r];
+      const float m_new = fmaxf(m_old, mx);
+      const float m_use = (m_new == neg_inf()) ? 0.f : m_new;
+      const float p0 = fast_ex2(x0 - m_use), p1 = fast_ex2(x1 - m_use);
+      ps[r * kPRow + lane] = p0;
+      ps[r * kPRow + lane + 32] = p1;
+      const float sum = warp_sum(p0 + p1);
+      if (lane == 0) {
+        const float alpha = fast_ex2(m_old - m_use);
+        row_a[r] = alpha;
+        row_l[r] = row_l[r] * alpha + sum;
+        row_m[r] = m_new;
+      }
+    }
+    __syncthreads();
+
+    // O = O·alpha + P·V for this warp's columns.
+    {
+      const float a_lo = row_a[g], a_hi = row_a[g + 8];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        o[nt][0] *= a_lo;
+        o[nt][1] *= a_lo;
+        o[nt][2] *= a_hi;
+        o[nt][3] *= a_hi;
+      }
+      const uint32_t vtile = sm100::smem_u32(smem + L::kOffV + stage * L::kTileBytes);
+#pragma unroll
+      for (int kk = 0; kk < kChunk / 16; ++kk) {
+        const float2 p00 = *reinterpret_cast<const float2*>(ps + g * kPRow + 16 * kk + 2 * t);
+        const float2 p10 = *reinterpret_cast<const float2*>(ps + (g + 8) * kPRow + 16 * kk + 2 * t);
+        const float2 p01 = *reinterpret_cast<const float2*>(ps + g * kPRow + 16 * kk + 8 + 2 * t);
+        const float2 p11 = *reinterpret_cast<const float2*>(ps + (g + 8) * kPRow + 16 * kk + 8 + 2 * t);
+        uint32_t pa[4];
+        if constexpr (BF16) {
+          pa[0] = sm100::pack_bf16(p00.x, p00.y);
+          pa[1] = sm100::pack_bf16(p10.x, p10.y);
+          pa[2] = sm100::pack_bf16(p01.x, p01.y);
+          pa[3] = sm100::pack_bf16(p11.x, p11.y);
+        } else {
+          pa[0] = sm100::pack_f16(p00.x, p00.y);
+          pa[1] = sm100::pack_f16(p10.x, p10.y);
+          pa[2] = sm100::pack_f16(p01.x, p01.y);
+          pa[3] = sm100::pack_f16(p11.x, p11.y);
+        }
+        // B fragments: keys 16kk + (lane & 15), columns col0 + 8nt (+8 for
+        // the upper lanes), transposed on the way in.
+        const uint32_t rowaddr = vtile + (uint32_t)((16 * kk + (lane & 15)) * L::kRowBytes);
+        if constexpr (NT == 1) {
+          uint32_t b0, b1;
+          ldsm_x2_trans(rowaddr + (uint32_t)(col0 * 2), b0, b1);
+          mma16816<BF16>(o[0], pa, b0, b1);
+        } else {
+#pragma unroll
+          for (int nt = 0; nt < NT; nt += 2) {
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_trans(rowaddr + (uint32_t)((col0 + 8 * nt + 8 * (lane >> 4)) * 2), b0, b1, b2, b3);
+            mma16816<BF16>(o[nt], pa, b0, b1);
+            mma16816<BF16>(o[nt + 1], pa, b2, b3);
+          }
+        }
+      }
+    }
+    __syncthreads();  // the stage and the P tile are rewritten by the next chunk
+  }
+
+  // The split's normalised O and LSE.
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = g + 8 * h;
+    if (r < R) {
+      const int gg = r / p.Sq, s = r - gg * p.Sq;
+      const int64_t row = ((int64_t)b * p.Hq + hkv * p.G + gg) * p.Sq + s;
+      const float l = row_l[r];
+      const float inv = (l > 0.f) ? 1.f / l : 0.f;
+      float* dst = part_o + (row * n_split + split) * D + col0 + 2 * t;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        *reinterpret_cast<float2*>(dst + 8 * nt) = make_float2(o[nt][2 * h] * inv, o[nt][2 * h + 1] * inv);
+    }
+  }
+  if (tid < R) {
+    const int gg = tid / p.Sq, s = tid - gg * p.Sq;
+    const int64_t row = ((int64_t)b * p.Hq + hkv * p.G + gg) * p.Sq + s;
+    const float l = row_l[tid];
+    part_lse[row * n_split + split] = (l > 0.f) ? (row_m[tid] + __log2f(l)) * kLn2 : neg_inf();
+  }
+}
+
 // One block per row: lse = log Σ_s exp(lse_s), O = Σ_s exp(lse_s - lse) O_s
 // (the reduce of npu_flash_attention.py:255-293, over the splits that exist).
 // The split weights are formed once in shared memory; each thread then sums
@@ -426,11 +680,42 @@ int launch_decode(const Params& p, cudaStream_t st) {
     klo = (int)l;
     khi = (int)h;
   }
+  const bool plain = !(p.soft_cap > 0.f) && p.alibi == nullptr;
+  const int R = p.G * p.Sq;
+  using Kern = void (*)(const Params, int, int, int, float*, float*);
+  Kern kern;
+  int smem_bytes;
+  if constexpr (sizeof(T) == 2) {
+    kern = plain ? decode_mma_kernel<T, D, true> : decode_mma_kernel<T, D, false>;
+    smem_bytes = DecLayoutM<T, D>::kSmemBytes;
+  } else {
+    auto pick = [&](auto rb) -> Kern {
+      constexpr int RB = decltype(rb)::value;
+      return plain ? decode_split_kernel<T, D, RB, true> : decode_split_kernel<T, D, RB, false>;
+    };
+    kern = R <= 4 ? pick(std::integral_constant<int, 4>{})
+                  : R <= 8 ? pick(std::integral_constant<int, 8>{}) : pick(std::integral_constant<int, 16>{});
+    smem_bytes = L::kSmemBytes;
+  }
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess)
+    return BFA_ERR_CUDA;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kDecThreads, smem_bytes) != cudaSuccess ||
+      per_sm < 1) {
+    cudaGetLastError();
+    per_sm = 1;
+  }
+
   const int kv_heads = p.B * p.Hkv;
   const int vis = khi - klo;
-  // About eight CTAs per resident slot (two per SM), so that the last wave
-  // is a small part of the run, and at least four 64-key chunks per split.
-  int n_split = (16 * sm_count() + kv_heads - 1) / kv_heads;
+  // One wave: as many splits as fill the resident CTA slots, each split a
+  // long run of keys (the per-CTA start-up, pipeline fill and merge input grow
+  // with the split count); two waves when one fills under 3/4 of the slots.
+  // At least four 64-key chunks per split. (Same-box sweep on four decode
+  // shapes: this beats two, four and eight waves by 0-30%.)
+  const int slots = per_sm * sm_count();
+  int n_split = std::max(1, slots / kv_heads);
+  if (4 * kv_heads * n_split < 3 * slots) n_split = std::max(1, 2 * slots / kv_heads);
   n_split = std::max(1, std::min(n_split, std::min(kMaxSplits, (vis + 4 * kChunk - 1) / (4 * kChunk))));
   const int split_len = std::max(kChunk, (vis + n_split - 1) / n_split);
   n_split = std::max(1, (vis + split_len - 1) / split_len);
@@ -447,21 +732,10 @@ int launch_decode(const Params& p, cudaStream_t st) {
   float* part_o = static_cast<float*>(buf);
   float* part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(buf) + o_bytes);
 
-  const bool plain = !(p.soft_cap > 0.f) && p.alibi == nullptr;
-  const int R = p.G * p.Sq;
-  auto pick = [&](auto rb) {
-    constexpr int RB = decltype(rb)::value;
-    return plain ? decode_split_kernel<T, D, RB, true> : decode_split_kernel<T, D, RB, false>;
-  };
-  auto kern = R <= 4 ? pick(std::integral_constant<int, 4>{})
-                     : R <= 8 ? pick(std::integral_constant<int, 8>{}) : pick(std::integral_constant<int, 16>{});
-  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
-  if (err == cudaSuccess) {
-    kern<<<(unsigned)(kv_heads * n_split), kDecThreads, L::kSmemBytes, st>>>(p, n_split, klo, split_len, part_o,
-                                                                             part_lse);
-    note_launch();
-    err = cudaGetLastError();
-  }
+  kern<<<(unsigned)(kv_heads * n_split), kDecThreads, smem_bytes, st>>>(p, n_split, klo, split_len, part_o,
+                                                                        part_lse);
+  note_launch();
+  cudaError_t err = cudaGetLastError();
   if (err == cudaSuccess) {
     decode_merge_kernel<T><<<(unsigned)rows, kMergeThreads, 0, st>>>(p, n_split, part_o, part_lse);
     note_launch();
