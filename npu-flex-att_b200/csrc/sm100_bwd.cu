@@ -66,6 +66,12 @@ struct DkdvLayout {
   static_assert(kStages * kStageBytes >= 2u * kRows * D * 4, "fp32 dK/dV staging");
 };
 
+// (batch, kv-head) units per group in the dK/dV block order (see below).
+#ifndef BFA_DKDV_UNIT_GROUP
+#define BFA_DKDV_UNIT_GROUP 8
+#endif
+constexpr int kUnitGroup = BFA_DKDV_UNIT_GROUP;
+
 template <int D, bool BF16, bool CAP, bool ALIBI>
 __global__ void __launch_bounds__(kThreads, 1)
     dkdv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
@@ -96,11 +102,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* warp_ok = (int*)(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Key tiles are the slow index, so all (batch, kv-head) units' first key
-  // tiles -- the longest under a causal mask -- are dispatched first
-  // (longest-first over the whole grid).
-  const int kt = (int)(blockIdx.x / (p.B * p.Hkv));
-  const int bh = (int)(blockIdx.x % (p.B * p.Hkv));
+  // Block order: (batch, kv-head) units in groups of kUnitGroup; within a
+  // group the key tile is the slow index, so the group's first key tiles --
+  // the longest under a causal mask -- are dispatched first (longest-first),
+  // and the CTAs in flight share one group's Q and dO in L2 instead of every
+  // unit's (which would not fit).
+  const int BHkv = p.B * p.Hkv;
+  const int n_kt = (p.Sk + kRows - 1) / kRows;
+  const int grp = (int)(blockIdx.x / ((unsigned)kUnitGroup * n_kt));
+  const int gsize = min(kUnitGroup, BHkv - grp * kUnitGroup);
+  const int rem = (int)(blockIdx.x - (unsigned)grp * kUnitGroup * n_kt);
+  const int kt = rem / gsize;
+  const int bh = grp * kUnitGroup + rem % gsize;
   const int hkv = bh % p.Hkv, b = bh / p.Hkv;
   const int c0 = kt * kRows;
   int qlo, qhi;
