@@ -306,7 +306,7 @@ __global__ void __launch_bounds__(kDecThreads)
 // This takes about a quarter of the instructions of the CUDA-core version,
 // whose issue rate bounds it, so the kernel can run at HBM speed.
 constexpr int kPRow = kChunk + 8;  // P row pitch (floats): conflict-free float2 reads
-// K/V chunks per CTA in the cp.async ring. Two stages (three CTAs per SM at
+// K/V chunks per CTA: a double buffer. Two stages (three CTAs per SM at
 // D = 128) measured faster than three (two CTAs per SM) on every decode shape
 // tried: more CTAs per SM keep more loads in flight than a deeper ring.
 constexpr int kStagesM = 2;
@@ -400,12 +400,7 @@ __global__ void __launch_bounds__(kDecThreads)
     }
     cp_async_commit();
   };
-  // The first kStagesM - 1 chunks; one commit group per chunk slot (empty
-  // past the end) keeps the group count that cp.async.wait_group relies on.
-  for (int i = 0; i < kStagesM - 1; ++i) {
-    if (i < n_chunks) load_chunk(i, i);
-    else cp_async_commit();
-  }
+  if (n_chunks > 0) load_chunk(0, 0);
 
   // q as A fragments: rows g and g + 8, columns 16ks + 2t (+1) and
   // 16ks + 8 + 2t (+1); raw 16-bit pairs, low half = lower column.
@@ -439,26 +434,30 @@ __global__ void __launch_bounds__(kDecThreads)
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
 
+  // Three barriers per chunk. The one at the top also means every warp has
+  // finished the previous chunk (its P·V read the other K/V slot and the P
+  // tile), so the next chunk's loads and this chunk's S may overwrite them.
   for (int c = 0; c < n_chunks; ++c) {
-    const int stage = c % kStagesM;
-    // Chunk c + kStagesM - 1 goes into the slot chunk c - 1 used (read by
-    // every thread before the last barrier of the previous chunk).
-    const int nxt = c + kStagesM - 1;
-    if (nxt < n_chunks) load_chunk(nxt, nxt % kStagesM);
-    else cp_async_commit();
-    cp_async_wait<kStagesM - 1>();
+    const int stage = c & 1;
+    cp_async_wait<0>();
     __syncthreads();  // chunk c (and, at c = 0, the row state and P tile) visible
+    if (c + 1 < n_chunks) load_chunk(c + 1, stage ^ 1);
 
-    // S for keys [8w, 8w + 8) of the chunk.
+    // S for keys [8w, 8w + 8) of the chunk, in two independent MMA chains.
     {
       const uint8_t* krow = smem + L::kOffK + stage * L::kTileBytes + (8 * warp + g) * L::kRowBytes;
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int ks = 0; ks < D / 16; ++ks) {
+      for (int ks = 0; ks < D / 16; ks += 2) {
         const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow + (16 * ks + 2 * t) * 2);
         const uint32_t b1 = *reinterpret_cast<const uint32_t*>(krow + (16 * ks + 8 + 2 * t) * 2);
+        const uint32_t b2 = *reinterpret_cast<const uint32_t*>(krow + (16 * ks + 16 + 2 * t) * 2);
+        const uint32_t b3 = *reinterpret_cast<const uint32_t*>(krow + (16 * ks + 24 + 2 * t) * 2);
         mma16816<BF16>(acc, qa[ks], b0, b1);
+        mma16816<BF16>(acc2, qa[ks + 1], b2, b3);
       }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[e] += acc2[e];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int r = g + 8 * (e >> 1);
@@ -548,7 +547,6 @@ __global__ void __launch_bounds__(kDecThreads)
         }
       }
     }
-    __syncthreads();  // the stage and the P tile are rewritten by the next chunk
   }
 
   // The split's normalised O and LSE.
