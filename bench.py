@@ -397,13 +397,16 @@ def run_e2e(nfa, dev, args, world):
 
 C5 = dict(B=1, Hq=64, Hkv=8, S=65536, D=128)
 C5_WORKLOAD = "c5: bf16 B=1 Hq=64 Hkv=8 D=128 S=65536 causal + ALiBi, context-parallel K/V ring"
+C5U_WORKLOAD = ("c5: bf16 B=1 Hq=64 Hkv=8 D=128 S=65536 causal + ALiBi, context-parallel Ulysses "
+                "(head-sequence all-to-alls)")
 
 
-def run_c5(args):
-    """Config 5 through the context-parallel ring (one process per GPU): each
-    rank holds its zigzag shard (2 chunks of S/(2N) rows) of Q, K, V and runs
-    forward + backward with context_parallel_attention. FLOPs count the
-    unmasked pairs of the whole causal sequence (14·D per pair per q-head)."""
+def run_c5(args, ulysses=False):
+    """Config 5 through context parallelism (one process per GPU): each rank
+    holds its zigzag shard (2 chunks of S/(2N) rows) of Q, K, V and runs
+    forward + backward with context_parallel_attention (the K/V ring) or, for
+    --workload c5u, ulysses_attention. FLOPs count the unmasked pairs of the
+    whole causal sequence (14·D per pair per q-head)."""
     import datetime
     import context_parallel as cp
     rank, world, local = dist_env()
@@ -424,7 +427,8 @@ def run_c5(args):
 
     def step():
         q.grad = k.grad = v.grad = None
-        o = cp.context_parallel_attention(q, k, v, causal=True, alibi_slope=slopes)
+        attn = cp.ulysses_attention if ulysses else cp.context_parallel_attention
+        o = attn(q, k, v, causal=True, alibi_slope=slopes)
         o.backward(do)
 
     for _ in range(args.warmup):
@@ -449,11 +453,13 @@ def run_c5(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1), generated on device)",
-            "config": {"workload": C5_WORKLOAD, "global_batch": B, "seq_len": S,
-                       "parallelism": f"context-parallel zigzag K/V ring over {world} GPU(s), NCCL"},
+            "config": {"workload": C5U_WORKLOAD if ulysses else C5_WORKLOAD, "global_batch": B, "seq_len": S,
+                       "parallelism": (f"Ulysses all-to-alls over {world} GPU(s), NCCL" if ulysses else
+                                       f"context-parallel zigzag K/V ring over {world} GPU(s), NCCL")},
             "pct_of_peak": round(100.0 * value / world / peak_tf, 2),
             "gpu_launches": None, "roofline": None, "cpu_baseline": None, "e2e": None,
-            "note": "auxiliary measurement of the P-2 ring; the headline line is the default c3 run"}),
+            "note": ("auxiliary measurement of " + ("Ulysses" if ulysses else "the P-2 ring") +
+                     "; the headline line is the default c3 run")}),
             flush=True)
     torch.distributed.barrier()
     torch.distributed.destroy_process_group()
@@ -539,9 +545,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["c3", "c5", "decode"], default="c3",
-                    help="c3 (default, the headline), c5 (context-parallel ring) or decode "
-                         "(split-KV decoding forward)")
+    ap.add_argument("--workload", choices=["c3", "c5", "c5u", "decode"], default="c3",
+                    help="c3 (default, the headline), c5 (context-parallel ring), c5u (context-"
+                         "parallel Ulysses) or decode (split-KV decoding forward)")
     ap.add_argument("--profile", action="store_true",
                     help="for ncu: only the warm-up and timed steps (no e2e, no CPU baseline)")
     args = ap.parse_args()
@@ -549,8 +555,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
-    elif args.workload == "c5":
-        run_c5(args)
+    elif args.workload in ("c5", "c5u"):
+        run_c5(args, ulysses=args.workload == "c5u")
     elif args.workload == "decode":
         run_decode(args)
     else:

@@ -71,6 +71,30 @@ class ZigzagLayout:
         return torch.cat(parts, dim=dim)
 
 
+class ContiguousLayout:
+    """Rows [r·S/N, (r+1)·S/N) of the sequence on rank r (N = world size)."""
+
+    def __init__(self, seqlen: int, world: int):
+        if world < 1 or seqlen % world != 0:
+            raise ValueError(f"seqlen {seqlen} must be a multiple of world ({world})")
+        self.seqlen, self.world = seqlen, world
+        self.rows = seqlen // world
+
+    def shard(self, x: torch.Tensor, rank: int, dim: int = 2) -> torch.Tensor:
+        return x.narrow(dim, rank * self.rows, self.rows).contiguous()
+
+    def unshard(self, shards: list[torch.Tensor], dim: int = 2) -> torch.Tensor:
+        return torch.cat(list(shards), dim=dim)
+
+
+def make_layout(name: str, seqlen: int, world: int):
+    if name == "zigzag":
+        return ZigzagLayout(seqlen, world)
+    if name == "contiguous":
+        return ContiguousLayout(seqlen, world)
+    raise ValueError(f"unknown layout {name!r} (zigzag or contiguous)")
+
+
 @dataclass
 class MaskArgs:
     causal: bool = False
@@ -324,6 +348,156 @@ def run_simulated(gens):
             return results
         if done:
             raise RuntimeError("ranks finished at different steps")
+
+
+# ---------------------------------------------------------------- Ulysses
+# The alternative to the ring for head-rich configurations: two all-to-alls
+# turn sequence shards of every head into the whole sequence of a group of
+# heads, the single-GPU operator runs on it unchanged (positions 0..S-1, no
+# blockwise merging), and two all-to-alls turn the result back. Rank r takes
+# q-heads [r·Hq/N, (r+1)·Hq/N) and kv-heads [r·Hkv/N, (r+1)·Hkv/N): contiguous
+# head groups keep every GQA group (hq -> hq / G) on one rank. Needs Hq and
+# Hkv divisible by N. Bytes per rank per all-to-all: the rank's shard of the
+# tensor, (N-1)/N of it crossing NVLink; forward moves q, k, v and O, backward
+# dO, dq, dk, dv.
+class CudaAttentionOps:
+    """Whole-sequence attention on this rank's GPU through libbfa."""
+
+    def fwd(self, q, k, v, m: MaskArgs):
+        return _nfa.npu_flash_attention_forward(
+            q, k, v, causal=m.causal, sliding_window=m.sliding_window,
+            alibi_slope=m.alibi_slope, scale=m.scale, soft_cap=m.soft_cap, return_lse=True)
+
+    def bwd(self, q, k, v, o, lse, do, m: MaskArgs):
+        return _nfa.npu_flash_attention_backward(
+            q, k, v, o, lse, do, causal=m.causal, sliding_window=m.sliding_window,
+            alibi_slope=m.alibi_slope, scale=m.scale, soft_cap=m.soft_cap)
+
+
+def _h2s_send(x, world: int):
+    """[B, H, S/N, D] (this rank's rows, every head) -> the all-to-all input
+    [N, B, H/N, S/N, D]: entry j (head group j) goes to rank j."""
+    B, H, Sl, D = x.shape
+    return x.reshape(B, world, H // world, Sl, D).transpose(0, 1).contiguous()
+
+
+def _h2s_finish(recv, layout):
+    """All-to-all output (entry i: rank i's rows of this rank's head group)
+    -> [B, H/N, S, D], every row in sequence order."""
+    return layout.unshard(list(recv.unbind(0)), dim=2).contiguous()
+
+
+def _s2h_send(x, world: int, layout):
+    """[B, H/N, S, D] -> [N, B, H/N, S/N, D]: entry j holds rank j's rows."""
+    return torch.stack([layout.shard(x, j, dim=2) for j in range(world)], 0).contiguous()
+
+
+def _s2h_finish(recv):
+    """All-to-all output (entry j: this rank's rows of head group j)
+    -> [B, H, S/N, D]."""
+    N, B, Hg, Sl, D = recv.shape
+    return recv.transpose(0, 1).reshape(B, N * Hg, Sl, D).contiguous()
+
+
+def heads_to_sequence(x, world: int, layout, a2a):
+    """[B, H, S/N, D] (this rank's rows, every head) -> [B, H/N, S, D] (every
+    row, this rank's head group). ``a2a`` exchanges dim 0 of an [N, ...]
+    tensor: entry j goes to rank j, entry i of the result came from rank i."""
+    return _h2s_finish(a2a(_h2s_send(x, world)), layout)
+
+
+def sequence_to_heads(x, world: int, layout, a2a):
+    """Inverse of ``heads_to_sequence``: [B, H/N, S, D] -> [B, H, S/N, D]."""
+    return _s2h_finish(a2a(_s2h_send(x, world, layout)))
+
+
+def _ulysses_check(hq: int, hkv: int, world: int):
+    if hq % world or hkv % world:
+        raise ValueError(f"Ulysses needs heads_q ({hq}) and heads_kv ({hkv}) divisible by "
+                         f"the group size ({world}); use the ring (context_parallel_attention)")
+
+
+def _local_mask(m: MaskArgs, rank: int, hq: int, world: int) -> MaskArgs:
+    """The mask for this rank's q-head group (ALiBi slopes of those heads)."""
+    hg = hq // world
+    slopes = None if m.alibi_slope is None else m.alibi_slope[rank * hg:(rank + 1) * hg].contiguous()
+    return MaskArgs(m.causal, m.sliding_window, slopes, m.scale, m.soft_cap)
+
+
+def _dist_a2a(group):
+    import torch.distributed as dist
+
+    def a2a(send):
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=group)
+        return recv
+    return a2a
+
+
+class UlyssesFlexAttention(torch.autograd.Function):
+    """Autograd over Ulysses: inputs and outputs are this rank's sequence shard."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, causal, sliding_window, alibi_slope, scale, soft_cap, group, layout, ops):
+        import torch.distributed as dist
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        _ulysses_check(q.shape[1], k.shape[1], world)
+        lay = make_layout(layout, q.shape[2] * world, world)
+        a2a = _dist_a2a(group)
+        m = _local_mask(MaskArgs(causal, int(sliding_window), alibi_slope, scale, float(soft_cap)),
+                        rank, q.shape[1], world)
+        qf, kf, vf = (heads_to_sequence(t.contiguous(), world, lay, a2a) for t in (q, k, v))
+        of, lsef = ops.fwd(qf, kf, vf, m)
+        ctx.save_for_backward(qf, kf, vf, of, lsef)
+        ctx.m, ctx.world, ctx.lay, ctx.a2a, ctx.ops = m, world, lay, a2a, ops
+        return sequence_to_heads(of, world, lay, a2a)
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        qf, kf, vf, of, lsef = ctx.saved_tensors
+        world, lay, a2a = ctx.world, ctx.lay, ctx.a2a
+        dof = heads_to_sequence(grad_out.to(qf.dtype).contiguous(), world, lay, a2a)
+        dqf, dkf, dvf = ctx.ops.bwd(qf, kf, vf, of, lsef, dof, ctx.m)
+        grads = [sequence_to_heads(t, world, lay, a2a) for t in (dqf, dkf, dvf)]
+        return (*grads, None, None, None, None, None, None, None, None)
+
+
+def ulysses_attention(q, k, v, causal=False, sliding_window=0, alibi_slope=None, scale=None,
+                      soft_cap=0.0, group=None, layout="zigzag", _ops=None):
+    """Attention over a sequence sharded across the ranks of ``group`` by
+    head-sequence all-to-alls (Ulysses). q [B, Hq, S/N, D], k/v
+    [B, Hkv, S/N, D] are this rank's rows in ``layout`` ("zigzag", as for
+    context_parallel_attention, or "contiguous"); Hq and Hkv must be divisible
+    by N. Returns this rank's rows of O; differentiable. ``alibi_slope`` holds
+    all Hq slopes on every rank."""
+    return UlyssesFlexAttention.apply(q, k, v, causal, sliding_window, alibi_slope, scale, soft_cap,
+                                      group, layout, _ops or CudaAttentionOps())
+
+
+def ulysses_simulated(qs, ks, vs, dos, m: MaskArgs, ops, layout="zigzag"):
+    """Ulysses forward and backward for N simulated ranks in one process
+    (shards as lists, one entry per rank); the all-to-alls are in-memory.
+    Returns (o shards, dq shards, dk shards, dv shards)."""
+    world = len(qs)
+    _ulysses_check(qs[0].shape[1], ks[0].shape[1], world)
+    lay = make_layout(layout, qs[0].shape[2] * world, world)
+
+    def a2a_all(sends):  # recv_r[i] = send_i[r]
+        return [torch.stack([sends[i][r] for i in range(world)], 0) for r in range(world)]
+
+    def h2s(xs):
+        return [_h2s_finish(rv, lay) for rv in a2a_all([_h2s_send(x, world) for x in xs])]
+
+    def s2h(xs):
+        return [_s2h_finish(rv) for rv in a2a_all([_s2h_send(x, world, lay) for x in xs])]
+
+    qf, kf, vf, dof = (h2s(xs) for xs in (qs, ks, vs, dos))
+    masks = [_local_mask(m, r, qs[0].shape[1], world) for r in range(world)]
+    fw = [ops.fwd(qf[r], kf[r], vf[r], masks[r]) for r in range(world)]
+    o = s2h([f[0] for f in fw])
+    bw = [ops.bwd(qf[r], kf[r], vf[r], fw[r][0], fw[r][1], dof[r], masks[r]) for r in range(world)]
+    dq, dk, dv = (s2h([b[i] for b in bw]) for i in range(3))
+    return o, dq, dk, dv
 
 
 # ---------------------------------------------------------------- public API

@@ -1,9 +1,11 @@
-"""Context-parallel ring over NCCL, one process per GPU (run under torchrun).
+"""Context parallelism over NCCL, one process per GPU (run under torchrun).
 
-Each rank takes its zigzag shard of one long sequence, runs the ring forward
-and backward through the autograd entry point (context_parallel_attention),
-and rank 0 compares the gathered O, dQ, dK, dV with the single-GPU kernels on
-the whole sequence. Prints "cp ring ok" on success; exits non-zero otherwise.
+Each rank takes its zigzag shard of one long sequence, runs forward and
+backward through an autograd entry point -- the K/V ring
+(context_parallel_attention) by default, Ulysses (ulysses_attention) with the
+argument "ulysses" -- and rank 0 compares the gathered O, dQ, dK, dV with the
+single-GPU kernels on the whole sequence. Prints "cp ring ok" / "cp ulysses
+ok" on success; exits non-zero otherwise.
 """
 import os
 import sys
@@ -28,6 +30,8 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=dev)
+    mode = sys.argv[1] if len(sys.argv) > 1 else "ring"
+    attn = cp.ulysses_attention if mode == "ulysses" else cp.context_parallel_attention
     ok = True
     try:
         B, Hq, Hkv, S, D = 1, 8, 2, 2048, 128
@@ -40,7 +44,7 @@ def main():
         mask = dict(causal=True, alibi_slope=slopes)
         lay = cp.ZigzagLayout(S, world)
         qs, ks, vs = (lay.shard(t, rank).requires_grad_(True) for t in (q, k, v))
-        o = cp.context_parallel_attention(qs, ks, vs, **mask)
+        o = attn(qs, ks, vs, **mask)
         o.backward(lay.shard(go, rank))
         outs = [o.detach(), qs.grad, ks.grad, vs.grad]
         gathered = []
@@ -64,7 +68,7 @@ def main():
     finally:
         dist.destroy_process_group()
     if rank == 0 and ok:
-        print("cp ring ok")
+        print(f"cp {mode} ok")
     sys.exit(0 if ok else 1)
 
 

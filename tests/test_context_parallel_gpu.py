@@ -101,3 +101,37 @@ def test_ring_over_nccl_two_gpus():
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "cp ring ok" in r.stdout
+
+
+@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("case", ["causal", "alibi", "full_cap"])
+def test_simulated_ulysses_cuda_matches_single_gpu(world, case):
+    """Ulysses over simulated ranks with the CUDA ops: each rank runs the
+    single-GPU kernels on the whole sequence for its head group, so the
+    gathered O and gradients equal the single-GPU run on all heads."""
+    import npu_flash_attention as nfa
+    mask = CASES[case]
+    mask_dev = {**mask, **({"alibi_slope": mask["alibi_slope"].to(DEV)} if "alibi_slope" in mask else {})}
+    g = torch.Generator().manual_seed(10 + world)
+    B, Hq, Hkv, S, D = 1, 8, 4, 1024, 128
+    q, k, v = (torch.randn(B, h, S, D, generator=g).to(torch.bfloat16).to(DEV) for h in (Hq, Hkv, Hkv))
+    go = torch.randn(B, Hq, S, D, generator=g).to(torch.bfloat16).to(DEV)
+    lay = cp.ZigzagLayout(S, world)
+    sh = [[lay.shard(t, r) for r in range(world)] for t in (q, k, v, go)]
+    got = cp.ulysses_simulated(*sh, cp.MaskArgs(**mask_dev), cp.CudaAttentionOps())
+    o1, l1 = nfa.npu_flash_attention_forward(q, k, v, return_lse=True, **mask_dev)
+    ref = (o1, *nfa.npu_flash_attention_backward(q, k, v, o1, l1, go, **mask_dev))
+    torch.cuda.synchronize()
+    for name, shards, r in zip(("o", "dq", "dk", "dv"), got, ref):
+        assert _err(lay.unshard(shards), r.cpu()) < TOL, name
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ulysses_over_nccl_two_gpus():
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", "--nproc-per-node=2", "--master-addr", "127.0.0.1",
+           "--master-port", "29532", os.path.join(ROOT, "tests", "cp_ring_check.py"), "ulysses"]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "cp ulysses ok" in r.stdout
