@@ -25,7 +25,7 @@ bool sm100_bwd_fused_eligible(const Params& p, int dtype);
 int sm100_bwd_fused(const Params& p, int dtype, uint32_t* order, float* dq_acc, cudaStream_t st);
 
 // Split-KV decoding forward (decode.cu): the G q-heads of a KV head have at
-// most 16 query rows. decode_fwd returns a bfa_status, or -1 when it could not
+// most 64 query rows. decode_fwd returns a bfa_status, or -1 when it could not
 // run (the caller falls back to the regular forward).
 bool decode_eligible(const Params& p, int dtype);
 int decode_fwd(const Params& p, int dtype, cudaStream_t st);

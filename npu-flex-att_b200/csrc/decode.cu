@@ -7,11 +7,13 @@
 // flash_attn_fwd_reduce_kernel merges them with an LSE-weighted sum). There it
 // is never launched (and fixes B = 1). This is the working B200 version of that
 // path, chosen automatically by bfa_fwd when the G q-heads of a KV head
-// together have at most kMaxRows query rows.
+// together have at most kMaxRowsTotal (64) query rows.
 //
 // Decode is HBM-bound: every K/V byte is used by only G·Sq rows. So:
-//   - one CTA per (batch, KV head, key split) serves all G·Sq rows of that KV
-//     head, so K/V cross HBM once however large G is;
+//   - one CTA per (batch, KV head, key split, group of up to 16 rows) serves
+//     those rows of all G q-heads of that KV head, so K/V cross HBM once however
+//     large G is (the row groups of one KV head, up to 4, run side by side and
+//     share the K/V in L2);
 //   - K/V stream through a cp.async double buffer in 64-key chunks (rows
 //     padded by 16 bytes so the shared-memory reads are conflict-free);
 //   - for bf16 / fp16 the two small GEMMs (S = q·kᵀ and P·V, all rows in one
@@ -39,7 +41,8 @@ namespace {
 
 constexpr int kDecThreads = 256;
 constexpr int kChunk = 64;    // keys per pipeline stage
-constexpr int kMaxRows = 16;  // G·Sq rows per CTA
+constexpr int kMaxRows = 16;       // query rows per CTA (one row group)
+constexpr int kMaxRowsTotal = 64;  // G·Sq rows per KV head on this path (<= 4 row groups)
 constexpr int kRowGroupsS = kDecThreads / kChunk;  // row groups in the S phase
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
@@ -124,9 +127,14 @@ __global__ void __launch_bounds__(kDecThreads)
   float* row_a = row_l + kMaxRows;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int R = p.G * p.Sq;
-  const int split = (int)(blockIdx.x % n_split);
-  const int bkv = (int)(blockIdx.x / n_split);
+  // Block: (KV head, split, row group); the row group is the fastest index so
+  // that the CTAs of one KV head's row groups read the same K/V at once (L2).
+  const int n_rg = (p.G * p.Sq + kMaxRows - 1) / kMaxRows;
+  const int rg = (int)(blockIdx.x % n_rg);
+  const int row0 = rg * kMaxRows;  // this CTA's rows: row0 + [0, R)
+  const int R = min(kMaxRows, p.G * p.Sq - row0);
+  const int split = (int)((blockIdx.x / n_rg) % n_split);
+  const int bkv = (int)(blockIdx.x / n_rg / n_split);
   const int hkv = bkv % p.Hkv, b = bkv / p.Hkv;
   int klo, khi;
   key_range(p, 0, p.Sq, &klo, &khi);
@@ -164,7 +172,7 @@ __global__ void __launch_bounds__(kDecThreads)
     const int r = idx / D, d = idx - r * D;
     float x = 0.f;
     if (r < R) {
-      const int g = r / p.Sq, s = r - g * p.Sq;
+      const int g = (row0 + r) / p.Sq, s = (row0 + r) - g * p.Sq;
       const int hq = hkv * p.G + g;
       x = to_f32(qg[(int64_t)b * p.sq_[0] + (int64_t)hq * p.sq_[1] + (int64_t)s * p.sq_[2] + (int64_t)d * p.sq_[3]]) *
           qmul;
@@ -219,7 +227,7 @@ __global__ void __launch_bounds__(kDecThreads)
       for (int j = 0; j < RB / kRowGroupsS; ++j) {
         const int r = rgs + kRowGroupsS * j;
         if (r < R) {
-          const int g = r / p.Sq, s = r - g * p.Sq;
+          const int g = (row0 + r) / p.Sq, s = (row0 + r) - g * p.Sq;
           const int64_t gi = (int64_t)s + p.q_off, gj = (int64_t)key + p.k_off;
           const bool keep = key < ke && keep_pair(gi, gj, p.causal, p.window);
           float x = acc[j];
@@ -281,7 +289,7 @@ __global__ void __launch_bounds__(kDecThreads)
   for (int j = 0; j < RO; ++j) {
     const int r = rgo + L::kRowGroupsO * j;
     if (r < R) {
-      const int g = r / p.Sq, s = r - g * p.Sq;
+      const int g = (row0 + r) / p.Sq, s = (row0 + r) - g * p.Sq;
       const int64_t row = ((int64_t)b * p.Hq + hkv * p.G + g) * p.Sq + s;
       const float l = row_l[r];
       const float inv = (l > 0.f) ? 1.f / l : 0.f;
@@ -368,9 +376,14 @@ __global__ void __launch_bounds__(kDecThreads)
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
-  const int R = p.G * p.Sq;
-  const int split = (int)(blockIdx.x % n_split);
-  const int bkv = (int)(blockIdx.x / n_split);
+  // Block: (KV head, split, row group); the row group is the fastest index so
+  // that the CTAs of one KV head's row groups read the same K/V at once (L2).
+  const int n_rg = (p.G * p.Sq + kMaxRows - 1) / kMaxRows;
+  const int rg = (int)(blockIdx.x % n_rg);
+  const int row0 = rg * kMaxRows;  // this CTA's rows: row0 + [0, R)
+  const int R = min(kMaxRows, p.G * p.Sq - row0);
+  const int split = (int)((blockIdx.x / n_rg) % n_split);
+  const int bkv = (int)(blockIdx.x / n_rg / n_split);
   const int hkv = bkv % p.Hkv, b = bkv / p.Hkv;
   int klo, khi;
   key_range(p, 0, p.Sq, &klo, &khi);
@@ -409,7 +422,7 @@ __global__ void __launch_bounds__(kDecThreads)
     const uint16_t* qg = static_cast<const uint16_t*>(p.q);
     auto qpair = [&](int r, int c) -> uint32_t {
       if (r >= R) return 0u;
-      const int gg = r / p.Sq, s = r - gg * p.Sq;
+      const int gg = (row0 + r) / p.Sq, s = (row0 + r) - gg * p.Sq;
       const uint16_t* base = qg + (int64_t)b * p.sq_[0] + (int64_t)(hkv * p.G + gg) * p.sq_[1] + (int64_t)s * p.sq_[2];
       return (uint32_t)base[(int64_t)c * p.sq_[3]] | ((uint32_t)base[(int64_t)(c + 1) * p.sq_[3]] << 16);
     };
@@ -464,7 +477,7 @@ __global__ void __launch_bounds__(kDecThreads)
         const int n = 8 * warp + 2 * t + (e & 1);
         if (r < R) {
           const int key = kb + c * kChunk + n;
-          const int gg = r / p.Sq, s = r - gg * p.Sq;
+          const int gg = (row0 + r) / p.Sq, s = (row0 + r) - gg * p.Sq;
           const int64_t gi = (int64_t)s + p.q_off, gj = (int64_t)key + p.k_off;
           const bool keep = key < ke && keep_pair(gi, gj, p.causal, p.window);
           float x;
@@ -554,7 +567,7 @@ __global__ void __launch_bounds__(kDecThreads)
   for (int h = 0; h < 2; ++h) {
     const int r = g + 8 * h;
     if (r < R) {
-      const int gg = r / p.Sq, s = r - gg * p.Sq;
+      const int gg = (row0 + r) / p.Sq, s = (row0 + r) - gg * p.Sq;
       const int64_t row = ((int64_t)b * p.Hq + hkv * p.G + gg) * p.Sq + s;
       const float l = row_l[r];
       const float inv = (l > 0.f) ? 1.f / l : 0.f;
@@ -565,7 +578,7 @@ __global__ void __launch_bounds__(kDecThreads)
     }
   }
   if (tid < R) {
-    const int gg = tid / p.Sq, s = tid - gg * p.Sq;
+    const int gg = (row0 + tid) / p.Sq, s = (row0 + tid) - gg * p.Sq;
     const int64_t row = ((int64_t)b * p.Hq + hkv * p.G + gg) * p.Sq + s;
     const float l = row_l[tid];
     part_lse[row * n_split + split] = (l > 0.f) ? (row_m[tid] + __log2f(l)) * kLn2 : neg_inf();
@@ -679,7 +692,8 @@ int launch_decode(const Params& p, cudaStream_t st) {
     khi = (int)h;
   }
   const bool plain = !(p.soft_cap > 0.f) && p.alibi == nullptr;
-  const int R = p.G * p.Sq;
+  const int n_rg = (p.G * p.Sq + kMaxRows - 1) / kMaxRows;  // row groups of <= 16 rows
+  const int R = std::min(p.G * p.Sq, kMaxRows);             // rows of the largest group
   using Kern = void (*)(const Params, int, int, int, float*, float*);
   Kern kern;
   int smem_bytes;
@@ -704,7 +718,7 @@ int launch_decode(const Params& p, cudaStream_t st) {
     per_sm = 1;
   }
 
-  const int kv_heads = p.B * p.Hkv;
+  const int kv_heads = p.B * p.Hkv * n_rg;  // (KV head, row group) pairs
   const int vis = khi - klo;
   // One wave: as many splits as fill the resident CTA slots, each split a
   // long run of keys (the per-CTA start-up, pipeline fill and merge input grow
@@ -774,7 +788,7 @@ bool decode_eligible(const Params& p, int dtype) {
   if (!decode_enabled()) return false;
   if (dtype != BFA_DTYPE_BF16 && dtype != BFA_DTYPE_F16 && dtype != BFA_DTYPE_F32) return false;
   if (p.D != 64 && p.D != 128 && !(p.D == 256 && dtype != BFA_DTYPE_F32)) return false;
-  if (p.G * p.Sq > kMaxRows || p.Sq < 1 || p.Sk < 1 || p.B < 1 || p.Hkv < 1) return false;
+  if (p.G * p.Sq > kMaxRowsTotal || p.Sq < 1 || p.Sk < 1 || p.B < 1 || p.Hkv < 1) return false;
   // K/V rows are copied in 16-byte pieces: unit stride along D, 16-byte
   // aligned bases and row / head / batch strides.
   const int64_t es = dtype == BFA_DTYPE_F32 ? 4 : 2;

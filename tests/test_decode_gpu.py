@@ -1,8 +1,9 @@
 """GPU parity of the split-KV decoding forward (csrc/decode.cu).
 
-bfa_fwd takes this path when the G q-heads of a KV head have at most 16 query
-rows together (G·Sq <= 16). It is the working form of the reference's unused
-split-KV forward + reduce (npu_flash_attention.py:171-293). Each case checks
+bfa_fwd takes this path when the G q-heads of a KV head have at most 64 query
+rows together (G·Sq <= 64; one CTA per group of up to 16 rows). It is the
+working form of the reference's unused split-KV forward + reduce
+(npu_flash_attention.py:171-293). Each case checks
 the decode result against the CPU oracle with the forward tolerances of
 test_parity_gpu.py (fp32 1e-4, fp16 1e-2, bf16 2e-2; LSE 1e-3 relative) and
 against the regular path run on the same inputs (BFA_FWD_DECODE=0), and that
@@ -23,10 +24,13 @@ pytestmark = pytest.mark.gpu
 # (b, hq, hkv, sq, sk, d)
 SHAPES = [
     (2, 8, 2, 1, 3000, 128),  # G = 4, one query per head, long key sequence
-    (1, 16, 2, 2, 4096, 128),  # G = 8, 16 rows: the row limit
+    (1, 16, 2, 2, 4096, 128),  # G = 8, 16 rows: one full row group
     (3, 4, 4, 4, 1000, 64),  # MHA, 4 queries
     (1, 4, 1, 3, 777, 256),  # D = 256, key count not a multiple of the chunk
     (2, 2, 2, 1, 65, 128),  # one full 64-key chunk + 1 key
+    (1, 32, 4, 4, 2048, 128),  # G = 8, 4 queries: 32 rows, two row groups
+    (1, 8, 1, 5, 999, 128),  # G = 8, 5 queries: 40 rows, a ragged third row group
+    (2, 16, 2, 8, 1500, 64),  # G = 8, 8 queries: 64 rows, the limit (four row groups)
 ]
 
 MASKS = {
@@ -93,15 +97,15 @@ def test_decode_bf16(shape, mask_name):
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.float32], ids=["f16", "f32"])
-@pytest.mark.parametrize("shape", SHAPES[:3], ids=lambda s: "b{}h{}k{}q{}s{}d{}".format(*s))
+@pytest.mark.parametrize("shape", SHAPES[:3] + SHAPES[6:7], ids=lambda s: "b{}h{}k{}q{}s{}d{}".format(*s))
 def test_decode_dtypes(shape, dtype):
     _check(shape, dtype, "none", seed=1)
     _check(shape, dtype, "causal_end", seed=2)
 
 
 def test_decode_not_taken_for_many_rows():
-    # G·Sq > 16 goes to the regular tcgen05 forward (one launch).
-    q, k, v, _ = _inputs(5, 1, 8, 2, 8, 512, 128, torch.bfloat16)
+    # G·Sq > 64 goes to the regular tcgen05 forward (one launch).
+    q, k, v, _ = _inputs(5, 1, 8, 2, 20, 512, 128, torch.bfloat16)
     qd, kd, vd = (t.to(DEV) for t in (q, k, v))
     _, _, launches = _run(qd, kd, vd, {}, decode=True)
     assert launches == 1
