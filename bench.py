@@ -10,12 +10,17 @@ kernel is timed on its own). FLOPs count only unmasked (i, j) pairs,
 element-exact: 4·D per pair forward, 10·D backward.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload c3|c2|c4|c4t|c5|c5u|decode]
 
 N > 1 is launched with torchrun (one process per GPU); each rank runs its own
 batch shard (weak scaling, no collective on the data path); the step time is
-the max over ranks. `--impl reference` times the reference's math path on the
-host CPU cores (the CPU restatement in oracle/; the reference itself is
-Triton for Ascend NPUs and has no GPU or CPU build that runs here).
+the max over ranks and `value` is the aggregate over all ranks (`value_is`
+says so; `per_gpu_value` is value / N). The c3 line also carries `cp`: config
+5 through the context-parallel K/V ring and through Ulysses on the same N
+GPUs, beside the same problem run whole on each GPU alone. `--impl reference`
+times the reference's math path on the host CPU cores (the CPU restatement in
+oracle/; the reference itself is Triton for Ascend NPUs and has no GPU or CPU
+build that runs here).
 """
 from __future__ import annotations
 
@@ -36,17 +41,37 @@ sys.path.insert(0, ROOT)
 import torch  # noqa: E402
 
 METRIC = "fwd+bwd attention TFLOPS/GPU (unmasked FLOPs) and % of bf16 tensor peak"
-CFG = dict(B=4, Hq=32, Hkv=8, S=4096, D=128, causal=True)
+CFG = dict(B=4, Hq=32, Hkv=8, S=4096, D=128, causal=True, window=0, soft_cap=0.0)
 WORKLOAD = "c3: bf16 GQA B=4/GPU Hq=32 Hkv=8 D=128 S=4096 causal fwd+bwd"
+# Config 4 (Gemma2-style): D=256, causal + window 4096 + soft-cap 50; c4t is
+# the second run at S=8190, a key length that is not a tile multiple.
+CFG_C4 = dict(B=2, Hq=16, Hkv=8, S=8192, D=256, causal=True, window=4096, soft_cap=50.0)
+CFG_C4T = dict(CFG_C4, S=8190)
+WORKLOADS = {
+    "c3": (CFG, WORKLOAD),
+    "c4": (CFG_C4, "c4: bf16 Gemma2-style B=2/GPU Hq=16 Hkv=8 D=256 S=8192 causal + window 4096 + "
+                   "soft-cap 50 fwd+bwd"),
+    "c4t": (CFG_C4T, "c4: bf16 Gemma2-style B=2/GPU Hq=16 Hkv=8 D=256 S=8190 (key tail not a tile "
+                     "multiple) causal + window 4096 + soft-cap 50 fwd+bwd"),
+}
 
 
 def causal_pairs(s: int) -> int:
     return s * (s + 1) // 2
 
 
+def pairs_per_head(cfg) -> int:
+    """Element-exact kept (i, j) pairs of one head (causal, optional window)."""
+    s, w = cfg["S"], cfg.get("window", 0)
+    if not cfg.get("causal", True):
+        raise ValueError("bench workloads are causal")
+    if w <= 0 or w >= s - 1:
+        return causal_pairs(s)
+    return causal_pairs(w + 1) - (w + 1) + (s - w) * (w + 1)
+
+
 def step_flops(cfg=CFG) -> float:
-    pairs = causal_pairs(cfg["S"]) * cfg["B"] * cfg["Hq"]
-    return 14.0 * cfg["D"] * pairs
+    return 14.0 * cfg["D"] * pairs_per_head(cfg) * cfg["B"] * cfg["Hq"]
 
 
 def peaks():
@@ -59,11 +84,11 @@ def peaks():
         return 1590.0, 6650.0, "fallback"
 
 
-def committed_traffic(phase: str):
+def committed_traffic(phase: str, workload: str = "c3"):
     """DRAM bytes per launch of a kernel from the committed ncu capture, or None."""
     kernel = {"fwd": "fwd_kernel", "dkdv": "dkdv_kernel", "dq": "dq_kernel"}.get(phase)
     try:
-        with open(os.path.join(ROOT, "profiles", "c3_dram_traffic.json")) as f:
+        with open(os.path.join(ROOT, "profiles", f"{workload}_dram_traffic.json")) as f:
             return json.load(f)["kernels"][kernel]["dram_bytes_per_launch"]
     except Exception:
         return None
@@ -130,7 +155,6 @@ class ClockSampler:
 
 
 def make_inputs(seed, device, cfg=CFG):
-    g = torch.Generator().manual_seed(seed)
     B, Hq, Hkv, S, D = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["S"], cfg["D"]
     # Generated on the device from a seeded generator (the full tensors are GBs).
     gd = torch.Generator(device=device).manual_seed(seed)
@@ -138,87 +162,115 @@ def make_inputs(seed, device, cfg=CFG):
     k = torch.randn(B, Hkv, S, D, generator=gd, device=device, dtype=torch.bfloat16)
     v = torch.randn(B, Hkv, S, D, generator=gd, device=device, dtype=torch.bfloat16)
     do = torch.randn(B, Hq, S, D, generator=gd, device=device, dtype=torch.bfloat16)
-    del g
     return q, k, v, do
 
 
-def cpu_baseline_sample(budget_s: float = 15.0):
+def cpu_baseline_sample(budget_s: float = 15.0, cfg=CFG):
     """The reference's math path (oracle restatement) on the host cores.
 
-    Times fwd+bwd of single (b, q-head) slices of the workload (S=4096,
-    D=128, causal, fp32) until ~budget_s seconds of CPU work, and scales FLOPs
-    per slice; returns (TFLOPS, threads, slices)."""
+    Times fwd+bwd of single (b, q-head) slices of the workload (fp32, the
+    workload's S, D and mask) until ~budget_s seconds of CPU work, and scales
+    FLOPs per slice; returns (TFLOPS, threads, slices, seconds)."""
     from oracle.attention_math import attention_backward, attention_forward
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     g = torch.Generator().manual_seed(0)
-    S, D = CFG["S"], CFG["D"]
+    S, D = cfg["S"], cfg["D"]
+    mask = dict(causal=True, sliding_window=cfg.get("window", 0), soft_cap=cfg.get("soft_cap", 0.0))
     q, k, v, do = (torch.randn(1, 1, S, D, generator=g) for _ in range(4))
-    slice_flops = 14.0 * D * causal_pairs(S)
-    attention_forward(q[:, :, :256], k[:, :, :256], v[:, :, :256], causal=True, dtype=torch.float32)
+    slice_flops = 14.0 * D * pairs_per_head(cfg)
+    attention_forward(q[:, :, :256], k[:, :, :256], v[:, :, :256], dtype=torch.float32, **mask)
     t0 = time.perf_counter()
     n = 0
     while True:
-        o, lse = attention_forward(q, k, v, causal=True, dtype=torch.float32)
-        attention_backward(q, k, v, do, causal=True, out=o, lse=lse, dtype=torch.float32)
+        o, lse = attention_forward(q, k, v, dtype=torch.float32, **mask)
+        attention_backward(q, k, v, do, out=o, lse=lse, dtype=torch.float32, **mask)
         n += 1
         if time.perf_counter() - t0 > budget_s:
             break
     dt = time.perf_counter() - t0
-    return n * slice_flops / dt / 1e12, threads, n
+    return n * slice_flops / dt / 1e12, threads, n, dt
 
 
 def run_reference(args):
+    """The reference's CPU math path on the workload's own config, timed per
+    step: a step is a bounded sample of whole (b, q-head) slices (fwd+bwd,
+    fp32, all host threads) taking about `--ref-step-s` seconds. `ms_per_step`
+    is the wall time each of those steps took; the time a whole step of the
+    workload (every slice) would take at the measured rate is reported apart,
+    as `extrapolated_full_step_ms`."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
+    cfg, workload = WORKLOADS.get(args.workload, (CFG, WORKLOAD))
     threads = os.cpu_count() or 1
-    per_step = []
-    tflops_all = []
+    tflops_all, wall_ms, slices = [], [], []
     for i in range(args.warmup + args.steps):
-        tf, threads, n = cpu_baseline_sample(budget_s=2.0)
+        budget = args.ref_step_s if i >= args.warmup else min(args.ref_step_s, 0.3)
+        tf, threads, n, dt = cpu_baseline_sample(budget_s=budget, cfg=cfg)
         if i >= args.warmup:
             tflops_all.append(tf)
-            per_step.append(n)
+            wall_ms.append(dt * 1e3)
+            slices.append(n)
     value = statistics.median(tflops_all)
-    ms = step_flops() / (value * 1e12) * 1e3
+    full_ms = step_flops(cfg) / (value * 1e12) * 1e3
+    n_slices = cfg["B"] * cfg["Hq"]
+    sample = (f"per step: fwd+bwd of whole (b, q-head) slices of the workload (S={cfg['S']}, "
+              f"D={cfg['D']}, causal" + (f", window {cfg['window']}" if cfg.get("window") else "")
+              + (f", soft-cap {cfg['soft_cap']:g}" if cfg.get("soft_cap") else "")
+              + f", fp32) for ~{args.ref_step_s:g} s (median {statistics.median(slices)} of the "
+              f"step's {n_slices} slices); TFLOPS scale per slice")
     out = {
         "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": "TFLOPS",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(statistics.mean(wall_ms), 3),
+        "ms_per_step_is": "wall time of each timed step, i.e. of its bounded sample of slices",
+        "extrapolated_full_step_ms": round(full_ms, 3),
+        "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
-        "config": {"workload": WORKLOAD, "global_batch": CFG["B"] * args.gpus, "seq_len": CFG["S"],
-                   "parallelism": "host CPU, all cores"},
+        "config": {"workload": workload, "global_batch": cfg["B"] * args.gpus, "seq_len": cfg["S"],
+                   "parallelism": "host CPU, all cores, rank 0 only"},
         "cpu_baseline": {"value": round(value, 6), "unit": "TFLOPS", "cores": threads,
-                         "kind": "port",
-                         "sample": "per step: fwd+bwd of whole (b, q-head) slices of the workload "
-                                   "(S=4096, D=128, causal, fp32) for ~2 s; TFLOPS scale per slice"},
+                         "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 6), "unit": "TFLOPS", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out), flush=True)
 
 
+def init_dist(dev, world):
+    """NCCL process group over the ranks of this node (no-op for one rank)."""
+    if world > 1 and not torch.distributed.is_initialized():
+        import datetime
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=dev)
+
+
+def max_over_ranks(x: float, dev, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
 def run_ours(args):
     import bfa_lib
     import npu_flash_attention as nfa
 
+    cfg, workload = WORKLOADS[args.workload]
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                             device_id=dev)
+    init_dist(dev, world)
     lib = bfa_lib.load()
-    q, k, v, do = make_inputs(1234 + rank, dev)
-    B, Hq, Hkv, S, D = CFG["B"], CFG["Hq"], CFG["Hkv"], CFG["S"], CFG["D"]
-    o = torch.empty_like(q)
-    lse = torch.empty(B, Hq, S, device=dev, dtype=torch.float32)
+    q, k, v, do = make_inputs(1234 + rank, dev, cfg)
+    B, Hq, Hkv, S, D = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["S"], cfg["D"]
     grads = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v))
-    pr = nfa._problem(q, k, True, 0, None, 1.0 / math.sqrt(D), 0.0)
+    kw = dict(causal=True, sliding_window=cfg.get("window", 0), soft_cap=cfg.get("soft_cap", 0.0))
+    pr = nfa._problem(q, k, True, kw["sliding_window"], None, 1.0 / math.sqrt(D), kw["soft_cap"])
     ws = torch.empty(lib.bfa_bwd_workspace_bytes(pr), dtype=torch.uint8, device=dev)
-    kw = dict(causal=True)
 
     def step(ev=None):
         if ev:
@@ -264,53 +316,60 @@ def run_ours(args):
         torch.distributed.barrier()
     clocks = sampler.stop()
     nfa.check_device_status(dev)
-    total_ms = start.elapsed_time(end)
+    total_ms = max_over_ranks(start.elapsed_time(end), dev, world)
     phase_ms = [sum(events[i][j].elapsed_time(events[i][j + 1]) for i in range(args.steps)) / args.steps
                 for j in range(4)]
-    if world > 1:
-        t = torch.tensor([total_ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        total_ms = float(t.item())
     ms_step = total_ms / args.steps
-    flops = step_flops()
+    flops = step_flops(cfg)
     value = world * flops / (ms_step * 1e-3) / 1e12
+    del q, k, v, do, grads, ws
 
     # ---- e2e: public autograd API, host (pinned) buffers, copies inside the timed region
-    e2e = None if args.profile else run_e2e(nfa, dev, args, world)
+    e2e = None if args.profile else run_e2e(nfa, dev, args, world, cfg)
+    # ---- context parallelism (config 5) on the same GPUs
+    cp = run_cp(args, dev, rank, world) if (args.workload == "c3" and not (args.profile or args.no_cp)) else None
 
     peak_tf, _, peak_kind = peaks()
-    pairs = causal_pairs(S) * B * Hq
+    pairs = pairs_per_head(cfg) * B * Hq
     kern_flops = {"fwd": 4.0 * D * pairs, "delta": 0.0, "dkdv": 8.0 * D * pairs, "dq": 6.0 * D * pairs}
     names = ["fwd", "delta", "dkdv", "dq"]
     dom = max(range(4), key=lambda j: phase_ms[j])
     achieved = kern_flops[names[dom]] / (phase_ms[dom] * 1e-3) / 1e12
+    kernel_frac = {n: round(kern_flops[n] / (phase_ms[j] * 1e-3) / 1e12 / peak_tf, 4)
+                   for j, n in enumerate(names) if kern_flops[n] > 0}
     roofline = {"bound": "tensor", "kernel": names[dom], "achieved": round(achieved, 2),
                 "peak": peak_tf, "unit": "TFLOP/s", "frac": round(achieved / peak_tf, 4),
                 "peak_kind": f"bf16 dense burst, {peak_kind}",
-                "traffic": committed_traffic(names[dom]),
-                "traffic_unit": "DRAM bytes per launch (ncu capture, profiles/c3_dram_traffic.json)",
+                "traffic": committed_traffic(names[dom], args.workload),
+                "traffic_unit": f"DRAM bytes per launch (ncu capture, profiles/{args.workload}_dram_traffic.json)",
                 "algorithmic_flop_per_launch": kern_flops[names[dom]],
-                "phase_ms": {n: round(x, 4) for n, x in zip(names, phase_ms)}}
+                "phase_ms": {n: round(x, 4) for n, x in zip(names, phase_ms)},
+                "kernel_frac_of_peak": kernel_frac}
     cpu = None
     if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.profile):
-        tf, threads, n = cpu_baseline_sample(budget_s=args.cpu_budget)
+        tf, threads, n, dt = cpu_baseline_sample(budget_s=args.cpu_budget, cfg=cfg)
         cpu = {"value": round(tf, 6), "unit": "TFLOPS", "cores": threads, "kind": "port",
-               "sample": f"{n} whole (b, q-head) slices of the workload (S=4096, D=128, causal, "
-                         f"fp32 fwd+bwd) in ~{args.cpu_budget:.0f} s; TFLOPS scale per slice"}
+               "sample": f"{n} whole (b, q-head) slices of the workload (S={S}, D={D}, same mask, "
+                         f"fp32 fwd+bwd) in {dt:.1f} s; TFLOPS scale per slice"}
     if rank == 0:
+        l2 = ("inputs larger than L2 (q {:.0f} MB, dO {:.0f} MB, k/v {:.0f} MB each)".format(
+            B * Hq * S * D * 2 / 1e6, B * Hq * S * D * 2 / 1e6, B * Hkv * S * D * 2 / 1e6))
         out = {
             "metric": METRIC, "value": round(value, 3), "unit": "TFLOPS", "n_gpus": world,
+            "value_is": f"aggregate over the {world} GPU(s) (sum of per-GPU TFLOPS)",
+            "per_gpu_value": round(value / world, 3),
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1), generated on device)",
-            "config": {"workload": WORKLOAD, "global_batch": B * world, "seq_len": S,
+            "config": {"workload": workload, "global_batch": B * world, "seq_len": S,
                        "parallelism": f"batch x head shards on {world} GPU(s), no collective",
-                       "l2": "inputs larger than L2 (q 268 MB, dO 268 MB, k/v 67 MB each)"},
+                       "l2": l2},
             "pct_of_peak": round(100.0 * value / world / peak_tf, 2),
             "gpu_launches": int(launches),
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,
+            "cp": cp,
             "clocks": clocks,
         }
         print(json.dumps(out), flush=True)
@@ -319,7 +378,7 @@ def run_ours(args):
         torch.distributed.destroy_process_group()
 
 
-def run_e2e(nfa, dev, args, world):
+def run_e2e(nfa, dev, args, world, cfg=CFG):
     """Same metric through the public autograd API with host buffers: every
     step copies q, k, v, dO from pinned host memory, runs flex_attention
     forward + backward, and reads dQ, dK, dV back to pinned host memory.
@@ -329,8 +388,10 @@ def run_e2e(nfa, dev, args, world):
     buffers) and step i-1's gradients are copied out on another while step i
     computes, so the two PCIe directions overlap each other and the kernels.
     The timed region holds every step's copies, from the first input copy to
-    the last gradient read-back."""
-    B, Hq, Hkv, S, D = CFG["B"], CFG["Hq"], CFG["Hkv"], CFG["S"], CFG["D"]
+    the last gradient read-back, for the same number of steps as the
+    device-timed run."""
+    B, Hq, Hkv, S, D = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["S"], cfg["D"]
+    mask = dict(causal=True, sliding_window=cfg.get("window", 0), soft_cap=cfg.get("soft_cap", 0.0))
     shapes = [(B, Hq, S, D), (B, Hkv, S, D), (B, Hkv, S, D), (B, Hq, S, D)]
     host_in = [torch.randn(*s, dtype=torch.float32).to(torch.bfloat16).pin_memory() for s in shapes]
     host_out = [torch.empty(*s, dtype=torch.bfloat16).pin_memory() for s in shapes[:3]]
@@ -361,7 +422,7 @@ def run_e2e(nfa, dev, args, world):
             comp.wait_event(ev_in[b_])
             qd, kd, vd, dod = bufs[b_]
             qd, kd, vd = (t.detach().requires_grad_(True) for t in (qd, kd, vd))
-            out = nfa.flex_attention(qd, kd, vd, causal=True)
+            out = nfa.flex_attention(qd, kd, vd, **mask)
             out.backward(dod)
             ev_used[b_].record(comp)
             grads = (qd.grad, kd.grad, vd.grad)
@@ -374,7 +435,7 @@ def run_e2e(nfa, dev, args, world):
         done.record(s_out)
         return done
 
-    steps = max(2, min(args.steps, 5))
+    steps = max(2, args.steps)
     run(2)
     torch.cuda.synchronize()
     if world > 1:
@@ -385,12 +446,9 @@ def run_e2e(nfa, dev, args, world):
     s_in.wait_event(done)
     e.record(s_in)
     torch.cuda.synchronize()
-    ms = s.elapsed_time(e) / steps
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
-    return {"value": round(world * step_flops() / (ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
+    ms = max_over_ranks(s.elapsed_time(e) / steps, dev, world)
+    return {"value": round(world * step_flops(cfg) / (ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
+            "value_is": f"aggregate over the {world} GPU(s)",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 3),
             "steps": steps, "pipelined": "H2D of step i+1 and D2H of step i-1 overlap step i"}
 
@@ -401,59 +459,97 @@ C5U_WORKLOAD = ("c5: bf16 B=1 Hq=64 Hkv=8 D=128 S=65536 causal + ALiBi, context-
                 "(head-sequence all-to-alls)")
 
 
-def run_c5(args, ulysses=False):
-    """Config 5 through context parallelism (one process per GPU): each rank
-    holds its zigzag shard (2 chunks of S/(2N) rows) of Q, K, V and runs
-    forward + backward with context_parallel_attention (the K/V ring) or, for
-    --workload c5u, ulysses_attention. FLOPs count the unmasked pairs of the
-    whole causal sequence (14·D per pair per q-head)."""
-    import datetime
+def c5_flops():
+    return 14.0 * C5["D"] * causal_pairs(C5["S"]) * C5["B"] * C5["Hq"]
+
+
+def time_c5(mode, dev, rank, world, steps, warmup):
+    """ms per fwd+bwd step of config 5, max over ranks. `mode` "ring" and
+    "ulysses" shard the sequence over the ranks (each holds its zigzag shard,
+    2 chunks of S/(2N) rows); "single" runs the whole problem on every GPU
+    alone, at the same time, with no communication."""
     import context_parallel as cp
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-    os.environ.setdefault("MASTER_PORT", "29517")
-    torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev,
-                                         rank=rank, world_size=world)
+    import npu_flash_attention as nfa
     B, Hq, Hkv, S, D = C5["B"], C5["Hq"], C5["Hkv"], C5["S"], C5["D"]
-    rows = S // world
+    rows = S if mode == "single" else S // world
     gd = torch.Generator(device=dev).manual_seed(4321 + rank)
     q = torch.randn(B, Hq, rows, D, generator=gd, device=dev, dtype=torch.bfloat16).requires_grad_(True)
     k = torch.randn(B, Hkv, rows, D, generator=gd, device=dev, dtype=torch.bfloat16).requires_grad_(True)
     v = torch.randn(B, Hkv, rows, D, generator=gd, device=dev, dtype=torch.bfloat16).requires_grad_(True)
     do = torch.randn(B, Hq, rows, D, generator=gd, device=dev, dtype=torch.bfloat16)
     slopes = torch.tensor([2.0 ** (-8.0 * (i + 1) / Hq) for i in range(Hq)], device=dev)
+    attn = {"ring": cp.context_parallel_attention, "ulysses": cp.ulysses_attention,
+            "single": nfa.npu_flex_attention}[mode]
 
     def step():
         q.grad = k.grad = v.grad = None
-        attn = cp.ulysses_attention if ulysses else cp.context_parallel_attention
         o = attn(q, k, v, causal=True, alibi_slope=slopes)
         o.backward(do)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
-    torch.distributed.barrier()
+    if world > 1:
+        torch.distributed.barrier()
     s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s_.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         step()
     e_.record()
     torch.cuda.synchronize()
-    t = torch.tensor([s_.elapsed_time(e_) / args.steps], device=dev)
-    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms = float(t.item())
-    flops = 14.0 * D * causal_pairs(S) * B * Hq
+    ms = max_over_ranks(s_.elapsed_time(e_) / steps, dev, world)
+    del q, k, v, do
+    torch.cuda.empty_cache()
+    return ms
+
+
+def run_cp(args, dev, rank, world):
+    """Config 5 through context parallelism on the bench's N GPUs, for the
+    `cp` key of the c3 line: the K/V ring, Ulysses (when the head counts
+    divide by N), and the whole problem on each GPU alone as the N=1 base of
+    the strong-scaling efficiency single_ms / (N * ms)."""
+    steps = max(1, min(args.steps, args.cp_steps))
+    warmup = min(args.warmup, 2)
+    flops = c5_flops()
+    res = {"workload": "c5: bf16 B=1 Hq=64 Hkv=8 D=128 S=65536 causal + ALiBi, fwd+bwd, "
+                       "strong scaling over the bench's GPUs",
+           "steps": steps, "warmup": warmup}
+    single = time_c5("single", dev, rank, world, steps, warmup)
+    res["single_gpu"] = {"ms_per_step": round(single, 3), "tflops": round(flops / (single * 1e-3) / 1e12, 1)}
+    modes = [] if world == 1 else ["ring"] + (["ulysses"] if C5["Hkv"] % world == 0 else [])
+    for mode in modes:
+        ms = time_c5(mode, dev, rank, world, steps, warmup)
+        res[mode] = {"ms_per_step": round(ms, 3), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+                     "eff_vs_single_gpu": round(single / (world * ms), 4)}
+    return res
+
+
+def run_c5(args, ulysses=False):
+    """Config 5 through context parallelism (one process per GPU): each rank
+    holds its zigzag shard (2 chunks of S/(2N) rows) of Q, K, V and runs
+    forward + backward with context_parallel_attention (the K/V ring) or, for
+    --workload c5u, ulysses_attention. FLOPs count the unmasked pairs of the
+    whole causal sequence (14·D per pair per q-head)."""
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import datetime
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29517")
+    torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev,
+                                         rank=rank, world_size=world)
+    ms = time_c5("ulysses" if ulysses else "ring", dev, rank, world, args.steps, args.warmup)
     peak_tf, _, peak_kind = peaks()
     if rank == 0:
-        value = flops / (ms * 1e-3) / 1e12
+        value = c5_flops() / (ms * 1e-3) / 1e12
         print(json.dumps({
             "metric": METRIC, "value": round(value, 3), "unit": "TFLOPS", "n_gpus": world,
+            "value_is": f"aggregate over the {world} GPU(s)",
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1), generated on device)",
-            "config": {"workload": C5U_WORKLOAD if ulysses else C5_WORKLOAD, "global_batch": B, "seq_len": S,
+            "config": {"workload": C5U_WORKLOAD if ulysses else C5_WORKLOAD, "global_batch": C5["B"],
+                       "seq_len": C5["S"],
                        "parallelism": (f"Ulysses all-to-alls over {world} GPU(s), NCCL" if ulysses else
                                        f"context-parallel zigzag K/V ring over {world} GPU(s), NCCL")},
             "pct_of_peak": round(100.0 * value / world / peak_tf, 2),
@@ -463,6 +559,77 @@ def run_c5(args, ulysses=False):
             flush=True)
     torch.distributed.barrier()
     torch.distributed.destroy_process_group()
+
+
+# Config 2 and the reference's published 910B3 latencies for it (fp16 causal
+# B1 H2 D64, no window): RESULT.md:180-184 (forward) and :200-204 (backward).
+C2_S = (128, 512, 1024, 2048)
+C2_910B3_MS = {128: (0.325, 1.371), 512: (0.979, 3.265), 1024: (1.547, 4.240), 2048: (2.262, 9.269)}
+
+
+def run_c2(args):
+    """Config 2: fp16 B1 H2 D64 causal, S in {128, 512, 1024, 2048}, with and
+    without window 64. Latency-bound, so each case is timed per call: forward
+    and backward separately, CUDA events around each call, L2 flushed (a
+    256 MB write) before every call, median over the reps. The reference's
+    published Ascend 910B3 latencies for the unwindowed cases stand beside
+    them as context, not as a target."""
+    import bfa_lib
+    import npu_flash_attention as nfa
+    _, _, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    lib = bfa_lib.load()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    reps = max(args.steps, 30)
+    cases = []
+    launches = 0
+    for w in (0, 64):
+        for S in C2_S:
+            g = torch.Generator(device=dev).manual_seed(S + w)
+            q, k, v, do = (torch.randn(1, 2, S, 64, generator=g, device=dev, dtype=torch.float16)
+                           for _ in range(4))
+            kw = dict(causal=True, sliding_window=w)
+            f_ms, b_ms = [], []
+            for i in range(args.warmup + reps):
+                flush.fill_(i & 255)
+                e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+                n0 = lib.bfa_launch_count()
+                e[0].record()
+                o, lse = nfa.npu_flash_attention_forward(q, k, v, return_lse=True, **kw)
+                e[1].record()
+                flush.fill_((i + 1) & 255)
+                e[2].record()
+                nfa.npu_flash_attention_backward(q, k, v, o, lse, do, **kw)
+                e3 = torch.cuda.Event(enable_timing=True)
+                e3.record()
+                torch.cuda.synchronize()
+                if i >= args.warmup:
+                    f_ms.append(e[0].elapsed_time(e[1]))
+                    b_ms.append(e[2].elapsed_time(e3))
+                    launches += lib.bfa_launch_count() - n0
+            nfa.check_device_status(dev)
+            pairs = pairs_per_head(dict(S=S, window=w, causal=True)) * 2
+            fm, bm = statistics.median(f_ms), statistics.median(b_ms)
+            case = {"S": S, "window": w, "fwd_ms": round(fm, 4), "bwd_ms": round(bm, 4),
+                    "fwd_bwd_tflops": round(14.0 * 64 * pairs / ((fm + bm) * 1e-3) / 1e12, 3)}
+            if w == 0:
+                case["ascend_910b3_ms"] = {"fwd": C2_910B3_MS[S][0], "bwd": C2_910B3_MS[S][1],
+                                           "source": "reference RESULT.md:180-184, 200-204"}
+            cases.append(case)
+    head = next(c for c in cases if c["S"] == 2048 and c["window"] == 0)
+    print(json.dumps({
+        "metric": METRIC, "value": head["fwd_bwd_tflops"], "unit": "TFLOPS", "n_gpus": 1,
+        "value_is": "fwd+bwd TFLOPS of the S=2048 unwindowed case (sum of its median fwd and bwd latencies)",
+        "steps": reps, "warmup": args.warmup, "ms_per_step": round(head["fwd_ms"] + head["bwd_ms"], 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded N(0,1), generated on device)",
+        "config": {"workload": "c2: fp16 B=1 H=2 D=64 causal, S in {128,512,1024,2048}, window 0 and 64",
+                   "global_batch": 1, "seq_len": 2048, "parallelism": "1 GPU",
+                   "l2": "flushed (256 MB write) before every timed call"},
+        "gpu_launches": int(launches), "cases": cases,
+        "roofline": None, "cpu_baseline": None, "e2e": None,
+        "note": "latency-bound configuration; auxiliary to the c3 headline line"}), flush=True)
 
 
 DEC = dict(B=8, Hq=32, Hkv=8, Sq=1, Sk=32768, D=128)
@@ -545,9 +712,14 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["c3", "c5", "c5u", "decode"], default="c3",
-                    help="c3 (default, the headline), c5 (context-parallel ring), c5u (context-"
+    ap.add_argument("--workload", choices=["c3", "c2", "c4", "c4t", "c5", "c5u", "decode"], default="c3",
+                    help="c3 (default, the headline), c2 (fp16 latencies), c4 / c4t (D=256 window + "
+                         "soft-cap at S=8192 / 8190), c5 (context-parallel ring), c5u (context-"
                          "parallel Ulysses) or decode (split-KV decoding forward)")
+    ap.add_argument("--ref-step-s", type=float, default=2.0,
+                    help="CPU seconds per step of the reference arm (a bounded sample of slices)")
+    ap.add_argument("--no-cp", action="store_true", help="skip the context-parallel key of the c3 line")
+    ap.add_argument("--cp-steps", type=int, default=5, help="timed steps of each context-parallel run")
     ap.add_argument("--profile", action="store_true",
                     help="for ncu: only the warm-up and timed steps (no e2e, no CPU baseline)")
     args = ap.parse_args()
@@ -557,6 +729,8 @@ def main():
         run_reference(args)
     elif args.workload in ("c5", "c5u"):
         run_c5(args, ulysses=args.workload == "c5u")
+    elif args.workload == "c2":
+        run_c2(args)
     elif args.workload == "decode":
         run_decode(args)
     else:

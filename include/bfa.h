@@ -25,8 +25,10 @@
  *    stride and 16-byte aligned outer strides; other layouts run on the
  *    generic CUDA path, never on the CPU.
  *  - The LSE is fp32, natural log, contiguous [B, Hq, Sq] (npu_flash_attention.py:632,161).
- *  - The library allocates no device memory. Backward scratch (Δ) lives in a
- *    caller-provided workspace of bfa_bwd_workspace_bytes() bytes.
+ *  - The library allocates no device memory. Scratch lives in caller-provided
+ *    workspaces: the backward's row statistics (Δ) in one of
+ *    bfa_bwd_workspace_bytes() bytes, the split-KV decoding forward's partial
+ *    results in one of bfa_fwd_workspace_bytes() bytes.
  *  - Calls are asynchronous on the given stream; they are thread-safe and
  *    re-entrant. The device is the caller's current CUDA device.
  *  - Return value: BFA_OK (0) or a negative bfa_status. Nothing is thrown
@@ -45,7 +47,7 @@
 extern "C" {
 #endif
 
-#define BFA_ABI_VERSION 2
+#define BFA_ABI_VERSION 3
 
 typedef enum bfa_dtype {
   BFA_DTYPE_F32 = 0,
@@ -103,6 +105,11 @@ typedef struct bfa_fwd_args {
   int32_t* status;         /* optional device status word */
   int64_t wait_timeout_ns; /* bound on any device-side wait; 0 = 1 second */
   uint32_t debug_flags;    /* 0 in production; BFA_DEBUG_* for tests */
+  void* workspace;         /* optional device scratch, 256-byte aligned: lets problems
+                              with few query rows per KV head take the split-KV
+                              decoding path (NULL: the regular forward runs) */
+  size_t workspace_bytes;  /* size of `workspace`; the decoding path needs
+                              bfa_fwd_workspace_bytes(problem) */
 } bfa_fwd_args;
 
 typedef struct bfa_bwd_args {
@@ -141,6 +148,14 @@ const char* bfa_strerror(int status);
 /* Forward: O and LSE. Replaces the launch at npu_flash_attention.py:631-652. */
 int bfa_fwd(const bfa_problem* problem, const bfa_fwd_args* args, void* stream);
 
+/* Bytes of workspace that let bfa_fwd take the split-KV decoding path for
+ * this problem on the current device (the partial O / LSE of each key split;
+ * the reference's unused split-KV forward, npu_flash_attention.py:171-293,
+ * wrote them to torch tensors it allocated at :255-262). 0 when the problem
+ * never takes that path (more than 64 query rows per KV head, or a dtype /
+ * head_dim it does not cover). */
+size_t bfa_fwd_workspace_bytes(const bfa_problem* problem);
+
 /* Bytes of workspace bfa_bwd needs for this problem (Δ and alignment). */
 size_t bfa_bwd_workspace_bytes(const bfa_problem* problem);
 
@@ -165,8 +180,12 @@ int bfa_bwd(const bfa_problem* problem, const bfa_bwd_args* args,
  * rows, each head's rows rounded up to 64 (batch*heads_q*ceil(seqlen_q/64)*64;
  * 16 MiB per GPU that loads the library, held until exit); larger problems
  * return BFA_ERR_SCRATCH_LIMIT. All calls share that array: calls that overlap on the
- * GPU race, so serialise them. The first call on each device looks up the
- * array's address and should come before any stream capture. */
+ * GPU race, so serialise them. Each call computes Δ itself: a `phases` mask
+ * without BFA_BWD_PHASE_DELTA is rejected (BFA_ERR_INVALID_ARGUMENT), since
+ * the array may hold another call's Δ. The first call on each device looks up
+ * the array's address and should come before any stream capture; the address
+ * is cached for the life of the process, so the library must not be used
+ * across a cudaDeviceReset. */
 int bfa_bwd_noalloc(const bfa_problem* problem, const bfa_bwd_args* args, void* stream);
 
 /* Merge a partial attention result into a running one, in place:

@@ -14,14 +14,14 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libbfa.so")
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 DEBUG_INJECT_STALL = 1
 ERR_DEVICE_TIMEOUT = -6
 
 EXPORTED = ("bfa_abi_version", "bfa_launch_count", "bfa_strerror", "bfa_fwd",
-            "bfa_bwd_workspace_bytes", "bfa_bwd_delta", "bfa_bwd", "bfa_bwd_noalloc",
+            "bfa_fwd_workspace_bytes", "bfa_bwd_workspace_bytes", "bfa_bwd_delta", "bfa_bwd", "bfa_bwd_noalloc",
             "bfa_merge_partial")
 ERR_SCRATCH_LIMIT = -7
 NOALLOC_MAX_ROWS = 1 << 21
@@ -48,7 +48,8 @@ class Tensor(ctypes.Structure):
 class FwdArgs(ctypes.Structure):
     _fields_ = [("q", Tensor), ("k", Tensor), ("v", Tensor), ("o", Tensor),
                 ("lse", ctypes.c_void_p), ("status", ctypes.c_void_p),
-                ("wait_timeout_ns", ctypes.c_int64), ("debug_flags", ctypes.c_uint32)]
+                ("wait_timeout_ns", ctypes.c_int64), ("debug_flags", ctypes.c_uint32),
+                ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t)]
 
 
 class BwdArgs(ctypes.Structure):
@@ -82,6 +83,8 @@ def load() -> ctypes.CDLL:
         lib.bfa_strerror.argtypes = [ctypes.c_int]
         lib.bfa_fwd.restype = ctypes.c_int
         lib.bfa_fwd.argtypes = [ctypes.POINTER(Problem), ctypes.POINTER(FwdArgs), ctypes.c_void_p]
+        lib.bfa_fwd_workspace_bytes.restype = ctypes.c_size_t
+        lib.bfa_fwd_workspace_bytes.argtypes = [ctypes.POINTER(Problem)]
         lib.bfa_bwd_workspace_bytes.restype = ctypes.c_size_t
         lib.bfa_bwd_workspace_bytes.argtypes = [ctypes.POINTER(Problem)]
         lib.bfa_bwd_delta.restype = ctypes.c_int

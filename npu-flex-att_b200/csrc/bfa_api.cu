@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <climits>
 #include <cstdlib>
 #include <cstring>
 
@@ -29,6 +30,8 @@ int check_problem(const bfa_problem* pr) {
   if (pr->batch < 0 || pr->heads_q < 0 || pr->heads_kv <= 0 || pr->seqlen_q < 0 ||
       pr->seqlen_k < 0 || pr->sliding_window < 0 || pr->soft_cap < 0.f)
     return BFA_ERR_INVALID_ARGUMENT;
+  // Query rows are padded to a multiple of 64 in int32 row pitches.
+  if (pr->seqlen_q > INT32_MAX - 63) return BFA_ERR_INVALID_ARGUMENT;
   if (pr->heads_q % pr->heads_kv != 0) return BFA_ERR_SHAPE;
   if (pr->head_dim < 1 || pr->head_dim > 256) return BFA_ERR_UNSUPPORTED;
   if (bfa::dtype_bytes(pr->dtype) == 0) return BFA_ERR_UNSUPPORTED;
@@ -105,12 +108,17 @@ int bfa_fwd(const bfa_problem* pr, const bfa_fwd_args* a, void* stream) {
   // Few query rows per KV head (decoding): the split-KV path streams K/V once
   // per KV head across the whole GPU. The fault-injection flags exercise the
   // tcgen05 kernels' bounded waits, so they keep the regular path.
-  if (p.debug_flags == 0 && bfa::decode_eligible(p, pr->dtype)) {
-    const int rc = bfa::decode_fwd(p, pr->dtype, st);
+  if (p.debug_flags == 0 && a->workspace && bfa::decode_eligible(p, pr->dtype)) {
+    const int rc = bfa::decode_fwd(p, pr->dtype, a->workspace, a->workspace_bytes, st);
     if (rc != -1) return rc;
   }
   if (bfa::sm100_fwd_eligible(p, pr->dtype)) return bfa::sm100_fwd(p, pr->dtype, st);
   return bfa::simt_fwd(p, pr->dtype, st);
+}
+
+size_t bfa_fwd_workspace_bytes(const bfa_problem* pr) {
+  if (check_problem(pr) || empty_q(pr)) return 0;
+  return bfa::decode_workspace_bytes(make_params(pr), pr->dtype);
 }
 
 // Backward workspace, in this order:
@@ -122,7 +130,7 @@ int bfa_fwd(const bfa_problem* pr, const bfa_fwd_args* a, void* stream) {
 // A workspace that holds only the row statistics (+256 bytes of alignment
 // slack) runs the two-kernel backward; bfa_bwd_workspace_bytes() reports the
 // size that enables the one-kernel path where it exists.
-static int32_t padded_rows(int32_t sq) { return (sq + 63) / 64 * 64; }
+static int64_t padded_rows(int32_t sq) { return ((int64_t)sq + 63) / 64 * 64; }
 
 static size_t round256(size_t n) { return (n + 255) / 256 * 256; }
 
@@ -210,7 +218,7 @@ int bfa_bwd(const bfa_problem* pr, const bfa_bwd_args* a, void* workspace, size_
   char* ws = (char*)workspace;
   p.delta = (float*)ws;
   p.lse2 = (float*)(ws + rowstat_bytes(pr));
-  p.Sq_pad = padded_rows(pr->seqlen_q);
+  p.Sq_pad = (int32_t)padded_rows(pr->seqlen_q);
   if (!empty_q(pr) && (p.phases & BFA_BWD_PHASE_DELTA)) {
     rc = bfa::launch_delta(p, pr->dtype, st);
     if (rc) return rc;

@@ -25,10 +25,13 @@ bool sm100_bwd_fused_eligible(const Params& p, int dtype);
 int sm100_bwd_fused(const Params& p, int dtype, uint32_t* order, float* dq_acc, cudaStream_t st);
 
 // Split-KV decoding forward (decode.cu): the G q-heads of a KV head have at
-// most 64 query rows. decode_fwd returns a bfa_status, or -1 when it could not
-// run (the caller falls back to the regular forward).
+// most 64 query rows. Its partial results live in a caller workspace of
+// decode_workspace_bytes() bytes (0: the problem never takes this path).
+// decode_fwd returns a bfa_status, or -1 when it could not run (no or too
+// small a workspace; the caller falls back to the regular forward).
 bool decode_eligible(const Params& p, int dtype);
-int decode_fwd(const Params& p, int dtype, cudaStream_t st);
+size_t decode_workspace_bytes(const Params& p, int dtype);
+int decode_fwd(const Params& p, int dtype, void* ws, size_t ws_bytes, cudaStream_t st);
 
 // Multiprocessors of the current device (cached per device).
 int sm_count();

@@ -18,11 +18,13 @@
 //  * All calls share the one array per device and it keeps the last call's
 //    contents. Calls whose work overlaps on the GPU (different streams, or
 //    different host threads on the same device) race on it; serialise them.
-//    Δ is fully rewritten by each call before it is read, so nothing needs
-//    clearing.
+//    Each call computes Δ itself before reading it (a `phases` mask without
+//    BFA_BWD_PHASE_DELTA is rejected: the array could hold another call's Δ),
+//    so nothing needs clearing.
 //  * The first call on a device looks up the array's device address
 //    (cudaGetSymbolAddress, with that device current) and caches it; make that
-//    first call before any stream capture.
+//    first call before any stream capture. The cached address is kept for the
+//    life of the process: do not use the library across a cudaDeviceReset.
 //  * Nothing here calls cudaMalloc, cudaFree or an allocating library routine.
 #include <cuda_runtime.h>
 
@@ -66,6 +68,8 @@ extern "C" int bfa_bwd_noalloc(const bfa_problem* problem, const bfa_bwd_args* a
         (int64_t)problem->batch * problem->heads_q * (((int64_t)problem->seqlen_q + 63) / 64 * 64);
     if (rows > kMaxRows) return BFA_ERR_SCRATCH_LIMIT;
   }
+  if (!args) return BFA_ERR_INVALID_ARGUMENT;
+  if (args->phases != 0 && !(args->phases & BFA_BWD_PHASE_DELTA)) return BFA_ERR_INVALID_ARGUMENT;
   float* scratch = nullptr;
   const int rc = scratch_address(&scratch);
   if (rc != BFA_OK) return rc;

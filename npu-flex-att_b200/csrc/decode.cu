@@ -21,7 +21,9 @@
 //     softmax on the CUDA cores; fp32 inputs run S, softmax and P·V on the
 //     CUDA cores;
 //   - the keys are split so that the CTAs fill the GPU in about one wave, and
-//     a merge kernel combines the splits' partial (O, LSE) per row.
+//     a merge kernel combines the splits' partial (O, LSE) per row. The
+//     partials live in the caller's workspace (bfa_fwd_workspace_bytes); the
+//     library allocates nothing.
 // The math per row is the forward's: S·scale, cap, ALiBi, mask on absolute
 // positions (q_off, k_off), base-2 online softmax, O = PV/l and
 // LSE = m + ln(l) (natural log), -inf with O = 0 for a row that sees no key.
@@ -29,7 +31,6 @@
 
 #include <algorithm>
 #include <cstdlib>
-#include <mutex>
 #include <cstring>
 #include <type_traits>
 
@@ -638,35 +639,6 @@ __global__ void __launch_bounds__(kMergeThreads)
   if (tid == 0) p.lse[row] = (wsum > 0.f) ? m + logf(wsum) : neg_inf();
 }
 
-// Library-private stream-ordered memory pool per device for the partials:
-// it keeps up to kPoolKeep bytes between calls, so a steady stream of decode
-// calls allocates without mapping new memory, and no process-wide pool
-// setting is touched.
-constexpr uint64_t kPoolKeep = 256ull << 20;
-
-cudaMemPool_t decode_pool() {
-  static std::mutex mu;
-  static cudaMemPool_t pools[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  std::lock_guard<std::mutex> lock(mu);
-  if (!pools[dev]) {
-    cudaMemPoolProps props = {};
-    props.allocType = cudaMemAllocationTypePinned;
-    props.location.type = cudaMemLocationTypeDevice;
-    props.location.id = dev;
-    cudaMemPool_t pool = nullptr;
-    if (cudaMemPoolCreate(&pool, &props) != cudaSuccess) {
-      cudaGetLastError();
-      return nullptr;
-    }
-    uint64_t keep = kPoolKeep;
-    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
-    pools[dev] = pool;
-  }
-  return pools[dev];
-}
-
 // BFA_FWD_DECODE=0 turns the path off (the regular forward runs instead).
 bool decode_enabled() {
   const char* e = std::getenv("BFA_FWD_DECODE");
@@ -675,10 +647,19 @@ bool decode_enabled() {
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
+// Launch plan of one decoding call: kernel, split count and the size of the
+// partial results, computed the same way by bfa_fwd_workspace_bytes (to size
+// the caller's workspace) and by the launch.
+struct DecodePlan {
+  void (*kern)(const Params, int, int, int, float*, float*);
+  int smem_bytes;
+  int klo, n_split, split_len, kv_heads;
+  size_t o_bytes, l_bytes;
+};
+
 template <typename T, int D>
-int launch_decode(const Params& p, cudaStream_t st) {
+bool plan_decode(const Params& p, DecodePlan* pl) {
   using L = DecLayout<T, D>;
-  int klo, khi;
   {
     // key_range on the host: same arithmetic as the device helper.
     int64_t l = 0, h = p.Sk;
@@ -688,8 +669,8 @@ int launch_decode(const Params& p, cudaStream_t st) {
     if (h < l) h = l;
     l = std::max<int64_t>(l, 0);
     h = std::max<int64_t>(h, 0);
-    klo = (int)l;
-    khi = (int)h;
+    pl->klo = (int)l;
+    pl->n_split = (int)(h - l);  // visible keys, replaced below
   }
   const bool plain = !(p.soft_cap > 0.f) && p.alibi == nullptr;
   const int n_rg = (p.G * p.Sq + kMaxRows - 1) / kMaxRows;  // row groups of <= 16 rows
@@ -709,8 +690,10 @@ int launch_decode(const Params& p, cudaStream_t st) {
                   : R <= 8 ? pick(std::integral_constant<int, 8>{}) : pick(std::integral_constant<int, 16>{});
     smem_bytes = L::kSmemBytes;
   }
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess)
-    return BFA_ERR_CUDA;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kDecThreads, smem_bytes) != cudaSuccess ||
       per_sm < 1) {
@@ -719,7 +702,7 @@ int launch_decode(const Params& p, cudaStream_t st) {
   }
 
   const int kv_heads = p.B * p.Hkv * n_rg;  // (KV head, row group) pairs
-  const int vis = khi - klo;
+  const int vis = pl->n_split;
   // One wave: as many splits as fill the resident CTA slots, each split a
   // long run of keys (the per-CTA start-up, pipeline fill and merge input grow
   // with the split count); two waves when one fills under 3/4 of the slots.
@@ -733,41 +716,78 @@ int launch_decode(const Params& p, cudaStream_t st) {
   n_split = std::max(1, (vis + split_len - 1) / split_len);
 
   const int64_t rows = (int64_t)p.B * p.Hq * p.Sq;
-  const size_t o_bytes = (size_t)rows * n_split * D * sizeof(float);
-  const size_t l_bytes = (size_t)rows * n_split * sizeof(float);
-  void* buf = nullptr;
-  cudaMemPool_t pool = decode_pool();
-  if (!pool || cudaMallocFromPoolAsync(&buf, o_bytes + l_bytes, pool, st) != cudaSuccess) {
-    cudaGetLastError();
-    return -1;  // caller falls back to the regular forward
-  }
-  float* part_o = static_cast<float*>(buf);
-  float* part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(buf) + o_bytes);
+  pl->kern = kern;
+  pl->smem_bytes = smem_bytes;
+  pl->n_split = n_split;
+  pl->split_len = split_len;
+  pl->kv_heads = kv_heads;
+  pl->o_bytes = (size_t)rows * n_split * D * sizeof(float);
+  pl->l_bytes = (size_t)rows * n_split * sizeof(float);
+  return true;
+}
 
-  kern<<<(unsigned)(kv_heads * n_split), kDecThreads, smem_bytes, st>>>(p, n_split, klo, split_len, part_o,
-                                                                        part_lse);
+// The partial O (fp32 [rows][splits][D]) and LSE (fp32 [rows][splits]) live
+// in the caller's workspace; -1 (the caller runs the regular forward) when it
+// is missing or too small.
+template <typename T, int D>
+int launch_decode(const Params& p, void* ws, size_t ws_bytes, cudaStream_t st) {
+  DecodePlan pl;
+  if (!plan_decode<T, D>(p, &pl)) return BFA_ERR_CUDA;
+  if (!ws || ((uintptr_t)ws & 255u) != 0 || ws_bytes < pl.o_bytes + pl.l_bytes) return -1;
+  float* part_o = static_cast<float*>(ws);
+  float* part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + pl.o_bytes);
+  const int64_t rows = (int64_t)p.B * p.Hq * p.Sq;
+  pl.kern<<<(unsigned)(pl.kv_heads * pl.n_split), kDecThreads, pl.smem_bytes, st>>>(p, pl.n_split, pl.klo,
+                                                                                    pl.split_len, part_o,
+                                                                                    part_lse);
   note_launch();
   cudaError_t err = cudaGetLastError();
   if (err == cudaSuccess) {
-    decode_merge_kernel<T><<<(unsigned)rows, kMergeThreads, 0, st>>>(p, n_split, part_o, part_lse);
+    decode_merge_kernel<T><<<(unsigned)rows, kMergeThreads, 0, st>>>(p, pl.n_split, part_o, part_lse);
     note_launch();
     err = cudaGetLastError();
   }
-  cudaFreeAsync(buf, st);
   return err == cudaSuccess ? BFA_OK : BFA_ERR_CUDA;
 }
 
+template <typename T, int D>
+size_t decode_bytes(const Params& p) {
+  DecodePlan pl;
+  if (!plan_decode<T, D>(p, &pl)) return 0;
+  return pl.o_bytes + pl.l_bytes;
+}
+
 template <typename T>
-int dispatch_d(const Params& p, cudaStream_t st) {
+int dispatch_d(const Params& p, void* ws, size_t ws_bytes, cudaStream_t st) {
   switch (p.D) {
-    case 64: return launch_decode<T, 64>(p, st);
-    case 128: return launch_decode<T, 128>(p, st);
+    case 64: return launch_decode<T, 64>(p, ws, ws_bytes, st);
+    case 128: return launch_decode<T, 128>(p, ws, ws_bytes, st);
     case 256:
       // fp32 rows of 256 do not fit two double-buffered 64-key K/V tiles.
-      if constexpr (sizeof(T) == 2) return launch_decode<T, 256>(p, st);
+      if constexpr (sizeof(T) == 2) return launch_decode<T, 256>(p, ws, ws_bytes, st);
       return -1;
     default: return -1;
   }
+}
+
+template <typename T>
+size_t bytes_d(const Params& p) {
+  switch (p.D) {
+    case 64: return decode_bytes<T, 64>(p);
+    case 128: return decode_bytes<T, 128>(p);
+    case 256:
+      if constexpr (sizeof(T) == 2) return decode_bytes<T, 256>(p);
+      return 0;
+    default: return 0;
+  }
+}
+
+// The shape part of decode_eligible (no pointers or strides involved).
+bool decode_shape_ok(const Params& p, int dtype) {
+  if (!decode_enabled()) return false;
+  if (dtype != BFA_DTYPE_BF16 && dtype != BFA_DTYPE_F16 && dtype != BFA_DTYPE_F32) return false;
+  if (p.D != 64 && p.D != 128 && !(p.D == 256 && dtype != BFA_DTYPE_F32)) return false;
+  return !(p.G * p.Sq > kMaxRowsTotal || p.Sq < 1 || p.Sk < 1 || p.B < 1 || p.Hkv < 1);
 }
 
 }  // namespace
@@ -785,10 +805,7 @@ int sm_count() {
 }
 
 bool decode_eligible(const Params& p, int dtype) {
-  if (!decode_enabled()) return false;
-  if (dtype != BFA_DTYPE_BF16 && dtype != BFA_DTYPE_F16 && dtype != BFA_DTYPE_F32) return false;
-  if (p.D != 64 && p.D != 128 && !(p.D == 256 && dtype != BFA_DTYPE_F32)) return false;
-  if (p.G * p.Sq > kMaxRowsTotal || p.Sq < 1 || p.Sk < 1 || p.B < 1 || p.Hkv < 1) return false;
+  if (!decode_shape_ok(p, dtype)) return false;
   // K/V rows are copied in 16-byte pieces: unit stride along D, 16-byte
   // aligned bases and row / head / batch strides.
   const int64_t es = dtype == BFA_DTYPE_F32 ? 4 : 2;
@@ -798,11 +815,23 @@ bool decode_eligible(const Params& p, int dtype) {
   return true;
 }
 
-int decode_fwd(const Params& p, int dtype, cudaStream_t st) {
+size_t decode_workspace_bytes(const Params& p, int dtype) {
+  if (!decode_shape_ok(p, dtype)) return 0;
+  size_t n = 0;
   switch (dtype) {
-    case BFA_DTYPE_BF16: return dispatch_d<__nv_bfloat16>(p, st);
-    case BFA_DTYPE_F16: return dispatch_d<__half>(p, st);
-    case BFA_DTYPE_F32: return dispatch_d<float>(p, st);
+    case BFA_DTYPE_BF16: n = bytes_d<__nv_bfloat16>(p); break;
+    case BFA_DTYPE_F16: n = bytes_d<__half>(p); break;
+    case BFA_DTYPE_F32: n = bytes_d<float>(p); break;
+    default: return 0;
+  }
+  return n ? (n + 255) / 256 * 256 : 0;
+}
+
+int decode_fwd(const Params& p, int dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
+  switch (dtype) {
+    case BFA_DTYPE_BF16: return dispatch_d<__nv_bfloat16>(p, ws, ws_bytes, st);
+    case BFA_DTYPE_F16: return dispatch_d<__half>(p, ws, ws_bytes, st);
+    case BFA_DTYPE_F32: return dispatch_d<float>(p, ws, ws_bytes, st);
     default: return -1;
   }
 }

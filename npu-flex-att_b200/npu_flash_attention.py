@@ -149,6 +149,12 @@ def npu_flash_attention_forward(
     args.wait_timeout_ns = int(_wait_timeout_ns)
     args.debug_flags = int(_debug_flags)
     with torch.cuda.device(dev):
+        # Scratch of the split-KV decoding path (few query rows per KV head),
+        # from torch's caching allocator: the library allocates nothing.
+        ws_bytes = lib.bfa_fwd_workspace_bytes(pr)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
+        if ws is not None:
+            args.workspace, args.workspace_bytes = ws.data_ptr(), ws_bytes
         _bfa.check(lib.bfa_fwd(pr, args, _bfa.stream_ptr(dev)))
     if o_k is not O:
         O.copy_(o_k)
@@ -238,7 +244,12 @@ def npu_flash_attention_backward(
 
 
 class NPUFlexAttention(torch.autograd.Function):
-    """Autograd wrapper (npu_flash_attention.py:742-781)."""
+    """torch.autograd.Function over the two library calls: forward saves
+    (q, k, v, LSE, O) for the backward, which returns gradients for q, k and
+    v only (the mask arguments get None). Same class name, argument order and
+    saved state as the reference's autograd class
+    (npu_flash_attention.py:742-781), so code that calls ``.apply`` on it
+    keeps working."""
 
     @staticmethod
     def forward(ctx, query, key, value, causal=False, sliding_window=0,
@@ -281,7 +292,8 @@ def npu_flex_attention(
     block_m=16, block_n=64,
     soft_cap=0.0,
 ):
-    """Differentiable attention (npu_flash_attention.py:784-794)."""
+    """Functional form of NPUFlexAttention.apply with keyword defaults
+    (signature of npu_flash_attention.py:784-794)."""
     return NPUFlexAttention.apply(
         query, key, value, causal, sliding_window,
         alibi_slope, scale, block_m, block_n, soft_cap,
@@ -290,11 +302,13 @@ def npu_flex_attention(
 
 @dataclass
 class AttentionConfig:
-    """Composable attention pattern (npu_flash_attention.py:820-844).
+    """Bundle of the mask and logit options that flex_attention applies
+    (fields, defaults and validation of npu_flash_attention.py:820-844).
 
-    Example -- Gemma2-style attention:
-        config = AttentionConfig(causal=True, sliding_window=1024, soft_cap=50.0)
-        out = flex_attention(q, k, v, config=config)
+    A negative window or cap raises ValueError when the config is built.
+    For instance a local-attention layer with capped logits:
+        cfg = AttentionConfig(causal=True, sliding_window=4096, soft_cap=50.0)
+        o = flex_attention(q, k, v, config=cfg)
     """
     causal: bool = False
     sliding_window: int = 0
@@ -312,9 +326,9 @@ class AttentionConfig:
 
 
 def flex_attention(query, key, value, config: Optional[AttentionConfig] = None, **kwargs):
-    """Config-driven entry (npu_flash_attention.py:847-886): builds an
-    AttentionConfig from kwargs when no config is given (kwargs are ignored
-    when one is) and runs the differentiable attention."""
+    """Differentiable attention driven by an AttentionConfig. With no
+    ``config`` the keyword arguments build one; with a config they are not
+    looked at (the rule of npu_flash_attention.py:847-886)."""
     if config is None:
         config = AttentionConfig(**kwargs)
     return npu_flex_attention(

@@ -23,6 +23,8 @@ the tests, and nothing on the GPU box reads the reference):
 
     python tests/golden/make_golden.py /path/to/reference  [out.npz]
 
+(or with the checkout's path in the environment variable NPU_FLEX_ATT_REFERENCE).
+
 Inputs are drawn with ``torch.manual_seed`` on the CPU in fp32 and cast, so
 the stored inputs are exact. Every case stores its inputs, the reference's
 outputs and a few flags. fp16 tensors are stored as float16 and bf16 tensors
@@ -154,7 +156,10 @@ def run_case(ref, case, seed):
 
 
 def main():
-    ref_path = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref_path = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("NPU_FLEX_ATT_REFERENCE")
+    if not ref_path:
+        sys.exit("usage: make_golden.py REFERENCE_CHECKOUT [out.npz] "
+                 "(or set NPU_FLEX_ATT_REFERENCE)")
     out = sys.argv[2] if len(sys.argv) > 2 else os.path.join(
         os.path.dirname(os.path.abspath(__file__)), "reference_cases.npz")
     ref = load_reference(ref_path)

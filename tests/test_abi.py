@@ -86,3 +86,23 @@ def test_merge_partial_validates():
     assert lib.bfa_merge_partial(1, 1, 1, 0, t, 0, None, t, 0, None, None) == -1
     assert lib.bfa_merge_partial(1, 1, 1, 64, t, 9, None, t, 0, None, None) == -3
     assert lib.bfa_merge_partial(0, 1, 1, 64, t, 0, None, t, 0, None, None) == 0
+
+
+def test_fwd_workspace_bytes_without_gpu():
+    """bfa_fwd_workspace_bytes reports 0 for problems that never take the
+    split-KV decoding path (and for invalid ones); the size of the decoding
+    path's scratch is checked on the GPU (test_decode_gpu.py)."""
+    lib = bfa_lib.load()
+    assert lib.bfa_fwd_workspace_bytes(None) == 0
+    assert lib.bfa_fwd_workspace_bytes(ctypes.byref(_problem(heads_q=3, heads_kv=2))) == 0
+    # 4 q-heads per KV head x 256 rows: far above the 64 rows per KV head of the decoding path.
+    assert lib.bfa_fwd_workspace_bytes(ctypes.byref(_problem(seqlen_q=256, seqlen_k=256))) == 0
+
+
+def test_seqlen_q_bound():
+    """Row pitches are padded to 64 in int32: lengths past INT32_MAX - 63 are
+    rejected instead of overflowing."""
+    lib = bfa_lib.load()
+    pr = _problem(seqlen_q=2 ** 31 - 1)
+    assert lib.bfa_fwd(ctypes.byref(pr), ctypes.byref(bfa_lib.FwdArgs()), None) == -1
+    assert lib.bfa_bwd_workspace_bytes(ctypes.byref(pr)) == 0

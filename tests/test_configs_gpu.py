@@ -1,0 +1,253 @@
+"""GPU parity at the benchmark configurations' own shapes.
+
+The sweeps in test_parity_gpu.py stay at S <= 1000. This file runs the CUDA
+path at the sizes the benchmark configurations name, against the fp64 oracle
+on identical inputs generated on the CPU from a fixed seed (fp32 N(0,1), then
+cast):
+
+  c1  fp32 B1 H2 S128 D64 causal, with LSE                        in full
+  c2  fp16 B1 H2 D64 S in {128, 512, 1024, 2048}, +-window 64     in full
+  c3  bf16 GQA Hq/Hkv = 32/8 at S=4096, D=128, causal: B=1 with
+      8 q-heads (2 KV groups of 4)                                in full
+  c4  bf16 D=256, causal + window 4096 + soft-cap 50, scale 1/16,
+      S=8192 and S=8190 (a key tail that is not a tile multiple),
+      2 q-heads on 1 KV head                                      in full
+  c5  bf16 B1 Hq64 Hkv8 D128 S=65536, causal + ALiBi with slopes
+      2^(-8(i+1)/64): the device runs the whole configuration; the
+      oracle checks O, LSE and dQ of three 128-row query blocks
+      against all keys, and dK, dV of three 128-key blocks against
+      all queries, for KV heads 0 and 7 (q-heads 0-7 and 56-63,
+      the largest and the smallest slopes)
+
+Each output and gradient is held to two bounds (the contract's absolute
+tolerances: fp32 1e-4, fp16 1e-2, bf16 2e-2; LSE 1e-3 relative):
+  * the allclose form the reference's own tests use,
+    |a - ref| <= tol * (1 + |ref|);
+  * the plain absolute error beyond one unit in the last place of the output
+    format at the reference value, |a - ref| - ulp(ref) <= tol. Storing the
+    exact result in a 16-bit format already costs half an ulp, and fp32
+    logits carry rounding of their own at large |logit| (c5's positive ALiBi
+    bias reaches 6e4, where an fp32 ulp is 4e-3), so no fp32 implementation
+    meets a pure absolute 2e-2 on bf16 gradients of magnitude 100. Where
+    |ref| < 1 this bound is within 2^-7 of the pure absolute tolerance.
+The plain max-abs error of every tensor is printed beside both (pytest -s).
+
+The backward is checked as the operator it is, a function of
+(q, k, v, out, lse, dout): the oracle gets the device's `out` and, for the
+full configurations, the exact LSE; for c5's key blocks, which need the LSE of
+all 65536 rows, it gets the device LSE (checked against the exact one on the
+sampled rows), as a caller's backward would.
+"""
+import math
+
+import pytest
+import torch
+
+import npu_flash_attention as nfa
+from oracle.attention_math import attention_backward, attention_forward
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+TOL = {torch.float32: 1e-4, torch.float16: 1e-2, torch.bfloat16: 2e-2}
+MANTISSA_BITS = {torch.float32: 23, torch.float16: 10, torch.bfloat16: 7}
+LSE_RTOL = 1e-3
+
+
+def _inputs(seed, b, hq, hkv, sq, sk, d, dtype):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(b, hq, sq, d, generator=g).to(dtype)
+    k = torch.randn(b, hkv, sk, d, generator=g).to(dtype)
+    v = torch.randn(b, hkv, sk, d, generator=g).to(dtype)
+    go = torch.randn(b, hq, sq, d, generator=g).to(dtype)
+    return q, k, v, go
+
+
+def _ulp(ref, dtype):
+    """Spacing of `dtype` at |ref| (normal range; the minimum normal below it)."""
+    bits = MANTISSA_BITS[dtype]
+    tiny = torch.finfo(dtype).tiny
+    e = torch.floor(torch.log2(ref.abs().clamp_min(tiny)))
+    return torch.pow(2.0, e - bits)
+
+
+def check_tensor(name, a, ref, dtype, tol=None):
+    """Both bounds of the module docstring; returns the plain max-abs error."""
+    tol = tol or TOL[dtype]
+    a = a.detach().cpu().double()
+    ref = ref.detach().cpu().double()
+    assert a.shape == ref.shape, f"{name}: shape {tuple(a.shape)} vs {tuple(ref.shape)}"
+    fin = torch.isfinite(ref)
+    assert torch.equal(torch.isfinite(a), fin), f"{name}: inf/nan pattern differs"
+    if not fin.any():
+        return 0.0
+    a, ref = a[fin], ref[fin]
+    d = (a - ref).abs()
+    max_abs = d.max().item()
+    rel_form = (d / (1.0 + ref.abs())).max().item()
+    beyond_ulp = (d - _ulp(ref, dtype)).max().item()
+    print(f"  {name:>4}: max|a-ref| {max_abs:.3e}  allclose-form {rel_form:.3e}  "
+          f"beyond 1 ulp {beyond_ulp:.3e}  (tol {tol:g}, max|ref| {ref.abs().max().item():.3g})")
+    assert rel_form < tol, f"{name}: allclose-form error {rel_form} >= {tol}"
+    assert beyond_ulp < tol, f"{name}: absolute error beyond 1 ulp {beyond_ulp} >= {tol}"
+    return max_abs
+
+
+def check_lse(lse, ref):
+    lse = lse.detach().cpu().double()
+    ref = ref.detach().cpu().double()
+    fin = torch.isfinite(ref)
+    assert torch.equal(torch.isfinite(lse), fin)
+    if not fin.any():
+        return
+    rel = ((lse[fin] - ref[fin]).abs() / ref[fin].abs().clamp_min(1.0)).max().item()
+    print(f"   lse: max rel {rel:.3e}  (tol {LSE_RTOL:g})")
+    assert rel < LSE_RTOL, f"LSE relative error {rel}"
+
+
+def run_device(q, k, v, go, **kw):
+    kw_dev = dict(kw)
+    if kw.get("alibi_slope") is not None:
+        kw_dev["alibi_slope"] = kw["alibi_slope"].to(DEV)
+    qd, kd, vd, god = (t.to(DEV) for t in (q, k, v, go))
+    o, lse = nfa.npu_flash_attention_forward(qd, kd, vd, return_lse=True, **kw_dev)
+    dq, dk, dv = nfa.npu_flash_attention_backward(qd, kd, vd, o, lse, god, **kw_dev)
+    torch.cuda.synchronize()
+    nfa.check_device_status(DEV)
+    return o, lse, dq, dk, dv
+
+
+def _head_kw(kw, h):
+    """Mask arguments for q-head `h` alone (its ALiBi slope)."""
+    out = dict(kw)
+    if kw.get("alibi_slope") is not None:
+        out["alibi_slope"] = kw["alibi_slope"][h:h + 1]
+    return out
+
+
+def check_full(q, k, v, go, **kw):
+    """Whole-problem check, one q-head at a time so the oracle's S x S
+    matrices stay a few hundred MB; dK/dV are summed over each GQA group."""
+    dtype = q.dtype
+    o, lse, dq, dk, dv = run_device(q, k, v, go, **kw)
+    o_c, lse_c = o.cpu(), lse.cpu()
+    hq, hkv = q.shape[1], k.shape[1]
+    grp = hq // hkv
+    op_dt = dtype if dtype in (torch.float16, torch.bfloat16) else None
+    o_ref = torch.empty(q.shape, dtype=torch.float64)
+    lse_ref = torch.empty(q.shape[:3], dtype=torch.float64)
+    dq_ref = torch.empty(q.shape, dtype=torch.float64)
+    dk_ref = torch.zeros(k.shape, dtype=torch.float64)
+    dv_ref = torch.zeros(v.shape, dtype=torch.float64)
+    for h in range(hq):
+        kh = h // grp
+        sl = slice(h, h + 1)
+        ks = slice(kh, kh + 1)
+        hkw = _head_kw(kw, h)
+        o_h, lse_h = attention_forward(q[:, sl], k[:, ks], v[:, ks], **hkw)
+        o_ref[:, sl], lse_ref[:, sl] = o_h, lse_h
+        dq_h, dk_h, dv_h = attention_backward(q[:, sl], k[:, ks], v[:, ks], go[:, sl],
+                                              out=o_c[:, sl], lse=lse_h, operand_dtype=op_dt,
+                                              **hkw)
+        dq_ref[:, sl] = dq_h
+        dk_ref[:, ks] += dk_h
+        dv_ref[:, ks] += dv_h
+    check_lse(lse_c, lse_ref)
+    errs = {name: check_tensor(name, a, r, dtype) for name, a, r in (
+        ("o", o_c, o_ref), ("dq", dq, dq_ref), ("dk", dk, dk_ref), ("dv", dv, dv_ref))}
+    return errs
+
+
+def test_c1_fp32_causal_with_lse():
+    print("\nc1 fp32 B1 H2 S128 D64 causal")
+    q, k, v, go = _inputs(1, 1, 2, 2, 128, 128, 64, torch.float32)
+    check_full(q, k, v, go, causal=True, scale=1.0 / math.sqrt(64))
+
+
+@pytest.mark.parametrize("window", [0, 64])
+@pytest.mark.parametrize("s", [128, 512, 1024, 2048])
+def test_c2_fp16_causal(s, window):
+    print(f"\nc2 fp16 B1 H2 D64 S{s} causal window {window}")
+    q, k, v, go = _inputs(2000 + s, 1, 2, 2, s, s, 64, torch.float16)
+    check_full(q, k, v, go, causal=True, sliding_window=window)
+
+
+def test_c3_bf16_gqa_s4096():
+    print("\nc3 bf16 B1 Hq8 Hkv2 (GQA 4, as 32/8) S4096 D128 causal")
+    q, k, v, go = _inputs(3, 1, 8, 2, 4096, 4096, 128, torch.bfloat16)
+    check_full(q, k, v, go, causal=True, scale=1.0 / math.sqrt(128))
+
+
+@pytest.mark.parametrize("s", [8192, 8190])
+def test_c4_bf16_d256_window_softcap(s):
+    print(f"\nc4 bf16 B1 Hq2 Hkv1 S{s} D256 causal W4096 cap50")
+    q, k, v, go = _inputs(4000 + s, 1, 2, 1, s, s, 256, torch.bfloat16)
+    check_full(q, k, v, go, causal=True, sliding_window=4096, soft_cap=50.0,
+               scale=1.0 / math.sqrt(256))
+
+
+C5_KV_HEADS = (0, 7)
+C5_ROW_BLOCKS = (0, 32704, 65408)
+C5_KEY_BLOCKS = (0, 32768, 65408)
+BLK = 128
+
+
+def test_c5_bf16_alibi_s65536_sliced():
+    """The whole configuration on the device; row/column slices in the oracle."""
+    print("\nc5 bf16 B1 Hq64 Hkv8 S65536 D128 causal + ALiBi (sliced oracle)")
+    B, Hq, Hkv, S, D = 1, 64, 8, 65536, 128
+    grp = Hq // Hkv
+    dtype = torch.bfloat16
+    q, k, v, go = _inputs(5, B, Hq, Hkv, S, S, D, dtype)
+    slopes = torch.tensor([2.0 ** (-8.0 * (i + 1) / Hq) for i in range(Hq)], dtype=torch.float32)
+    kw = dict(causal=True, alibi_slope=slopes, scale=1.0 / math.sqrt(D))
+    o, lse, dq, dk, dv = run_device(q, k, v, go, **kw)
+    heads = [h for kh in C5_KV_HEADS for h in range(kh * grp, (kh + 1) * grp)]
+    o_c = o[:, heads].cpu()
+    lse_c = lse[:, heads].cpu()
+    pos = {h: n for n, h in enumerate(heads)}
+    rows_dev = {r0: (dq[:, heads, r0:r0 + BLK].cpu()) for r0 in C5_ROW_BLOCKS}
+    keys_dev = {c0: (dk[:, list(C5_KV_HEADS), c0:c0 + BLK].cpu(),
+                     dv[:, list(C5_KV_HEADS), c0:c0 + BLK].cpu()) for c0 in C5_KEY_BLOCKS}
+    del o, dq, dk, dv
+    torch.cuda.empty_cache()
+
+    # O, LSE and dQ of each row block against all keys.
+    for r0 in C5_ROW_BLOCKS:
+        rs = slice(r0, r0 + BLK)
+        o_ref = torch.empty(B, len(heads), BLK, D, dtype=torch.float64)
+        lse_ref = torch.empty(B, len(heads), BLK, dtype=torch.float64)
+        dq_ref = torch.empty(B, len(heads), BLK, D, dtype=torch.float64)
+        for h in heads:
+            n, kh = pos[h], h // grp
+            hkw = _head_kw(kw, h)
+            qh, goh = q[:, h:h + 1, rs], go[:, h:h + 1, rs]
+            kk, vv = k[:, kh:kh + 1], v[:, kh:kh + 1]
+            o_h, lse_h = attention_forward(qh, kk, vv, q_offset=r0, **hkw)
+            o_ref[:, n:n + 1], lse_ref[:, n:n + 1] = o_h, lse_h
+            dq_h, _, _ = attention_backward(qh, kk, vv, goh, out=o_c[:, n:n + 1, rs],
+                                            lse=lse_c[:, n:n + 1, rs].double(), q_offset=r0,
+                                            operand_dtype=dtype, **hkw)
+            dq_ref[:, n:n + 1] = dq_h
+        print(f" rows [{r0}, {r0 + BLK})")
+        check_lse(lse_c[:, :, rs], lse_ref)
+        check_tensor("o", o_c[:, :, rs], o_ref, dtype)
+        check_tensor("dq", rows_dev[r0], dq_ref, dtype)
+
+    # dK, dV of each key block against all queries (summed over the group).
+    for c0 in C5_KEY_BLOCKS:
+        cs = slice(c0, c0 + BLK)
+        dk_ref = torch.zeros(B, len(C5_KV_HEADS), BLK, D, dtype=torch.float64)
+        dv_ref = torch.zeros_like(dk_ref)
+        for m, kh in enumerate(C5_KV_HEADS):
+            for h in range(kh * grp, (kh + 1) * grp):
+                n = pos[h]
+                _, dk_h, dv_h = attention_backward(
+                    q[:, h:h + 1], k[:, kh:kh + 1, cs], v[:, kh:kh + 1, cs], go[:, h:h + 1],
+                    out=o_c[:, n:n + 1], lse=lse_c[:, n:n + 1].double(), k_offset=c0,
+                    operand_dtype=dtype, **_head_kw(kw, h))
+                dk_ref[:, m:m + 1] += dk_h
+                dv_ref[:, m:m + 1] += dv_h
+        print(f" keys [{c0}, {c0 + BLK})")
+        check_tensor("dk", keys_dev[c0][0], dk_ref, dtype)
+        check_tensor("dv", keys_dev[c0][1], dv_ref, dtype)

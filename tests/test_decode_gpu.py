@@ -109,3 +109,33 @@ def test_decode_not_taken_for_many_rows():
     qd, kd, vd = (t.to(DEV) for t in (q, k, v))
     _, _, launches = _run(qd, kd, vd, {}, decode=True)
     assert launches == 1
+
+
+def test_decode_scratch_comes_from_the_caller():
+    """The partial O / LSE live in the caller's workspace: bfa_fwd_workspace_bytes
+    sizes it, and without one bfa_fwd runs the regular forward (one launch)
+    with the same result. The library keeps no memory pool of its own."""
+    import ctypes
+    lib = bfa_lib.load()
+    q, k, v, _ = _inputs(9, 2, 8, 2, 1, 3000, 128, torch.bfloat16)
+    qd, kd, vd = (t.to(DEV) for t in (q, k, v))
+    pr = nfa._problem(qd, kd, False, 0, None, 128 ** -0.5, 0.0)
+    need = lib.bfa_fwd_workspace_bytes(ctypes.byref(pr))
+    assert need > 0 and need % 256 == 0
+    o_ref, lse_ref, launches = _run(qd, kd, vd, {}, decode=True)
+    assert launches == 2
+    for ws_bytes in (0, need - 256):
+        o = torch.empty_like(qd)
+        lse = torch.empty(2, 8, 1, device=DEV)
+        args = bfa_lib.FwdArgs()
+        args.q, args.k, args.v, args.o = (bfa_lib.tensor(t) for t in (qd, kd, vd, o))
+        args.lse = lse.data_ptr()
+        ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=DEV)
+        if ws_bytes:
+            args.workspace, args.workspace_bytes = ws.data_ptr(), ws_bytes
+        n0 = lib.bfa_launch_count()
+        assert lib.bfa_fwd(ctypes.byref(pr), ctypes.byref(args),
+                           ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+        torch.cuda.synchronize()
+        assert lib.bfa_launch_count() - n0 == 1  # regular forward
+        assert _err(o, o_ref.cpu().double()) < TOL[torch.bfloat16]

@@ -37,11 +37,14 @@ def _problem_and_args(q, k, v, o, lse, do, dq, dk, dv, causal):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-def test_noalloc_backward_matches_bfa_bwd_twice(dtype):
+@pytest.mark.parametrize("dtype,S", [(torch.bfloat16, 640), (torch.float32, 640), (torch.bfloat16, 600)])
+def test_noalloc_backward_matches_bfa_bwd_twice(dtype, S):
+    """S=600 is not a multiple of 64, so each head's rows are padded inside
+    the static array (row pitch 640) and the second statistic starts past the
+    first one's padded rows."""
     lib = bfa_lib.load()
     g = torch.Generator().manual_seed(77)
-    B, Hq, Hkv, S, D = 2, 8, 2, 640, 128
+    B, Hq, Hkv, D = 2, 8, 2, 128
     q = torch.randn(B, Hq, S, D, generator=g).to(dtype).to(DEV)
     k = torch.randn(B, Hkv, S, D, generator=g).to(dtype).to(DEV)
     v = torch.randn(B, Hkv, S, D, generator=g).to(dtype).to(DEV)
@@ -71,3 +74,25 @@ def test_noalloc_rejects_problems_beyond_its_scratch():
     assert rc == bfa_lib.ERR_SCRATCH_LIMIT
     assert "2097152" in lib.bfa_strerror(rc).decode()
     assert lib.bfa_bwd_noalloc(None, None, None) == -1
+
+
+def test_noalloc_limit_edge_and_phase_rule():
+    """Host-side checks (no GPU): exactly 2^21 padded rows pass the size
+    check (the call then stops at the empty argument block), one more 64-row
+    tile does not; a phases mask without the Δ phase is rejected."""
+    lib = bfa_lib.load()
+    pr = bfa_lib.Problem()
+    pr.batch, pr.heads_q, pr.heads_kv, pr.seqlen_k, pr.head_dim = 1, 32, 8, 4096, 128
+    pr.dtype, pr.scale = bfa_lib.DTYPE_BF16, 0.088
+    pr.seqlen_q = bfa_lib.NOALLOC_MAX_ROWS // 32 - 63  # rounds up to exactly 2^16 rows per head
+    assert pr.heads_q * ((pr.seqlen_q + 63) // 64 * 64) == bfa_lib.NOALLOC_MAX_ROWS
+    rc = lib.bfa_bwd_noalloc(ctypes.byref(pr), None, None)
+    assert rc == -1  # past the size check: rejected for the missing arguments
+    pr.seqlen_q += 64
+    rc = lib.bfa_bwd_noalloc(ctypes.byref(pr), None, None)
+    assert rc == bfa_lib.ERR_SCRATCH_LIMIT
+    pr.seqlen_q = 256
+    args = bfa_lib.BwdArgs()
+    for phases in (bfa_lib.PHASE_DKDV, bfa_lib.PHASE_DQ, bfa_lib.PHASE_DKDV | bfa_lib.PHASE_DQ):
+        args.phases = phases
+        assert lib.bfa_bwd_noalloc(ctypes.byref(pr), ctypes.byref(args), None) == -1
