@@ -16,6 +16,7 @@ int launch_delta(const Params& p, int dtype, cudaStream_t st);
 // the fast path takes this problem; the launchers return a bfa_status.
 bool sm100_fwd_eligible(const Params& p, int dtype);
 int sm100_fwd(const Params& p, int dtype, cudaStream_t st);
+int sm100_fwd256(const Params& p, int dtype, cudaStream_t st);  // head_dim 256 (sm100_fwd256.cu)
 bool sm100_bwd_eligible(const Params& p, int dtype);
 int sm100_bwd(const Params& p, int dtype, cudaStream_t st);
 // One-kernel backward (sm100_bwd_fused.cu): `order` holds one counter per

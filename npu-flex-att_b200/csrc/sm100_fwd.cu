@@ -1,7 +1,7 @@
 // sm100_fwd.cu -- tcgen05 / TMA / TMEM flash-attention forward for B200.
 //
 // Replaces flash_attn_fwd_kernel (npu_flash_attention.py:17-166) for bf16/fp16
-// inputs with head_dim 64 or 128. Same math: S = QKᵀ·scale, optional soft-cap
+// inputs with head_dim 64 or 128 (head_dim 256 runs on sm100_fwd256.cu). Same math: S = QKᵀ·scale, optional soft-cap
 // and ALiBi, causal / sliding-window masks, online softmax in base 2, O = PV/l
 // and LSE = m + ln(l) in natural log.
 //
@@ -469,7 +469,7 @@ int dispatch_flags(const Params& p, const Tmaps4& tm, cudaStream_t st) {
 
 bool sm100_fwd_eligible(const Params& p, int dtype) {
   if (dtype != BFA_DTYPE_BF16 && dtype != BFA_DTYPE_F16) return false;
-  if (p.D != 64 && p.D != 128) return false;
+  if (p.D != 64 && p.D != 128 && p.D != 256) return false;
   if (p.Sq < 1 || p.Sk < 1 || p.B < 1 || p.Hq < 1) return false;
   if (!device_is_sm100()) return false;
   return tma_layout_ok(p.q, p.sq_, 2) && tma_layout_ok(p.k, p.sk_, 2) &&
@@ -477,6 +477,7 @@ bool sm100_fwd_eligible(const Params& p, int dtype) {
 }
 
 int sm100_fwd(const Params& p, int dtype, cudaStream_t st) {
+  if (p.D == 256) return sm100_fwd256(p, dtype, st);
   Tmaps4 tm;
   if (!make_tmap_bhsd(&tm.m[0], p.q, dtype, p.D, p.Sq, p.Hq, p.B, p.sq_, kBM) ||
       !make_tmap_bhsd(&tm.m[1], p.k, dtype, p.D, p.Sk, p.Hkv, p.B, p.sk_, kBN) ||

@@ -279,3 +279,27 @@ def test_training_loop_decreases_loss():
         _, dk, dv = nfa.npu_flash_attention_backward(q, k, v, out, lse, g, causal=True)
         k, v = k - 10.0 * dk, v - 10.0 * dv
     assert losses[-1] < losses[0]
+
+
+D256_CASES = [
+    # (dtype, sq, sk, causal, window, cap, alibi)
+    (torch.bfloat16, 300, 300, True, 0, 0.0, False),
+    (torch.bfloat16, 257, 257, False, 0, 0.0, False),
+    (torch.float16, 384, 384, True, 100, 0.0, False),
+    (torch.bfloat16, 520, 520, True, 0, 50.0, False),
+    (torch.bfloat16, 333, 333, True, 64, 50.0, True),
+    (torch.float16, 200, 450, False, 0, 5.0, False),   # cap with |s/cap| > 1/2 (exact tanh path)
+    (torch.bfloat16, 129, 1000, True, 0, 0.0, True),
+    (torch.bfloat16, 1, 130, False, 0, 0.0, False),
+]
+
+
+@pytest.mark.parametrize("case", D256_CASES, ids=lambda c: "{}-q{}-k{}-c{}-w{}-cap{}-a{}".format(
+    str(c[0]).split(".")[-1], *c[1:]))
+def test_head_dim_256(case):
+    """head_dim 256 (the tcgen05 D=256 forward): masks, soft-cap on both tanh
+    paths, ALiBi, GQA 2, ragged and Sq != Sk lengths."""
+    dt, sq, sk, causal, window, cap, alibi = case
+    q, k, v, go = _inputs(sq + 3 * sk, 1, 4, 2, sq, sk, 256, dt)
+    slopes = torch.tensor([2.0 ** (-8.0 * (i + 1) / 4) for i in range(4)]) if alibi else None
+    check_case(q, k, v, go, causal=causal, sliding_window=window, soft_cap=cap, alibi_slope=slopes)
