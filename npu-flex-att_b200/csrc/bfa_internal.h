@@ -19,6 +19,7 @@ int sm100_fwd(const Params& p, int dtype, cudaStream_t st);
 int sm100_fwd256(const Params& p, int dtype, cudaStream_t st);  // head_dim 256 (sm100_fwd256.cu)
 bool sm100_bwd_eligible(const Params& p, int dtype);
 int sm100_bwd(const Params& p, int dtype, cudaStream_t st);
+int sm100_bwd256(const Params& p, int dtype, cudaStream_t st);  // head_dim 256 (sm100_bwd256.cu)
 // One-kernel backward (sm100_bwd_fused.cu): `order` holds one counter per
 // 64-row query tile (B·Hq·Sq_pad/64), `dq_acc` an fp32 [B, Hq, Sq, D]
 // buffer (unused in accumulate mode).

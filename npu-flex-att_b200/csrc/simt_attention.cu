@@ -466,12 +466,15 @@ int simt_bwd(const Params& p, int dtype, cudaStream_t st) {
 int launch_delta(const Params& p, int dtype, cudaStream_t st) {
   const int64_t rows = (int64_t)p.B * p.Hq * p.Sq_pad;
   if (rows == 0) return BFA_OK;
-  if ((dtype == BFA_DTYPE_BF16 || dtype == BFA_DTYPE_F16) && (p.D == 64 || p.D == 128) &&
+  if ((dtype == BFA_DTYPE_BF16 || dtype == BFA_DTYPE_F16) && (p.D == 64 || p.D == 128 || p.D == 256) &&
       rows_vec_ok(p.o, p.so_, p.D) && rows_vec_ok(p.dout, p.sdo_, p.D)) {
     const int G = p.D / 8, per_block = 256 / G;
     const unsigned vblocks = (unsigned)((rows + per_block - 1) / per_block);
     const bool bf = dtype == BFA_DTYPE_BF16;
-    if (G == 16) {
+    if (G == 32) {
+      if (bf) delta_vec_kernel<__nv_bfloat16, 32><<<vblocks, 256, 0, st>>>(p);
+      else delta_vec_kernel<__half, 32><<<vblocks, 256, 0, st>>>(p);
+    } else if (G == 16) {
       if (bf) delta_vec_kernel<__nv_bfloat16, 16><<<vblocks, 256, 0, st>>>(p);
       else delta_vec_kernel<__half, 16><<<vblocks, 256, 0, st>>>(p);
     } else {

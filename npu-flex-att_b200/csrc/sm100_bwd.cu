@@ -2,7 +2,8 @@
 //
 // Replaces flash_attn_bwd_dkdv_kernel (npu_flash_attention.py:407-560),
 // flash_attn_bwd_dq_kernel (:298-402) and the host GQA sum (:735-737) for
-// bf16/fp16 inputs with head_dim 64 or 128. Per pair (i, j):
+// bf16/fp16 inputs with head_dim 64 or 128 (head_dim 256: sm100_bwd256.cu).
+// Per pair (i, j):
 //   P  = exp(u_ij − lse_i)        u = transformed logit (cap, ALiBi), masked
 //   dP = dO_i · V_j
 //   dS = P ∘ (dP − Δ_i) · scale · (1 − tanh²)   (tanh term only with soft-cap)
@@ -834,7 +835,7 @@ int dispatch_flags(const Params& p, int dtype, cudaStream_t st) {
 
 bool sm100_bwd_eligible(const Params& p, int dtype) {
   if (dtype != BFA_DTYPE_BF16 && dtype != BFA_DTYPE_F16) return false;
-  if (p.D != 64 && p.D != 128) return false;
+  if (p.D != 64 && p.D != 128 && p.D != 256) return false;
   if (p.Sq < 1 || p.Sk < 1 || p.B < 1 || p.Hq < 1) return false;
   if (!device_is_sm100()) return false;
   const int ges = p.grad_acc ? 4 : 2;
@@ -845,6 +846,7 @@ bool sm100_bwd_eligible(const Params& p, int dtype) {
 }
 
 int sm100_bwd(const Params& p, int dtype, cudaStream_t st) {
+  if (p.D == 256) return sm100_bwd256(p, dtype, st);
   const bool bf16 = dtype == BFA_DTYPE_BF16;
   if (p.D == 64) return bf16 ? dispatch_flags<64, true>(p, dtype, st) : dispatch_flags<64, false>(p, dtype, st);
   return bf16 ? dispatch_flags<128, true>(p, dtype, st) : dispatch_flags<128, false>(p, dtype, st);
