@@ -8,8 +8,6 @@
 
 #include <atomic>
 #include <climits>
-#include <cstdlib>
-#include <cstring>
 
 #include "bfa.h"
 #include "bfa_internal.h"
@@ -121,15 +119,10 @@ size_t bfa_fwd_workspace_bytes(const bfa_problem* pr) {
   return bfa::decode_workspace_bytes(make_params(pr), pr->dtype);
 }
 
-// Backward workspace, in this order:
-//   Δ and lse·log2(e), each [B, Hq, Sq_pad] fp32 with the row pitch padded to
-//   a multiple of 64 (one bulk copy per 64-row tile);
-//   one uint32 counter per 64-row query tile (the one-kernel backward's dQ
-//   order, B·Hq·Sq_pad/64);
-//   fp32 dQ [B, Hq, Sq, D] for the one-kernel backward.
-// A workspace that holds only the row statistics (+256 bytes of alignment
-// slack) runs the two-kernel backward; bfa_bwd_workspace_bytes() reports the
-// size that enables the one-kernel path where it exists.
+// Backward workspace: Δ and the row statistic lse2 (row_lse2), each
+// [B, Hq, Sq_pad] fp32 with the row pitch padded to a multiple of 64 (one
+// bulk copy per 64-row tile), plus 256 bytes of slack that covers the
+// padded rows of a last 128-row query tile.
 static int64_t padded_rows(int32_t sq) { return ((int64_t)sq + 63) / 64 * 64; }
 
 static size_t round256(size_t n) { return (n + 255) / 256 * 256; }
@@ -138,34 +131,11 @@ static size_t rowstat_bytes(const bfa_problem* pr) {
   return round256((size_t)pr->batch * pr->heads_q * padded_rows(pr->seqlen_q) * sizeof(float));
 }
 
-static size_t order_bytes(const bfa_problem* pr) {
-  return round256((size_t)pr->batch * pr->heads_q * (padded_rows(pr->seqlen_q) / 64) * 4);
-}
-
-static size_t dq_acc_bytes(const bfa_problem* pr) {
-  return round256((size_t)pr->batch * pr->heads_q * pr->seqlen_q * pr->head_dim * sizeof(float));
-}
-
 static size_t min_workspace_bytes(const bfa_problem* pr) { return 2 * rowstat_bytes(pr) + 256; }
-
-// Problems the one-kernel backward can take (the device check comes later).
-static bool fused_shape(const bfa_problem* pr) {
-  return pr->head_dim == 128 && (pr->dtype == BFA_DTYPE_BF16 || pr->dtype == BFA_DTYPE_F16);
-}
-
-// The one-kernel backward is opt-in (BFA_BWD_FUSED=1, read at each call): on
-// B200 its fp32 dQ reductions through L2 (one 64x128 tile per key tile and
-// query tile) cost more than recomputing S and dP in a separate dQ kernel.
-static bool fused_requested() {
-  const char* v = std::getenv("BFA_BWD_FUSED");
-  return v && std::strcmp(v, "1") == 0;
-}
 
 size_t bfa_bwd_workspace_bytes(const bfa_problem* pr) {
   if (check_problem(pr)) return 0;
-  size_t n = min_workspace_bytes(pr);
-  if (fused_shape(pr)) n += order_bytes(pr) + dq_acc_bytes(pr);
-  return n;
+  return min_workspace_bytes(pr);
 }
 
 static int fill_bwd(const bfa_problem* pr, const bfa_bwd_args* a, Params* p) {
@@ -224,17 +194,6 @@ int bfa_bwd(const bfa_problem* pr, const bfa_bwd_args* a, void* workspace, size_
     if (rc) return rc;
   }
   if (!(p.phases & (BFA_BWD_PHASE_DKDV | BFA_BWD_PHASE_DQ))) return BFA_OK;
-  // dK/dV and dQ in one kernel when both are asked for and the workspace has
-  // room for the dQ order counters (and, unless accumulating, the fp32 dQ).
-  const size_t need_fused = min_workspace_bytes(pr) + order_bytes(pr) +
-                            (p.grad_acc ? 0 : dq_acc_bytes(pr));
-  const uint32_t both = BFA_BWD_PHASE_DKDV | BFA_BWD_PHASE_DQ;
-  if ((p.phases & both) == both && fused_requested() && fused_shape(pr) && ws_bytes >= need_fused &&
-      bfa::sm100_bwd_fused_eligible(p, pr->dtype)) {
-    uint32_t* order = (uint32_t*)(ws + 2 * rowstat_bytes(pr));
-    float* dq_acc = (float*)(ws + 2 * rowstat_bytes(pr) + order_bytes(pr));
-    return bfa::sm100_bwd_fused(p, pr->dtype, order, dq_acc, st);
-  }
   if (bfa::sm100_bwd_eligible(p, pr->dtype)) return bfa::sm100_bwd(p, pr->dtype, st);
   return bfa::simt_bwd(p, pr->dtype, st);
 }

@@ -78,6 +78,35 @@ __device__ __forceinline__ float transform_logit(float dot, float scale, float c
   return s;
 }
 
+// ALiBi reference key g0 of query row i (absolute positions). The tcgen05
+// kernels form the bias of pair (i, j) as slope·(g0 - j) and fold the row
+// constant slope·(i - g0), which the softmax does not see, into the LSE
+// alone (the forward adds it to its LSE output; the backward's row statistic
+// is lse - slope·(i - g0), formed in double). For slope > 0 (the reference's
+// sign, npu_flash_attention.py:109) g0 is the row's first visible key in this
+// call, so the logits that carry the softmax stay O(1) instead of growing
+// with i - j: an fp32 logit near 6e4 (slope ~1 at 64k positions) has an ulp of
+// 4e-3, which shifts each probability by up to 0.3%. For slope <= 0 the bias
+// peaks at the diagonal and g0 = i (the bias is slope·(i - j) as written).
+__device__ __forceinline__ int64_t alibi_ref(const Params& p, float slope, int64_t gi) {
+  if (!(slope > 0.f)) return gi;
+  int64_t g0 = p.k_off;
+  if (p.window > 0) g0 = max(g0, gi - (int64_t)p.window);
+  return g0;
+}
+
+// Backward row statistic from the forward LSE of query row i of head hq:
+// lse·log2(e) minus the ALiBi row constant slope·(i - g0)·log2(e) that the
+// tcgen05 kernels keep out of their logits (alibi_ref). Formed in double, so
+// that the statistic carries exactly the fp32 LSE it was given.
+__device__ __forceinline__ float row_lse2(const Params& p, float lse, int hq, int i) {
+  if (!p.alibi) return lse * kLog2e;
+  const float slope = p.alibi[hq];
+  const int64_t gi = (int64_t)i + p.q_off;
+  const double shift = (double)slope * (double)(gi - alibi_ref(p, slope, gi));
+  return (float)(((double)lse - shift) * 1.4426950408889634);
+}
+
 // Kept key columns [lo, hi) for one query row: the columns are local keys
 // j0 + c, c in [0, n). `row_ok` false (a padding row) gives an empty range.
 __device__ __forceinline__ void keys_for_query(const Params& p, int64_t gi, bool row_ok, int j0,

@@ -20,12 +20,6 @@ int sm100_fwd256(const Params& p, int dtype, cudaStream_t st);  // head_dim 256 
 bool sm100_bwd_eligible(const Params& p, int dtype);
 int sm100_bwd(const Params& p, int dtype, cudaStream_t st);
 int sm100_bwd256(const Params& p, int dtype, cudaStream_t st);  // head_dim 256 (sm100_bwd256.cu)
-// One-kernel backward (sm100_bwd_fused.cu): `order` holds one counter per
-// 64-row query tile (B·Hq·Sq_pad/64), `dq_acc` an fp32 [B, Hq, Sq, D]
-// buffer (unused in accumulate mode).
-bool sm100_bwd_fused_eligible(const Params& p, int dtype);
-int sm100_bwd_fused(const Params& p, int dtype, uint32_t* order, float* dq_acc, cudaStream_t st);
-
 // Split-KV decoding forward (decode.cu): the G q-heads of a KV head have at
 // most 64 query rows. Its partial results live in a caller workspace of
 // decode_workspace_bytes() bytes (0: the problem never takes this path).

@@ -304,8 +304,9 @@ __global__ void __launch_bounds__(NT) simt_bwd_dkdv_kernel(Params p) {
 }
 
 // Δ = rowsum(O∘dO): one warp per (b, hq, i) row of pitch Sq_pad; rows past Sq
-// get Δ = 0. When `lse2` is set the kernel also writes lse·log2(e) there
-// (+inf for rows past Sq and rows whose LSE is −inf).
+// get Δ = 0. When `lse2` is set the kernel also writes the tcgen05 backward's
+// row statistic there: lse·log2(e), less the ALiBi row constant (row_lse2),
+// and +inf for rows past Sq and rows whose LSE is −inf.
 template <typename T>
 __global__ void __launch_bounds__(256) delta_kernel(Params p) {
   const int64_t warp = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -330,7 +331,7 @@ __global__ void __launch_bounds__(256) delta_kernel(Params p) {
       float l2 = __int_as_float(0x7f800000);
       if (i < p.Sq) {
         const float lse = p.lse[((int64_t)b * p.Hq + hq) * p.Sq + i];
-        if (lse != neg_inf()) l2 = lse * kLog2e;
+        if (lse != neg_inf()) l2 = row_lse2(p, lse, hq, i);
       }
       p.lse2[warp] = l2;
     }
@@ -369,7 +370,7 @@ __global__ void __launch_bounds__(256) delta_vec_kernel(Params p) {
       float l2 = __int_as_float(0x7f800000);
       if (i < p.Sq) {
         const float lse = p.lse[((int64_t)b * p.Hq + hq) * p.Sq + i];
-        if (lse != neg_inf()) l2 = lse * kLog2e;
+        if (lse != neg_inf()) l2 = row_lse2(p, lse, hq, i);
       }
       p.lse2[row] = l2;
     }

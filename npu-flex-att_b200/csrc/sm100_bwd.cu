@@ -267,8 +267,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tDb = tmem + lane_base + L::kTmemDP + 64 * bf;
       const float* rowv = (const float*)(smem + L::kOffRow + st * 512);
       const bool full = tile_full(p, q0, q0 + kInner, c0, c0 + kRows);
-      const float slope2 = ALIBI ? p.alibi[hq] * kLog2e : 0.f;
-      const float abase = ALIBI ? slope2 * (float)((int64_t)q0 + p.q_off - gj) : 0.f;
+      const float slope = ALIBI ? p.alibi[hq] : 0.f;
+      const float slope2 = slope * kLog2e;
+      // ALiBi bias slope·(g0_i - j) (alibi_ref): with slope > 0, g0_i =
+      // max(k_off, i - W) and the bias is the larger of the two terms
+      // below; with slope <= 0, g0_i = i (the second term alone).
+      const bool shifted = ALIBI && slope > 0.f;
+      const float ba = shifted ? slope2 * (float)(p.k_off - gj) : neg_inf();
+      const float bq = !ALIBI ? 0.f
+                       : !shifted ? slope2 * (float)((int64_t)q0 + p.q_off - gj)
+                       : p.window > 0 ? slope2 * (float)((int64_t)q0 + p.q_off - p.window - gj)
+                                      : neg_inf();
       int clo, chi;  // kept query columns [clo, chi) of this key row
       queries_for_key(p, gj, kj < p.Sk, q0, kInner, &clo, &chi);
       // One body per case (mask or not), chosen once per step: no branches
@@ -319,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               float pr, t = 0.f;
               if (CAP || ALIBI) {
                 float x = logit2<CAP>(raw, sl2, cap_in, cap_out, &t);
-                if (ALIBI) x = fmaf(slope2, (float)cc, x + abase);
+                if (ALIBI) x += fmaxf(ba, fmaf(slope2, (float)cc, bq));
                 pr = ex2(x - lse_c[h]);
               } else {
                 pr = ex2(fmaf(raw, sl2, -lse_c[h]));
@@ -607,7 +616,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float sl2 = p.scale * kLog2e;
     const float cap_in = CAP ? p.scale / p.soft_cap : 0.f;
     const float cap_out = CAP ? p.soft_cap * kLog2e : 0.f;
-    const float slope2 = ALIBI ? p.alibi[hq] * kLog2e : 0.f;
+    const float slope = ALIBI ? p.alibi[hq] : 0.f;
+    const float slope2 = slope * kLog2e;
+    const int64_t g0 = ALIBI ? alibi_ref(p, slope, gi) : gi;  // ALiBi bias slope·(g0 - j)
     const int64_t ridx = ((int64_t)b * p.Hq + hq) * p.Sq_pad + qi;
     const float lse2 = p.lse2[ridx];
     const float dlt = p.delta[ridx];
@@ -655,7 +666,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kSRead));
       const bool full = tile_full(p, q0, q0 + kRows, j0, j0 + NK);
-      const float abase = ALIBI ? slope2 * (float)(gi - (int64_t)j0 - p.k_off) : 0.f;
+      const float abase = ALIBI ? slope2 * (float)(g0 - (int64_t)j0 - p.k_off) : 0.f;
       int clo, chi;  // kept key columns [clo, chi) of this query row
       keys_for_query(p, gi, qi < p.Sq, j0, NK, &clo, &chi);
       uint8_t* ds_row = smem + L::kOffDS + eg * (kRows * 128);  // this warpgroup's 64 keys

@@ -330,8 +330,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tDb = tmem + lane_base + L::kTmemDP + 64 * bf + 32 * eg;
       const float* rowv = (const float*)(smem + L::kOffRow + e * L::kRowBytes);
       const bool full = tile_full(p, q0, q0 + kInner, c0, c0 + kRows);
-      const float slope2 = ALIBI ? p.alibi[hq] * kLog2e : 0.f;
-      const float abase = ALIBI ? slope2 * (float)((int64_t)q0 + p.q_off - gj) : 0.f;
+      const float slope = ALIBI ? p.alibi[hq] : 0.f;
+      const float slope2 = slope * kLog2e;
+      // ALiBi bias slope·(g0_i - j) (alibi_ref): with slope > 0, g0_i =
+      // max(k_off, i - W) and the bias is the larger of the two terms
+      // below; with slope <= 0, g0_i = i (the second term alone).
+      const bool shifted = ALIBI && slope > 0.f;
+      const float ba = shifted ? slope2 * (float)(p.k_off - gj) : neg_inf();
+      const float bq = !ALIBI ? 0.f
+                       : !shifted ? slope2 * (float)((int64_t)q0 + p.q_off - gj)
+                       : p.window > 0 ? slope2 * (float)((int64_t)q0 + p.q_off - p.window - gj)
+                                      : neg_inf();
       int clo, chi;  // kept query columns [clo, chi) of this key row
       queries_for_key(p, gj, kj < p.Sk, q0, kInner, &clo, &chi);
       uint32_t sr[32], dr[32];
@@ -350,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float raw = __uint_as_float(sr[c + h]);
             float t = 0.f;
             float x = (CAP || ALIBI) ? logit2<CAP>(raw, sl2, cap_in, cap_out, &t) : raw * sl2;
-            if (ALIBI) x = fmaf(slope2, (float)cc, x + abase);
+            if (ALIBI) x += fmaxf(ba, fmaf(slope2, (float)cc, bq));
             float pr = ex2(x - rowv[cc]);
             if (MASKED) pr = ((unsigned)(cc - clo) < (unsigned)(chi - clo)) ? pr : 0.f;
             if (DK) {
@@ -610,7 +619,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float sl2 = p.scale * kLog2e;
     const float cap_in = CAP ? p.scale / p.soft_cap : 0.f;
     const float cap_out = CAP ? p.soft_cap * kLog2e : 0.f;
-    const float slope2 = ALIBI ? p.alibi[hq] * kLog2e : 0.f;
+    const float slope = ALIBI ? p.alibi[hq] : 0.f;
+    const float slope2 = slope * kLog2e;
+    const int64_t g0 = ALIBI ? alibi_ref(p, slope, gi) : gi;  // ALiBi bias slope·(g0 - j)
     const int64_t ridx = ((int64_t)b * p.Hq + hq) * p.Sq_pad + qi;
     const float lse2 = p.lse2[ridx];
     const float dlt = p.delta[ridx];
@@ -658,7 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kDPRead));
       const bool full = tile_full(p, q0, q0 + kRows, j0, j0 + NK);
-      const float abase = ALIBI ? slope2 * (float)(gi - (int64_t)j0 - p.k_off) : 0.f;
+      const float abase = ALIBI ? slope2 * (float)(g0 - (int64_t)j0 - p.k_off) : 0.f;
       int clo, chi;  // kept key columns [clo, chi) of this query row
       keys_for_query(p, gi, qi < p.Sq, j0, NK, &clo, &chi);
       uint32_t dpk[16];

@@ -1,5 +1,5 @@
 // sm100_bwd_common.cuh -- device helpers shared by the tcgen05 backward kernels
-// (sm100_bwd.cu: separate dK/dV and dQ kernels; sm100_bwd_fused.cu: one kernel).
+// (sm100_bwd.cu: head_dim 64 / 128; sm100_bwd256.cu: head_dim 256).
 #pragma once
 
 #include <stdint.h>

@@ -257,7 +257,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float sl2 = p.scale * kLog2e;
     const float cap_in = CAP ? p.scale / p.soft_cap : 0.f;
     const float cap_out = CAP ? p.soft_cap * kLog2e : 0.f;
-    const float slope2 = ALIBI ? p.alibi[hq] * kLog2e : 0.f;
+    const float slope = ALIBI ? p.alibi[hq] : 0.f;
+    const float slope2 = slope * kLog2e;
+    // ALiBi: bias slope·(g0 - j); slope·(i - g0) goes into the LSE only.
+    const int64_t g0 = ALIBI ? alibi_ref(p, slope, gi) : gi;
     const int tr0 = q0 + t * kBM;
     float m = neg_inf(), l = 0.f;
     bool ok = true;
@@ -281,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // sum accumulators break the dependency chains.
       const bool full = tile_full(p, tr0, tr0 + kBM, c0, c0 + kBN);
       const bool store_x = CAP || ALIBI || !full || !(sl2 > 0.f);  // x != S * sl2
-      const float abase = ALIBI ? slope2 * (float)(gi - (int64_t)c0 - p.k_off) : 0.f;
+      const float abase = ALIBI ? slope2 * (float)(g0 - (int64_t)c0 - p.k_off) : 0.f;
       int clo, chi;  // kept key columns [clo, chi) of this row (all of them on a full tile)
       keys_for_query(p, gi, r_local < p.Sq, c0, kBN, &clo, &chi);
       if (full) {
@@ -426,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (good && r_local < p.Sq) {
       p.lse[((int64_t)b * p.Hq + hq) * p.Sq + r_local] =
-          (l > 0.f) ? (m + lg2(l)) * kLn2 : neg_inf();
+          (l > 0.f) ? fmaf(slope, (float)(gi - g0), (m + lg2(l)) * kLn2) : neg_inf();
     }
   }
 

@@ -253,7 +253,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float sl2 = p.scale * kLog2e;
     const float cap_in = CAP ? p.scale / p.soft_cap : 0.f;
     const float cap_out = CAP ? p.soft_cap * kLog2e : 0.f;
-    const float slope2 = ALIBI ? p.alibi[hq] * kLog2e : 0.f;
+    const float slope = ALIBI ? p.alibi[hq] : 0.f;
+    const float slope2 = slope * kLog2e;
+    // ALiBi: bias slope·(g0 - j); slope·(i - g0) goes into the LSE only.
+    const int64_t g0 = ALIBI ? alibi_ref(p, slope, gi) : gi;
     // cap_out · tanh(u) = u · (c0 + z (c1 + z (c2 + ...))), z = u^2.
     const float c0 = cap_out, c1 = cap_out * kT1, c2 = cap_out * kT2, c3 = cap_out * kT3,
                 c4 = cap_out * kT4, c5 = cap_out * kT5;
@@ -274,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       const bool full = tile_full(p, q0, q0 + kBM, c0k, c0k + kBN);
       const bool store_x = CAP || ALIBI || !full || !(sl2 > 0.f);  // x != S * sl2
-      const float abase = ALIBI ? slope2 * (float)(gi - (int64_t)c0k - p.k_off) : 0.f;
+      const float abase = ALIBI ? slope2 * (float)(g0 - (int64_t)c0k - p.k_off) : 0.f;
       int clo, chi;  // kept key columns [clo, chi) of this row
       keys_for_query(p, gi, r_local < p.Sq, c0k, kBN, &clo, &chi);
       if (full) {
@@ -450,7 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_store_wait_all();
     }
     if (good && r_local < p.Sq) {
-      p.lse[((int64_t)b * p.Hq + hq) * p.Sq + r_local] = (l > 0.f) ? (m + lg2(l)) * kLn2 : neg_inf();
+      p.lse[((int64_t)b * p.Hq + hq) * p.Sq + r_local] = (l > 0.f) ? fmaf(slope, (float)(gi - g0), (m + lg2(l)) * kLn2) : neg_inf();
     }
   }
 
