@@ -83,16 +83,17 @@ __device__ __forceinline__ float transform_logit(float dot, float scale, float c
 // constant slope·(i - g0), which the softmax does not see, into the LSE
 // alone (the forward adds it to its LSE output; the backward's row statistic
 // is lse - slope·(i - g0), formed in double). For slope > 0 (the reference's
-// sign, npu_flash_attention.py:109) g0 is the row's first visible key in this
-// call, so the logits that carry the softmax stay O(1) instead of growing
-// with i - j: an fp32 logit near 6e4 (slope ~1 at 64k positions) has an ulp of
-// 4e-3, which shifts each probability by up to 0.3%. For slope <= 0 the bias
-// peaks at the diagonal and g0 = i (the bias is slope·(i - j) as written).
+// sign, npu_flash_attention.py:109) g0 is the first key the row can see at
+// all, max(0, i - W) (0 without a window): the logits that carry the softmax
+// then stay O(1) instead of growing with i - j (an fp32 logit near 6e4,
+// slope ~1 at 64k positions, has an ulp of 4e-3, which shifts each
+// probability by up to 0.3%). g0 does not depend on the call's key offset, so
+// the row statistic agrees across the calls of a blockwise (context-parallel)
+// backward. For slope <= 0 the bias peaks at the diagonal and g0 = i (the
+// bias is slope·(i - j) as written).
 __device__ __forceinline__ int64_t alibi_ref(const Params& p, float slope, int64_t gi) {
   if (!(slope > 0.f)) return gi;
-  int64_t g0 = p.k_off;
-  if (p.window > 0) g0 = max(g0, gi - (int64_t)p.window);
-  return g0;
+  return p.window > 0 ? max((int64_t)0, gi - (int64_t)p.window) : (int64_t)0;
 }
 
 // Backward row statistic from the forward LSE of query row i of head hq:

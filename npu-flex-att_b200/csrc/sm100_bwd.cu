@@ -270,10 +270,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float slope = ALIBI ? p.alibi[hq] : 0.f;
       const float slope2 = slope * kLog2e;
       // ALiBi bias slope·(g0_i - j) (alibi_ref): with slope > 0, g0_i =
-      // max(k_off, i - W) and the bias is the larger of the two terms
-      // below; with slope <= 0, g0_i = i (the second term alone).
+      // max(0, i - W) and the bias is the larger of the two terms below;
+      // with slope <= 0, g0_i = i (the second term alone).
       const bool shifted = ALIBI && slope > 0.f;
-      const float ba = shifted ? slope2 * (float)(p.k_off - gj) : neg_inf();
+      const float ba = shifted ? slope2 * (float)(-gj) : neg_inf();
       const float bq = !ALIBI ? 0.f
                        : !shifted ? slope2 * (float)((int64_t)q0 + p.q_off - gj)
                        : p.window > 0 ? slope2 * (float)((int64_t)q0 + p.q_off - p.window - gj)
