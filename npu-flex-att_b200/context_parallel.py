@@ -138,8 +138,12 @@ class CudaBlockOps:
                 _bfa.bfa_dtype(o_part.dtype), ctypes.c_void_p(lse_p.data_ptr()),
                 ctypes.c_void_p(_bfa.stream_ptr(dev))))
 
-    def bwd_rows(self, q, k, o, do, lse, m: MaskArgs):
-        """Per-query-chunk state: Δ and the scaled LSE, computed once."""
+    def bwd_rows(self, q, k, o, do, lse, q_off, m: MaskArgs):
+        """Per-query-chunk state: Δ and the backward's row statistic, computed
+        once. The statistic depends on the rows' absolute positions (the
+        ALiBi row constant, alibi_ref in the library), so the chunk's
+        position offset is passed; it does not depend on the key offset, so
+        every key block of the ring can use it."""
         lib = _bfa.load()
         D = q.shape[-1]
         scale = m.scale if m.scale is not None else 1.0 / math.sqrt(D)
@@ -151,7 +155,7 @@ class CudaBlockOps:
         _nfa.npu_flash_attention_backward(
             q, k, k, o, lse, do, causal=m.causal, sliding_window=m.sliding_window,
             alibi_slope=m.alibi_slope, scale=m.scale, soft_cap=m.soft_cap,
-            _phases=_bfa.PHASE_DELTA, _workspace=ws, _outputs=(z, z, z))
+            q_pos_offset=q_off, _phases=_bfa.PHASE_DELTA, _workspace=ws, _outputs=(z, z, z))
         return ws
 
     def bwd_into(self, state, q, k, v, o, lse, do, q_off, k_off, m: MaskArgs,
@@ -214,7 +218,7 @@ def ring_backward(q, k, v, o, lse, do, rank: int, world: int, m: MaskArgs, ops):
     for ia in range(2):
         sl = slice(ia * C, ia * C + C)
         rows.append(ops.bwd_rows(q[:, :, sl], k, o[:, :, sl], do[:, :, sl],
-                                 lse[:, :, sl].contiguous(), m))
+                                 lse[:, :, sl].contiguous(), my[ia] * C, m))
     kv = (k, v)
     for t in range(world):
         src = (rank - t) % world

@@ -15,9 +15,12 @@ cast):
   c5  bf16 B1 Hq64 Hkv8 D128 S=65536, causal + ALiBi with slopes
       2^(-8(i+1)/64): the device runs the whole configuration; the
       oracle checks O, LSE and dQ of three 128-row query blocks
-      against all keys, and dK, dV of three 128-key blocks against
-      all queries, for KV heads 0 and 7 (q-heads 0-7 and 56-63,
-      the largest and the smallest slopes)
+      (first, middle, last) against all keys, and dK, dV of the
+      128-key blocks at 0, 1024 and 4096 against all queries, for KV
+      heads 0 and 7 (q-heads 0-7 and 56-63, the largest and the
+      smallest slopes). The positive ALiBi bias concentrates every
+      row's attention on the first few thousand keys, so key blocks
+      further out have gradients that are exactly zero in bf16.
 
 Each output and gradient is held to two bounds (the contract's absolute
 tolerances: fp32 1e-4, fp16 1e-2, bf16 2e-2; LSE 1e-3 relative):
@@ -200,7 +203,7 @@ def test_c4_bf16_d256_window_softcap(s):
 
 C5_KV_HEADS = (0, 7)
 C5_ROW_BLOCKS = (0, 32704, 65408)
-C5_KEY_BLOCKS = (0, 32768, 65408)
+C5_KEY_BLOCKS = (0, 1024, 4096)
 BLK = 128
 
 

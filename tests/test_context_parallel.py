@@ -37,7 +37,7 @@ class OracleBlockOps:
         o_acc.copy_(o_acc * wa.unsqueeze(-1) + o_part.to(o_acc.dtype) * wp.unsqueeze(-1))
         lse_acc.copy_(new)
 
-    def bwd_rows(self, q, k, o, do, lse, m):
+    def bwd_rows(self, q, k, o, do, lse, q_off, m):
         return None
 
     def bwd_into(self, state, q, k, v, o, lse, do, q_off, k_off, m, dq_acc, dk_acc, dv_acc):
