@@ -28,8 +28,6 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
-#include <cstdlib>
-#include <cstring>
 #include <mutex>
 #include <type_traits>
 
@@ -284,14 +282,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       queries_for_key(p, gj, kj < p.Sk, q0, kInner, &clo, &chi);
       // One body per case (mask or not), chosen once per step: no branches
       // inside the unrolled column loop.
-      auto step = [&](auto masked) {
+      const int half = eg;
+      uint32_t sr[32], dr[32];
+      tmem_ld32(tSb + 32 * half, sr);
+      tmem_ld32(tDb + 32 * half, dr);
+      tmem_ld_wait();
+      const bool small = CAP && cap_small<32>(sr, cap_in);
+      auto step = [&](auto masked, auto small_tag) {
         constexpr bool MASKED = decltype(masked)::value;
+        constexpr bool SMALL = decltype(small_tag)::value;
         {
-          const int half = eg;
-          uint32_t sr[32], dr[32];
-          tmem_ld32(tSb + 32 * half, sr);
-          tmem_ld32(tDb + 32 * half, dr);
-          tmem_ld_wait();
           uint32_t ppk[16], dpk[16];
 #pragma unroll
           for (int c = 0; c < 32; c += 4) {
@@ -329,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float raw = __uint_as_float(sr[c + h]);
               float pr, t = 0.f;
               if (CAP || ALIBI) {
-                float x = logit2<CAP>(raw, sl2, cap_in, cap_out, &t);
+                float x = logit2<CAP, SMALL>(raw, sl2, cap_in, cap_out, &t);
                 if (ALIBI) x += fmaxf(ba, fmaf(slope2, (float)cc, bq));
                 pr = ex2(x - lse_c[h]);
               } else {
@@ -353,8 +353,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st16(tDb + 32 * half, dpk);
         }
       };
-      if (full) step(std::false_type{});
-      else step(std::true_type{});
+      if (small) {
+        if (full) step(std::false_type{}, std::true_type{});
+        else step(std::true_type{}, std::true_type{});
+      } else {
+        if (full) step(std::false_type{}, std::false_type{});
+        else step(std::true_type{}, std::false_type{});
+      }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
@@ -369,339 +374,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       // In accumulate mode the fp32 tiles (2 x 128 x D x 4 bytes) go to the
       // Q/dO stages instead, which are free too; a key tile no query sees
       // adds nothing and skips the epilogue.
-      const bool acc = p.grad_acc != 0;
-      uint8_t* stage_dk = acc ? smem + L::kOffStage + kRows * D * 4 : smem + L::kOffK;
-      uint8_t* stage_dv = acc ? smem + L::kOffStage : smem + L::kOffV;
-      if (good && !(acc && n_iter == 0)) {
-        tc_fence_after();
-        if (acc) {
-          stage_tmem_row_f32<D>(tmem + lane_base + L::kTmemDV, stage_dv, row);
-          stage_tmem_row_f32<D>(tmem + lane_base + L::kTmemDK, stage_dk, row);
-        } else {
-          stage_tmem_row<D, BF16>(tmem + lane_base + L::kTmemDV, stage_dv, row, n_iter == 0);
-          stage_tmem_row<D, BF16>(tmem + lane_base + L::kTmemDK, stage_dk, row, n_iter == 0);
-        }
-        fence_async_shared();
-      }
-      if (lane == 0) warp_ok[wq] = good ? 1 : 0;
-      named_sync(1, 128);
-      if (wq == 0 && lane == 0 && warp_ok[0] && warp_ok[1] && warp_ok[2] && warp_ok[3]) {
-        if (!acc) {
-          for (int s = 0; s < L::kSub; ++s) {
-            tma_store_4d(&tmDV, smem_u32(stage_dv) + s * (kRows * 128), s * 64, c0, hkv, b);
-            tma_store_4d(&tmDK, smem_u32(stage_dk) + s * (kRows * 128), s * 64, c0, hkv, b);
-          }
-        } else if (n_iter > 0) {
-          for (int s = 0; s < D / 32; ++s) {
-            tma_reduce_add_4d(&tmDV, smem_u32(stage_dv) + s * (kRows * 128), s * 32, c0, hkv, b);
-            tma_reduce_add_4d(&tmDK, smem_u32(stage_dk) + s * (kRows * 128), s * 32, c0, hkv, b);
-          }
-        }
-        tma_store_commit();
-        tma_store_wait_all();
-      }
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 2) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
-// ============================================================== dK / dV, 128-query steps
-// dkdv_wide_kernel: the same work as dkdv_kernel in 128-query steps, so that
-// Sᵀ = K Qᵀ and dPᵀ = V dOᵀ run at N = 128 (the N = 64 tcgen05.mma costs
-// about 1.4x its nominal time). TMEM: Sᵀ [0, 128), dPᵀ [128, 256), dV at
-// 256, dK at 256 + D; Sᵀ / dPᵀ are single-buffered. To keep the tensor core
-// busy while the elementwise warps work, each warpgroup (query columns
-// [64w, 64w + 64)) handles its step in two 32-column chunks and signals each
-// one: the dV / dK MMAs over the first chunks' queries run while the second
-// chunks are computed. Pᵀ / dSᵀ are packed two per column over the
-// warpgroup's own fp32 columns: query q (0..63) of warpgroup w sits in
-// packed column 64w + q/2.
-// Per step: Sᵀ(i), dPᵀ(i) | wait chunk 0 | dV, dK over queries
-// {0-31, 64-95} | wait chunk 1 | dV, dK over {32-63, 96-127} | Sᵀ(i+1) ...
-template <int D>
-struct DkdvWideLayout {
-  static constexpr int kQ = 128;                        // queries per step
-  static constexpr int kSub = D / 64;
-  static constexpr int kStages = (D <= 64) ? 5 : 2;
-  static constexpr uint32_t kKVBytes = kRows * D * 2;    // K or V tile (128 keys)
-  static constexpr uint32_t kQBytes = kQ * D * 2;        // Q or dO tile (128 queries)
-  static constexpr uint32_t kOffK = 0;
-  static constexpr uint32_t kOffV = kOffK + kKVBytes;
-  static constexpr uint32_t kOffStage = kOffV + kKVBytes;
-  static constexpr uint32_t kStageBytes = 2 * kQBytes;
-  static constexpr uint32_t kOffRow = kOffStage + kStages * kStageBytes;  // lse2[128], delta[128] per stage
-  static constexpr uint32_t kOffBar = kOffRow + kStages * 1024;
-  static constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
-  static constexpr uint32_t kTmemS = 0, kTmemDP = 128, kTmemDV = 256, kTmemDK = 256 + D;
-  static_assert(kTmemDK + D <= 512, "TMEM budget");
-  static_assert(kSmemBytes <= 232448, "smem budget");
-  static_assert(kStages * kStageBytes >= 2u * kRows * D * 4, "fp32 dK/dV staging");
-};
-
-template <int D, bool BF16, bool CAP, bool ALIBI>
-__global__ void __launch_bounds__(kThreads, 1)
-    dkdv_wide_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
-                     const __grid_constant__ CUtensorMap tmDK, const __grid_constant__ CUtensorMap tmDV,
-                     const Params p) {
-  using L = DkdvWideLayout<D>;
-  constexpr int NS = L::kStages;
-  constexpr int NQ = L::kQ;
-  enum {
-    kKVFull = 0,
-    kQFull = 1,
-    kQEmpty = 1 + NS,
-    kSPFull = 1 + 2 * NS,  // Sᵀ(i), dPᵀ(i) in TMEM
-    kEW = kSPFull + 1,     // chunk c of Pᵀ(i) / dSᵀ(i) in TMEM (8 warps): kEW + c
-    kAccDone = kEW + 2,
-    kDrain = kAccDone + 1,
-    kNever = kDrain + 1,
-    kNumBars = kNever + 1
-  };
-
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw_addr = smem_u32(smem_raw);
-  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
-  const uint32_t sbase = smem_u32(smem);
-  auto bar = [&](int i) -> uint32_t { return sbase + L::kOffBar + 8u * (uint32_t)i; };
-  uint32_t* tmem_slot = (uint32_t*)(smem + L::kOffBar + 8 * kNumBars);
-  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
-  int* warp_ok = (int*)(tmem_slot + 2);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int BHkv = p.B * p.Hkv;
-  const int n_kt = (p.Sk + kRows - 1) / kRows;
-  const int grp = (int)(blockIdx.x / ((unsigned)kUnitGroup * n_kt));
-  const int gsize = min(kUnitGroup, BHkv - grp * kUnitGroup);
-  const int rem = (int)(blockIdx.x - (unsigned)grp * kUnitGroup * n_kt);
-  const int kt = rem / gsize;
-  const int bh = grp * kUnitGroup + rem % gsize;
-  const int hkv = bh % p.Hkv, b = bh / p.Hkv;
-  const int c0 = kt * kRows;
-  int qlo, qhi;
-  query_range(p, c0, min(c0 + kRows, p.Sk), &qlo, &qhi);
-  const int qt0 = qlo / NQ;
-  const int n_qt = (qhi > qlo) ? (qhi + NQ - 1) / NQ - qt0 : 0;
-  const int n_iter = n_qt * p.G;
-
-  WaitCtl ctl{abort_flag, p.status, p.timeout_ns};
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < kNumBars; ++i) mbar_init(bar(i), (i >= kEW && i < kEW + 2) ? 8u : 1u);
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 2) {
-    tmem_alloc(smem_u32(tmem_slot), 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      if (n_iter > 0) {
-        mbar_arrive_expect_tx(bar(kKVFull), 2 * L::kKVBytes);
-        for (int s = 0; s < L::kSub; ++s) {
-          tma_load_4d(sbase + L::kOffK + s * (kRows * 128), &tmK, bar(kKVFull), s * 64, c0, hkv, b);
-          tma_load_4d(sbase + L::kOffV + s * (kRows * 128), &tmV, bar(kKVFull), s * 64, c0, hkv, b);
-        }
-      }
-      int issued = 0;
-      for (int i = 0; i < n_iter; ++i) {
-        const int st = i % NS;
-        if (i >= NS && !mbar_wait(bar(kQEmpty + st), ((i / NS) & 1) ^ 1, ctl, BFA_ERR_DEVICE_TIMEOUT))
-          break;
-        const int hq = hkv * p.G + i / n_qt;
-        const int q0 = (qt0 + i % n_qt) * NQ;
-        const uint32_t qs = sbase + L::kOffStage + st * L::kStageBytes;
-        const int64_t rrow = ((int64_t)b * p.Hq + hq) * p.Sq_pad + q0;
-        const uint32_t rs = sbase + L::kOffRow + st * 1024;
-        mbar_arrive_expect_tx(bar(kQFull + st), L::kStageBytes + 1024);
-        for (int s = 0; s < L::kSub; ++s) {
-          tma_load_4d(qs + s * (NQ * 128), &tmQ, bar(kQFull + st), s * 64, q0, hq, b);
-          tma_load_4d(qs + L::kQBytes + s * (NQ * 128), &tmDO, bar(kQFull + st), s * 64, q0, hq, b);
-        }
-        // 128 rows of statistics; past Sq_pad they read the next head's rows
-        // or the workspace's slack, and every such query column is masked.
-        bulk_load(rs, p.lse2 + rrow, 512, bar(kQFull + st));
-        bulk_load(rs + 512, p.delta + rrow, 512, bar(kQFull + st));
-        issued = i + 1;
-      }
-      if (n_iter > 0) drain_wait(bar(kKVFull), 0, p.timeout_ns);
-      for (int i = (issued > NS ? issued - NS : 0); i < issued; ++i)
-        drain_wait(bar(kQFull + i % NS), (i / NS) & 1, p.timeout_ns);
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idT = idesc_f16(kRows, NQ, BF16, false);  // M = 128 keys, N = 128 queries
-      constexpr uint32_t idAcc = idesc_f16(kRows, D, BF16, true);
-      const uint64_t dK0 = desc_kmajor(sbase + L::kOffK), dV0 = desc_kmajor(sbase + L::kOffV);
-      bool ok = n_iter == 0 || mbar_wait(bar(kKVFull), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
-      for (int i = 0; i < n_iter && ok; ++i) {
-        const int st = i % NS;
-        const uint32_t qs = sbase + L::kOffStage + st * L::kStageBytes;
-        // Q / dO come by TMA; the Sᵀ / dPᵀ columns were last read by the
-        // elementwise warps of step i - 1 (ordered by its chunk-1 wait).
-        if (!(ok = mbar_wait(bar(kQFull + st), (i / NS) & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
-        tc_fence_after();
-        const uint64_t dq = desc_kmajor(qs), ddo = desc_kmajor(qs + L::kQBytes);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = ((kk >> 2) * (kRows * 128) + (kk & 3) * 32) >> 4;  // K, V, Q, dO: 128 rows
-          mma_ss(tmem + L::kTmemS, dK0 + off, dq + off, idT, kk > 0 ? 1u : 0u);
-          mma_ss(tmem + L::kTmemDP, dV0 + off, ddo + off, idT, kk > 0 ? 1u : 0u);
-        }
-        mma_commit(bar(kSPFull));
-        const uint64_t mq = desc_mnmajor(qs, NQ * 128), mdo = desc_mnmajor(qs + L::kQBytes, NQ * 128);
-        for (int c = 0; c < 2 && ok; ++c) {
-          if (!(ok = mbar_wait(bar(kEW + c), i & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
-          tc_fence_after();
-#pragma unroll
-          for (int w = 0; w < 2; ++w)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int kq = 4 * w + 2 * c + e;  // K-step of 16 queries
-              const uint32_t col = 64 * w + 16 * c + 8 * e;
-              const uint32_t acc = (i > 0 || c > 0 || w > 0 || e > 0) ? 1u : 0u;
-              mma_ts(tmem + L::kTmemDV, tmem + L::kTmemS + col, mdo + ((kq * 2048) >> 4), idAcc, acc);
-              mma_ts(tmem + L::kTmemDK, tmem + L::kTmemDP + col, mq + ((kq * 2048) >> 4), idAcc, acc);
-            }
-        }
-        if (!ok) break;
-        mma_commit(bar(kQEmpty + st));
-      }
-      mma_commit(bar(kAccDone));
-      mma_commit(bar(kDrain));
-      drain_wait(bar(kDrain), 0, p.timeout_ns);
-    }
-  } else if (warp >= 4) {
-    // ------------------------------------------------------------ elementwise
-    // Warpgroup h takes query columns [64h, 64h + 64) of every step, in two
-    // 32-column chunks; each thread owns one key row (TMEM lane).
-    const int eg = (warp - 4) >> 2;
-    const int wq = warp & 3;
-    const int row = wq * 32 + lane;  // key row within the tile
-    const int kj = c0 + row;
-    const int64_t gj = (int64_t)kj + p.k_off;
-    const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
-    const float sl2 = p.scale * kLog2e;
-    const float cap_in = CAP ? p.scale / p.soft_cap : 0.f;
-    const float cap_out = CAP ? p.soft_cap * kLog2e : 0.f;
-    bool ok = true;
-    for (int i = 0; i < n_iter && ok; ++i) {
-      const int st = i % NS;
-      const int hq = hkv * p.G + i / n_qt;
-      const int q0 = (qt0 + i % n_qt) * NQ;
-      uint32_t wbar = bar(kSPFull), wpar = (uint32_t)(i & 1);
-      if ((p.debug_flags & BFA_DEBUG_INJECT_STALL) && i == 0) {
-        wbar = bar(kNever);
-        wpar = 0;
-      }
-      if (!(ok = warp_wait(wbar, wpar, ctl))) break;
-      // The stage's lse2 / Δ arrived with its Q / dO (same barrier phase).
-      if (!(ok = warp_wait(bar(kQFull + st), (uint32_t)((i / NS) & 1), ctl))) break;
-      tc_fence_after();
-      const float* rowv = (const float*)(smem + L::kOffRow + st * 1024);
-      const bool full = tile_full(p, q0, q0 + NQ, c0, c0 + kRows);
-      const float slope = ALIBI ? p.alibi[hq] : 0.f;
-      const float slope2 = slope * kLog2e;
-      // ALiBi bias slope·(g0_i - j) (alibi_ref), as in dkdv_kernel.
-      const bool shifted = ALIBI && slope > 0.f;
-      const float ba = shifted ? slope2 * (float)(-gj) : neg_inf();
-      const float bq = !ALIBI ? 0.f
-                       : !shifted ? slope2 * (float)((int64_t)q0 + p.q_off - gj)
-                       : p.window > 0 ? slope2 * (float)((int64_t)q0 + p.q_off - p.window - gj)
-                                      : neg_inf();
-      int clo, chi;  // kept query columns [clo, chi) of this key row
-      queries_for_key(p, gj, kj < p.Sk, q0, NQ, &clo, &chi);
-      for (int c = 0; c < 2; ++c) {
-        const int cb = 64 * eg + 32 * c;  // first query column of the chunk
-        auto chunk = [&](auto masked) {
-          constexpr bool MASKED = decltype(masked)::value;
-          uint32_t sr[32], dr[32];
-          tmem_ld32(tmem + lane_base + L::kTmemS + cb, sr);
-          tmem_ld32(tmem + lane_base + L::kTmemDP + cb, dr);
-          tmem_ld_wait();
-          uint32_t ppk[16], dpk[16];
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            float pr2[2], ds2[2];
-            if (!CAP && !ALIBI) {
-              // Plain logits: two queries per packed instruction, which
-              // leaves issue slots to the MMA thread on the same sub-partition.
-              const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[e]), __uint_as_float(sr[e + 1])),
-                                          make_float2(sl2, sl2), make_float2(-rowv[cb + e], -rowv[cb + e + 1]));
-              pr2[0] = ex2(x.x);
-              pr2[1] = ex2(x.y);
-              const float2 dd = __fadd2_rn(make_float2(__uint_as_float(dr[e]), __uint_as_float(dr[e + 1])),
-                                           make_float2(-rowv[NQ + cb + e], -rowv[NQ + cb + e + 1]));
-              const float2 ds = __fmul2_rn(__fmul2_rn(make_float2(pr2[0], pr2[1]), dd), make_float2(p.scale, p.scale));
-              ds2[0] = ds.x;
-              ds2[1] = ds.y;
-              if (MASKED) {
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                  const bool keep = (unsigned)(cb + e + h - clo) < (unsigned)(chi - clo);
-                  pr2[h] = keep ? pr2[h] : 0.f;
-                  ds2[h] = keep ? ds2[h] : 0.f;
-                }
-              }
-            } else
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int cc = cb + e + h;
-              const float raw = __uint_as_float(sr[e + h]);
-              float t = 0.f;
-              float x = (CAP || ALIBI) ? logit2<CAP>(raw, sl2, cap_in, cap_out, &t) : raw * sl2;
-              if (ALIBI) x += fmaxf(ba, fmaf(slope2, (float)cc, bq));
-              float pr = ex2(x - rowv[cc]);
-              float ds = pr * (__uint_as_float(dr[e + h]) - rowv[NQ + cc]) * p.scale;
-              if (CAP) ds *= (1.f - t * t);
-              if (MASKED) {
-                // Masked columns include query rows past Sq, whose statistics
-                // are not this head's: select, never multiply, them away.
-                const bool keep = (unsigned)(cc - clo) < (unsigned)(chi - clo);
-                pr = keep ? pr : 0.f;
-                ds = keep ? ds : 0.f;
-              }
-              pr2[h] = pr;
-              ds2[h] = ds;
-            }
-            ppk[e / 2] = pack2<BF16>(pr2[0], pr2[1]);
-            dpk[e / 2] = pack2<BF16>(ds2[0], ds2[1]);
-          }
-          // Packed column 64w + q/2 for query q of the warpgroup: this chunk's
-          // 16 columns lie inside the warpgroup's fp32 columns already read.
-          tmem_st16(tmem + lane_base + L::kTmemS + 64 * eg + 16 * c, ppk);
-          tmem_st16(tmem + lane_base + L::kTmemDP + 64 * eg + 16 * c, dpk);
-        };
-        if (full) chunk(std::false_type{});
-        else chunk(std::true_type{});
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(kEW + c));
-      }
-    }
-    // Warpgroup 0 runs the epilogue; warpgroup 1 goes straight to the exit.
-    if (eg == 0) {
-      bool good = ok;
-      if (good && n_iter > 0) good = warp_wait(bar(kAccDone), 0, ctl);
-      good = good && !*abort_flag;
-      // K and V tiles are free once every MMA is done: they stage dK and dV.
-      // In accumulate mode the fp32 tiles go to the Q/dO stages instead; a
-      // key tile no query sees adds nothing and skips the epilogue.
       const bool acc = p.grad_acc != 0;
       uint8_t* stage_dk = acc ? smem + L::kOffStage + kRows * D * 4 : smem + L::kOffK;
       uint8_t* stage_dv = acc ? smem + L::kOffStage : smem + L::kOffV;
@@ -1005,8 +677,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int clo, chi;  // kept key columns [clo, chi) of this query row
       keys_for_query(p, gi, qi < p.Sq, j0, NK, &clo, &chi);
       uint8_t* ds_row = smem + L::kOffDS + eg * (kRows * 128);  // this warpgroup's 64 keys
-      auto step = [&](auto masked) {
+      const bool small = CAP && cap_small<64>(sr, cap_in);
+      auto step = [&](auto masked, auto small_tag) {
         constexpr bool MASKED = decltype(masked)::value;
+        constexpr bool SMALL = decltype(small_tag)::value;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           uint32_t dr[32];
@@ -1049,7 +723,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               float pr, t = 0.f;
               float x;
               if (CAP || ALIBI) {
-                x = logit2<CAP>(raw, sl2, cap_in, cap_out, &t);
+                x = logit2<CAP, SMALL>(raw, sl2, cap_in, cap_out, &t);
                 if (ALIBI) x = fmaf(-slope2, (float)cc, x + abase);
                 x -= lse2;
               } else {
@@ -1074,7 +748,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         return true;
       };
-      if (!(ok = full ? step(std::false_type{}) : step(std::true_type{}))) break;
+      if (small) ok = full ? step(std::false_type{}, std::true_type{}) : step(std::true_type{}, std::true_type{});
+      else ok = full ? step(std::false_type{}, std::false_type{}) : step(std::true_type{}, std::false_type{});
+      if (!ok) break;
       fence_async_shared();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kDSFull));
@@ -1123,42 +799,10 @@ bool set_smem(K kern, uint32_t bytes) {
          cudaSuccess;
 }
 
-// dK/dV kernel choice: BFA_DKDV_WIDE=1 (read at each call) takes the
-// 128-query-step kernel.
-bool dkdv_wide() {
-  const char* v = std::getenv("BFA_DKDV_WIDE");
-  return v && std::strcmp(v, "1") == 0;
-}
-
-template <int D, bool BF16, bool CAP, bool ALIBI>
-int launch_dkdv_wide(const Params& p, int dtype, int gdt, cudaStream_t st) {
-  using L = DkdvWideLayout<D>;
-  auto kern = dkdv_wide_kernel<D, BF16, CAP, ALIBI>;
-  static std::once_flag once;
-  static bool attr_ok = false;
-  std::call_once(once, [&] { attr_ok = set_smem(kern, L::kSmemBytes); });
-  if (!attr_ok) return BFA_ERR_CUDA;
-  CUtensorMap m[6];
-  if (!make_tmap_bhsd(&m[0], p.k, dtype, D, p.Sk, p.Hkv, p.B, p.sk_, kRows) ||
-      !make_tmap_bhsd(&m[1], p.v, dtype, D, p.Sk, p.Hkv, p.B, p.sv_, kRows) ||
-      !make_tmap_bhsd(&m[2], p.q, dtype, D, p.Sq, p.Hq, p.B, p.sq_, L::kQ) ||
-      !make_tmap_bhsd(&m[3], p.dout, dtype, D, p.Sq, p.Hq, p.B, p.sdo_, L::kQ) ||
-      !make_tmap_bhsd(&m[4], p.dk, gdt, D, p.Sk, p.Hkv, p.B, p.sdk_, kRows) ||
-      !make_tmap_bhsd(&m[5], p.dv, gdt, D, p.Sk, p.Hkv, p.B, p.sdv_, kRows))
-    return BFA_ERR_CUDA;
-  const unsigned grid = (unsigned)((p.Sk + kRows - 1) / kRows) * p.Hkv * p.B;
-  kern<<<grid, kThreads, L::kSmemBytes, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], p);
-  note_launch();
-  return cudaGetLastError() == cudaSuccess ? BFA_OK : BFA_ERR_CUDA;
-}
-
 template <int D, bool BF16, bool CAP, bool ALIBI>
 int launch_bwd(const Params& p, int dtype, cudaStream_t st) {
   const int gdt = p.grad_acc ? BFA_DTYPE_F32 : dtype;  // dtype of dq/dk/dv
-  if ((p.phases & BFA_BWD_PHASE_DKDV) && dkdv_wide()) {
-    const int rc = launch_dkdv_wide<D, BF16, CAP, ALIBI>(p, dtype, gdt, st);
-    if (rc) return rc;
-  } else if (p.phases & BFA_BWD_PHASE_DKDV) {
+  if (p.phases & BFA_BWD_PHASE_DKDV) {
     using L = DkdvLayout<D>;
     auto kern = dkdv_kernel<D, BF16, CAP, ALIBI>;
     static std::once_flag once;

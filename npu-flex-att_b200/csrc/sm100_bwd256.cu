@@ -348,8 +348,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (DK) tmem_ld32(tDb, dr);
       tmem_ld_wait();
       uint32_t pk[16];
-      auto body = [&](auto masked) {
+      auto body = [&](auto masked, auto small_tag) {
         constexpr bool MASKED = decltype(masked)::value;
+        constexpr bool SMALL = decltype(small_tag)::value;
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
           float v2[2];
@@ -358,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int cc = 32 * eg + c + h;
             const float raw = __uint_as_float(sr[c + h]);
             float t = 0.f;
-            float x = (CAP || ALIBI) ? logit2<CAP>(raw, sl2, cap_in, cap_out, &t) : raw * sl2;
+            float x = (CAP || ALIBI) ? logit2<CAP, SMALL>(raw, sl2, cap_in, cap_out, &t) : raw * sl2;
             if (ALIBI) x += fmaxf(ba, fmaf(slope2, (float)cc, bq));
             float pr = ex2(x - rowv[cc]);
             if (MASKED) pr = ((unsigned)(cc - clo) < (unsigned)(chi - clo)) ? pr : 0.f;
@@ -373,8 +374,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           pk[c / 2] = pack2<BF16>(v2[0], v2[1]);
         }
       };
-      if (full) body(std::false_type{});
-      else body(std::true_type{});
+      if (CAP && cap_small<32>(sr, cap_in)) {
+        if (full) body(std::false_type{}, std::true_type{});
+        else body(std::true_type{}, std::true_type{});
+      } else {
+        if (full) body(std::false_type{}, std::false_type{});
+        else body(std::true_type{}, std::false_type{});
+      }
       // The row statistics are in registers' use: release the entry.
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kREmpty + e));
@@ -673,8 +679,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int clo, chi;  // kept key columns [clo, chi) of this query row
       keys_for_query(p, gi, qi < p.Sq, j0, NK, &clo, &chi);
       uint32_t dpk[16];
-      auto body = [&](auto masked) {
+      auto body = [&](auto masked, auto small_tag) {
         constexpr bool MASKED = decltype(masked)::value;
+        constexpr bool SMALL = decltype(small_tag)::value;
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
           float ds2[2];
@@ -683,7 +690,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int cc = 32 * eg + c + h;
             const float raw = __uint_as_float(sr[c + h]);
             float t = 0.f;
-            float x = (CAP || ALIBI) ? logit2<CAP>(raw, sl2, cap_in, cap_out, &t) : raw * sl2;
+            float x = (CAP || ALIBI) ? logit2<CAP, SMALL>(raw, sl2, cap_in, cap_out, &t) : raw * sl2;
             if (ALIBI) x = fmaf(-slope2, (float)cc, x + abase);
             float pr = ex2(x - lse2);
             if (MASKED) pr = ((unsigned)(cc - clo) < (unsigned)(chi - clo)) ? pr : 0.f;
@@ -694,8 +701,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           dpk[c / 2] = pack2<BF16>(ds2[0], ds2[1]);
         }
       };
-      if (full) body(std::false_type{});
-      else body(std::true_type{});
+      if (CAP && cap_small<32>(sr, cap_in)) {
+        if (full) body(std::false_type{}, std::true_type{});
+        else body(std::true_type{}, std::true_type{});
+      } else {
+        if (full) body(std::false_type{}, std::false_type{});
+        else body(std::true_type{}, std::false_type{});
+      }
       // dS of this warpgroup's 32 keys -> 16-byte chunks [4h, 4h + 4) of this
       // row of the swizzled [128 rows][64 keys] tile, once dQ(j-1) has read it.
       if (j > 0 && !(ok = warp_wait(bar(kDSFree), (uint32_t)((j - 1) & 1), ctl))) break;

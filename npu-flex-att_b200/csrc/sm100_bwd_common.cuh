@@ -31,11 +31,14 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 }
 
 // Logit in the base-2 domain: (cap·tanh(s·scale/cap) or s·scale)·log2(e).
-// `t` receives tanh(s·scale/cap) for the soft-cap chain.
-template <bool CAP>
+// `t` receives tanh(s·scale/cap) for the soft-cap chain. SMALL selects
+// tanh_small (every |s·scale/cap| of the warp's step is <= 1/2, see
+// cap_small), else tanh_any.
+template <bool CAP, bool SMALL = false>
 __device__ __forceinline__ float logit2(float raw, float sl2, float cap_in, float cap_out, float* t) {
   if (CAP) {
-    const float th = tanh_exp(raw * cap_in);
+    const float u = raw * cap_in;
+    const float th = SMALL ? tanh_small(u) : tanh_any(u);
     *t = th;
     return cap_out * th;
   }

@@ -305,19 +305,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int e = 0; e < 32; e += 2)
               m4[(e >> 1) & 3] = fmax3(m4[(e >> 1) & 3], __uint_as_float(r[ch][e]), __uint_as_float(r[ch][e + 1]));
         } else {
+          // Soft-cap tanh: tanh_small on the FMA pipe when every raw logit
+          // of the warp's step has |s/cap| <= 1/2, else tanh_any.
+          auto form = [&](auto small_tag) {
+            constexpr bool SMALL = decltype(small_tag)::value;
 #pragma unroll
-          for (int ch = 0; ch < kBN / 32; ++ch) {
+            for (int ch = 0; ch < kBN / 32; ++ch) {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const int c = 32 * ch + e;
-              const float raw = __uint_as_float(r[ch][e]);
-              float x = CAP ? cap_out * tanh_exp(raw * cap_in) : raw * sl2;
-              if (ALIBI) x = fmaf(-slope2, (float)c, x + abase);
-              x = ((unsigned)(c - clo) < (unsigned)(chi - clo)) ? x : neg_inf();
-              r[ch][e] = __float_as_uint(x);
-              m4[e & 3] = fmaxf(m4[e & 3], x);
+              for (int e = 0; e < 32; ++e) {
+                const int c = 32 * ch + e;
+                const float raw = __uint_as_float(r[ch][e]);
+                float x = raw * sl2;
+                if (CAP) x = cap_out * (SMALL ? tanh_small(raw * cap_in) : tanh_any(raw * cap_in));
+                if (ALIBI) x = fmaf(-slope2, (float)c, x + abase);
+                x = ((unsigned)(c - clo) < (unsigned)(chi - clo)) ? x : neg_inf();
+                r[ch][e] = __float_as_uint(x);
+                m4[e & 3] = fmaxf(m4[e & 3], x);
+              }
             }
+          };
+          bool small = false;
+          if (CAP) {
+            float am = 0.f;
+#pragma unroll
+            for (int ch = 0; ch < kBN / 32; ++ch)
+#pragma unroll
+              for (int e = 0; e < 32; e += 2)
+                am = fmax3(am, fabsf(__uint_as_float(r[ch][e])), fabsf(__uint_as_float(r[ch][e + 1])));
+            small = __all_sync(0xffffffffu, am * cap_in <= 0.5f);
           }
+          if (small) form(std::true_type{});
+          else form(std::false_type{});
         }
         mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
         if (!store_x) mx *= sl2;

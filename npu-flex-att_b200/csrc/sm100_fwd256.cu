@@ -13,15 +13,17 @@
 // MMAs consume them:
 //   S(0): K0[dims 0-127], K0[dims 128-255]   S(1): K1 lo, K1 hi
 //   PV(0): V0[keys 0-63], V0[keys 64-127]    S(2): K2 lo, K2 hi   PV(1) ...
-// Warp roles (256 threads):
+// Warp roles (384 threads):
 //   warp 0      TMA producer: Q once (64 KB), then the ring units
 //   warp 1      MMA issuer: S(j) = Q K_jᵀ (M=128, N=128, 16 K-steps), and
 //               O += P(j) V_j (M=128, N=256, TS form: P read from TMEM)
 //   warp 2      TMEM allocator (512 columns: S0, S1, O)
-//   warps 4-7   softmax: each thread owns one query row (one TMEM lane),
-//               reads its 128-column S row, writes P (16-bit) over the first
-//               64 columns of that S buffer, rescales its O row when the
-//               running max grows by more than 2^8, and writes O and the LSE.
+//   warps 4-11  softmax, two warpgroups over the same 128 query rows (one
+//               TMEM lane per thread): warpgroup h reads keys [64h, 64h + 64)
+//               of the S row, the two exchange the row maximum, and each
+//               writes its P (16-bit) into packed columns [32h, 32h + 32) of
+//               that S buffer and rescales O columns [128h, 128h + 128) when
+//               the running max grows by more than 2^8; then O and the LSE.
 // MMA order S(0), S(1), PV(0), S(2), PV(1), S(3), ...: the softmax of step j
 // overlaps PV(j-1) and S(j+1) on the tensor core.
 //
@@ -29,8 +31,8 @@
 // logits |s/cap| is small, and tanh there is evaluated on the FMA pipe by its
 // odd Taylor series to u^11 (truncation error < 1e-6 relative for |u| <= 1/2),
 // which leaves the MUFU unit to the exponentials. A step whose raw logits of
-// some row in the warp reach |s/cap| > 1/2 uses the exact form
-// 1 - 2/(1 + e^{2u}) instead (warp-uniform choice per step).
+// some row in the warp reach |s/cap| > 1/2 uses tanh_any, the closed form
+// 1 - 2/(1 + e^{2u}) (warp-uniform choice per step).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -49,8 +51,8 @@ using namespace sm100;
 constexpr int kD = 256;
 constexpr int kBM = 128;  // query rows per CTA (TMEM lanes)
 constexpr int kBN = 128;  // keys per step
-constexpr int kThreads = 256;
-constexpr int kStages = 5;                        // ring units in flight
+constexpr int kThreads = 384;
+constexpr int kStages = 4;                        // ring units in flight
 constexpr uint32_t kUnitBytes = 32768;            // one ring unit
 constexpr uint32_t kQSub = kBM * 128;             // [128 rows][64 dims], 128-byte swizzle
 constexpr uint32_t kQBytes = 4 * kQSub;           // 64 KB
@@ -58,7 +60,8 @@ constexpr uint32_t kKSub = kBN * 128;             // [128 keys][64 dims]
 constexpr uint32_t kVSub = 64 * 128;              // [64 keys][64 dims]
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffRing = kQBytes;
-constexpr uint32_t kOffBar = kOffRing + kStages * kUnitBytes;
+constexpr uint32_t kOffX = kOffRing + kStages * kUnitBytes;  // row-maximum exchange, 2 KB
+constexpr uint32_t kOffBar = kOffX + 2 * 2 * kBM * 4;
 constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
 constexpr uint32_t kTmemS = 0;       // S(b) at 128·b, fp32; P(b) packed over its first 64 columns
 constexpr uint32_t kTmemO = 2 * kBN; // O: 256 fp32 columns
@@ -115,7 +118,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     kSFull = 1 + 2 * NS,
     kPFull = kSFull + 2,
     kODone = kPFull + 2,
-    kDrain = kODone + 1,
+    kXch = kODone + 1,  // row-maximum exchange of parity b (8 softmax warps)
+    kXchL = kXch + 2,   // row-sum exchange in the epilogue (8 softmax warps)
+    kDrain = kXchL + 1,
     kNever = kDrain + 1,
     kNumBars = kNever + 1
   };
@@ -145,7 +150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; ++i)
-      mbar_init(bar(i), (i >= kPFull && i < kPFull + 2) ? 4u : 1u);
+      mbar_init(bar(i), ((i >= kPFull && i < kPFull + 2) || (i >= kXch && i <= kXchL)) ? 8u : 1u);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -244,12 +249,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ softmax
+    // Two warpgroups split every step's 128 keys: warpgroup h forms and
+    // exponentiates keys [64h, 64h + 64) and rescales O columns
+    // [128h, 128h + 128) of the same 128 rows (lane = row in both). They
+    // exchange each row's partial maximum through shared memory, so both
+    // derive the same running maximum; each keeps its partial row sum.
+    const int eg = (warp - 4) >> 2;
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
     const int r_local = q0 + row;
     const int64_t gi = (int64_t)r_local + p.q_off;
     const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
-    const uint32_t tO = tmem + lane_base + kTmemO;
+    const uint32_t tO = tmem + lane_base + kTmemO + 128 * eg;
+    float* xchg = (float*)(smem + kOffX);  // [parity][warpgroup][row]
     const float sl2 = p.scale * kLog2e;
     const float cap_in = CAP ? p.scale / p.soft_cap : 0.f;
     const float cap_out = CAP ? p.soft_cap * kLog2e : 0.f;
@@ -284,17 +296,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         clo = 0;
         chi = kBN;
       }
-      uint32_t r[kBN / 32][32];
-#pragma unroll
-      for (int ch = 0; ch < kBN / 32; ++ch) tmem_ld32(tS + 32 * ch, r[ch]);
+      uint32_t r[2][32];  // this warpgroup's keys [64h, 64h + 64)
+      tmem_ld32(tS + 64 * eg, r[0]);
+      tmem_ld32(tS + 64 * eg + 32, r[1]);
       tmem_ld_wait();
 
-      float mx;
+      float pm;  // partial maximum over this warpgroup's keys
       {
         float m4[4] = {neg_inf(), neg_inf(), neg_inf(), neg_inf()};
         if (!store_x) {
 #pragma unroll
-          for (int ch = 0; ch < kBN / 32; ++ch)
+          for (int ch = 0; ch < 2; ++ch)
 #pragma unroll
             for (int e = 0; e < 32; e += 2)
               m4[(e >> 1) & 3] = fmax3(m4[(e >> 1) & 3], __uint_as_float(r[ch][e]), __uint_as_float(r[ch][e + 1]));
@@ -303,10 +315,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           auto form = [&](auto poly_tag) {
             constexpr bool POLY = decltype(poly_tag)::value;
 #pragma unroll
-            for (int ch = 0; ch < kBN / 32; ++ch) {
+            for (int ch = 0; ch < 2; ++ch) {
 #pragma unroll
               for (int e = 0; e < 32; e += 2) {
-                const int c = 32 * ch + e;
+                const int c = 64 * eg + 32 * ch + e;
                 float2 x2;
                 const float2 raw2 = make_float2(__uint_as_float(r[ch][e]), __uint_as_float(r[ch][e + 1]));
                 if (CAP) {
@@ -320,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     q = __ffma2_rn(z, q, make_float2(c0, c0));
                     x2 = __fmul2_rn(u, q);
                   } else {
-                    x2 = make_float2(cap_out * tanh_exp(u.x), cap_out * tanh_exp(u.y));
+                    x2 = make_float2(cap_out * tanh_any(u.x), cap_out * tanh_any(u.y));
                   }
                 } else {
                   x2 = __fmul2_rn(raw2, make_float2(sl2, sl2));
@@ -337,26 +349,27 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           };
-          if (CAP) {
-            // |s/cap| <= 1/2 for every raw logit of every row in the warp?
-            float am = 0.f;
-#pragma unroll
-            for (int ch = 0; ch < kBN / 32; ++ch)
-#pragma unroll
-              for (int e = 0; e < 32; e += 2)
-                am = fmax3(am, fabsf(__uint_as_float(r[ch][e])), fabsf(__uint_as_float(r[ch][e + 1])));
-            if (__all_sync(0xffffffffu, am * cap_in <= 0.5f)) form(std::true_type{});
-            else form(std::false_type{});
-          } else {
-            form(std::false_type{});
-          }
+          if (CAP && cap_small<32>(r[0], cap_in) && cap_small<32>(r[1], cap_in)) form(std::true_type{});
+          else form(std::false_type{});
         }
-        mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-        if (!store_x) mx *= sl2;
+        pm = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        if (!store_x) pm *= sl2;
       }
+      // The row maximum over both halves, through shared memory and an
+      // mbarrier (a bounded wait: a warpgroup that gave up cannot strand the
+      // other one). The other warpgroup has loaded its S columns once it has
+      // arrived, so P may then be written over them. Two parity buffers: a
+      // slot is rewritten two steps later, after the other warpgroup has
+      // arrived in between, i.e. read it.
+      xchg[(bf * 2 + eg) * kBM + row] = pm;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kXch + bf));
+      if (!(ok = warp_wait(bar(kXch + bf), (uint32_t)((it >> 1) & 1), ctl))) break;
+      const float mx = fmaxf(pm, xchg[(bf * 2 + (eg ^ 1)) * kBM + row]);
       // Raise the reference max only when it grows by more than the
       // threshold (or is still -inf); warp-uniform, because the O rescale
-      // uses warp-collective TMEM loads / stores.
+      // uses warp-collective TMEM loads / stores. Both warpgroups see the
+      // same maxima for the same 32 rows, so they decide alike.
       const bool grow = (mx > m + kRescaleThreshold) || (m == neg_inf() && mx != neg_inf());
       const bool any_grow = __any_sync(0xffffffffu, grow);
       const bool rescale = any_grow && it > 0;
@@ -370,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto exps = [&](auto split) {
         constexpr bool SPLIT = decltype(split)::value && kPolyEvery > 0;
 #pragma unroll
-        for (int ch = 0; ch < kBN / 32; ++ch) {
+        for (int ch = 0; ch < 2; ++ch) {
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
@@ -380,7 +393,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             s2[(e >> 1) & 1] = __fadd2_rn(s2[(e >> 1) & 1], make_float2(p0, p1));
             pk[e / 2] = pack2<BF16>(p0, p1);
           }
-          tmem_st16(tS + 16 * ch, pk);
+          // Keys [64h + 32ch, +32) -> packed columns [32h + 16ch, +16).
+          tmem_st16(tS + 32 * eg + 16 * ch, pk);
         }
       };
       if (full) exps(std::true_type{});
@@ -398,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (rescale) {
 #pragma unroll 1
-        for (int c = 0; c < kD / 32; ++c) {
+        for (int c = 0; c < 128 / 32; ++c) {
           uint32_t o[32];
           tmem_ld32(tO + 32 * c, o);
           tmem_ld_wait();
@@ -414,16 +428,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     // ------------------------------------------------------------ epilogue
+    // Row sum: the two partial sums, exchanged through the parity buffer the
+    // last step did not use (the other warpgroup read it before arriving at
+    // that step's exchange), with a bounded wait.
     bool good = ok;
     if (good && n_iter > 0) good = warp_wait(bar(kODone), (uint32_t)((n_iter - 1) & 1), ctl);
+    const int lp = (n_iter & 1) * 2;
+    xchg[(lp + eg) * kBM + row] = l;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar(kXchL));
+    good = warp_wait(bar(kXchL), 0, ctl) && good;
+    const float l_tot = l + xchg[(lp + (eg ^ 1)) * kBM + row];
     // The Q tile is free once the last S MMA has run (MMAs complete in
-    // order, and PV(n-1) came after it): it stages O.
+    // order, and PV(n-1) came after it): it stages O, warpgroup h its
+    // columns [128h, 128h + 128) (sub-tiles 2h, 2h + 1).
     uint8_t* Ot = smem + kOffQ;
     if (good) {
       tc_fence_after();
-      const float inv = (l > 0.f) ? 1.f / l : 0.f;
+      const float inv = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
 #pragma unroll 1
-      for (int c = 0; c < kD / 32; ++c) {
+      for (int c = 0; c < 128 / 32; ++c) {
         uint32_t o[32];
         if (n_iter > 0) {
           tmem_ld32(tO + 32 * c, o);
@@ -439,24 +463,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           v.y = pack2<BF16>(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv);
           v.z = pack2<BF16>(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv);
           v.w = pack2<BF16>(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv);
-          const int col = 32 * c + 8 * q;
+          const int col = 128 * eg + 32 * c + 8 * q;
           *reinterpret_cast<uint4*>(Ot + (col >> 6) * kQSub + sw128_offset(row, (col & 63) >> 3)) = v;
         }
       }
       fence_async_shared();
     }
-    if (lane == 0) warp_ok[wq] = good ? 1 : 0;
-    named_sync(1, 128);
-    if (wq == 0 && lane == 0 && warp_ok[0] && warp_ok[1] && warp_ok[2] && warp_ok[3]) {
-      for (int s = 0; s < 4; ++s) tma_store_4d(&tmO, smem_u32(Ot) + s * kQSub, s * 64, q0, hq, b);
-      tma_store_commit();
-      tma_store_wait_all();
+    if (lane == 0) warp_ok[warp - 4] = good ? 1 : 0;
+    named_sync(3, 256);
+    if (warp == 4 && lane == 0) {
+      bool all = true;
+      for (int w = 0; w < 8; ++w) all = all && warp_ok[w];
+      if (all) {
+        for (int s = 0; s < 4; ++s) tma_store_4d(&tmO, smem_u32(Ot) + s * kQSub, s * 64, q0, hq, b);
+        tma_store_commit();
+        tma_store_wait_all();
+      }
     }
-    if (good && r_local < p.Sq) {
-      p.lse[((int64_t)b * p.Hq + hq) * p.Sq + r_local] = (l > 0.f) ? fmaf(slope, (float)(gi - g0), (m + lg2(l)) * kLn2) : neg_inf();
+    if (good && eg == 0 && r_local < p.Sq) {
+      p.lse[((int64_t)b * p.Hq + hq) * p.Sq + r_local] =
+          (l_tot > 0.f) ? fmaf(slope, (float)(gi - g0), (m + lg2(l_tot)) * kLn2) : neg_inf();
     }
   }
-
   tc_fence_before();
   __syncthreads();
   if (warp == 2) {

@@ -436,21 +436,44 @@ __device__ __forceinline__ float rcp(float x) {
   return y;
 }
 
-// tanh(x) = 1 - 2 / (1 + e^{2x}), evaluated with ex2 / rcp; for |x| < 2^-6 the
-// odd Taylor polynomial x - x^3/3 + 2x^5/15 avoids the cancellation of the
-// closed form near zero.
-__device__ __forceinline__ float tanh_exp(float x) {
-  const float ax = fabsf(x);
-  float t;
-  if (ax < 0.015625f) {
-    const float x2 = x * x;
-    t = x * fmaf(x2, fmaf(x2, 0.13333333f, -0.33333333f), 1.0f);
-  } else {
-    const float e = ex2(fminf(2.0f * 1.4426950408889634f * ax, 126.0f));
-    t = 1.0f - 2.0f * rcp(1.0f + e);
-    t = copysignf(t, x);
-  }
-  return t;
+// The soft-cap logit is cap·tanh(s/cap). Two forms of tanh, both without
+// data-dependent branches, so a warp never splits over them; a kernel picks
+// one per warp and step (tanh_small when every |x| of the warp is <= 1/2):
+//  * tanh_small: the odd Taylor series of tanh to x^11, on the FMA pipe;
+//    truncation error below 1e-6 relative for |x| <= 1/2.
+//  * tanh_any: sign(x)·(1 - 2/(1 + e^{2|x|})) with ex2 / rcp on the MUFU
+//    unit; absolute error a few fp32 ulps of 1, so where tanh x is tiny its
+//    relative error grows, but cap·tanh x is then tiny as well.
+constexpr float kTanhT1 = -1.0f / 3.0f;
+constexpr float kTanhT2 = 2.0f / 15.0f;
+constexpr float kTanhT3 = -17.0f / 315.0f;
+constexpr float kTanhT4 = 62.0f / 2835.0f;
+constexpr float kTanhT5 = -1382.0f / 155925.0f;
+
+__device__ __forceinline__ float tanh_small(float x) {
+  const float z = x * x;
+  float q = fmaf(z, kTanhT5, kTanhT4);
+  q = fmaf(z, q, kTanhT3);
+  q = fmaf(z, q, kTanhT2);
+  q = fmaf(z, q, kTanhT1);
+  q = fmaf(z, q, 1.0f);
+  return x * q;
+}
+
+__device__ __forceinline__ float tanh_any(float x) {
+  const float e = ex2(fminf(2.0f * 1.4426950408889634f * fabsf(x), 126.0f));
+  return copysignf(1.0f - 2.0f * rcp(1.0f + e), x);
+}
+
+// True when |raw·cap_in| <= 1/2 for all n raw logits of every thread of the
+// warp (warp-uniform), i.e. when tanh_small serves the whole step.
+template <int N>
+__device__ __forceinline__ bool cap_small(const uint32_t* raw, float cap_in) {
+  float am = 0.f;
+#pragma unroll
+  for (int e = 0; e < N; e += 2)
+    am = fmax3(am, fabsf(__uint_as_float(raw[e])), fabsf(__uint_as_float(raw[e + 1])));
+  return __all_sync(0xffffffffu, am * cap_in <= 0.5f);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {

@@ -304,34 +304,3 @@ def test_head_dim_256(case):
     slopes = torch.tensor([2.0 ** (-8.0 * (i + 1) / 4) for i in range(4)]) if alibi else None
     check_case(q, k, v, go, causal=causal, sliding_window=window, soft_cap=cap, alibi_slope=slopes)
 
-
-WIDE_CASES = [
-    # (dtype, d, g, sq, sk, causal, window, cap, alibi)
-    (torch.bfloat16, 128, 4, 640, 640, True, 0, 0.0, False),
-    (torch.float16, 128, 1, 300, 300, True, 96, 0.0, False),
-    (torch.bfloat16, 64, 2, 257, 257, False, 0, 0.0, False),
-    (torch.bfloat16, 128, 2, 333, 333, True, 50, 30.0, True),
-    (torch.float16, 64, 4, 200, 520, False, 80, 0.0, False),
-    (torch.bfloat16, 128, 8, 129, 1000, True, 0, 0.0, True),
-]
-
-
-@pytest.mark.parametrize("case", WIDE_CASES, ids=lambda c: "{}-d{}-g{}-q{}-k{}-c{}-w{}-cap{}-a{}".format(
-    str(c[0]).split(".")[-1], *c[1:]))
-def test_dkdv_wide_kernel(case, monkeypatch):
-    """The 128-query-step dK/dV kernel (BFA_DKDV_WIDE=1) against the oracle,
-    and in accumulate mode against its own 16-bit result."""
-    monkeypatch.setenv("BFA_DKDV_WIDE", "1")
-    dt, d, g, sq, sk, causal, window, cap, alibi = case
-    q, k, v, go = _inputs(sq + sk + d, 1, 2 * g, 2, sq, sk, d, dt)
-    slopes = torch.tensor([2.0 ** (-8.0 * (i + 1) / (2 * g)) for i in range(2 * g)]) if alibi else None
-    kw = dict(causal=causal, sliding_window=window, soft_cap=cap, alibi_slope=slopes)
-    check_case(q, k, v, go, **kw)
-    kw_dev = {**kw, "alibi_slope": None if slopes is None else slopes.to(DEV)}
-    qd, kd, vd, god = (t.to(DEV) for t in (q, k, v, go))
-    o, lse = nfa.npu_flash_attention_forward(qd, kd, vd, return_lse=True, **kw_dev)
-    ref = nfa.npu_flash_attention_backward(qd, kd, vd, o, lse, god, **kw_dev)
-    acc = tuple(torch.zeros(t.shape, dtype=torch.float32, device=DEV) for t in (qd, kd, vd))
-    nfa.npu_flash_attention_backward(qd, kd, vd, o, lse, god, _outputs=acc, _accumulate=True, **kw_dev)
-    for a, r in zip(acc, ref):
-        assert _err(a, r.float().cpu().double()) < TOL[dt]
