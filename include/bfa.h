@@ -47,7 +47,7 @@
 extern "C" {
 #endif
 
-#define BFA_ABI_VERSION 3
+#define BFA_ABI_VERSION 4
 
 typedef enum bfa_dtype {
   BFA_DTYPE_F32 = 0,
@@ -83,6 +83,14 @@ typedef struct bfa_problem {
   const float* alibi_slopes; /* NULL or device fp32 [heads_q]: logits += slope * (i - j) */
   int64_t q_pos_offset;    /* absolute position of query row 0 (0 unless context-parallel) */
   int64_t k_pos_offset;    /* absolute position of key row 0 */
+  /* Document masking (no reference counterpart; both NULL = off): device
+   * int32 arrays indexed by absolute position x, covering every query and
+   * key position of the problem. The document holding x spans
+   * [doc_start[x], doc_end[x]); a pair (i, j) is kept only when j lies in
+   * i's document (on top of causal / window). Tiles outside every row's
+   * document are skipped like causal ones. */
+  const int32_t* doc_start;
+  const int32_t* doc_end;
 } bfa_problem;
 
 /* A strided 4-D device tensor [B, H, S, D]; strides are in elements. */

@@ -14,7 +14,7 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libbfa.so")
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 DEBUG_INJECT_STALL = 1
@@ -38,7 +38,8 @@ class Problem(ctypes.Structure):
                 ("dtype", ctypes.c_int32), ("causal", ctypes.c_int32),
                 ("sliding_window", ctypes.c_int32), ("scale", ctypes.c_float),
                 ("soft_cap", ctypes.c_float), ("alibi_slopes", ctypes.c_void_p),
-                ("q_pos_offset", ctypes.c_int64), ("k_pos_offset", ctypes.c_int64)]
+                ("q_pos_offset", ctypes.c_int64), ("k_pos_offset", ctypes.c_int64),
+                ("doc_start", ctypes.c_void_p), ("doc_end", ctypes.c_void_p)]
 
 
 class Tensor(ctypes.Structure):

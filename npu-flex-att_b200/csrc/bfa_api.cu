@@ -30,6 +30,7 @@ int check_problem(const bfa_problem* pr) {
     return BFA_ERR_INVALID_ARGUMENT;
   // Query rows are padded to a multiple of 64 in int32 row pitches.
   if (pr->seqlen_q > INT32_MAX - 63) return BFA_ERR_INVALID_ARGUMENT;
+  if ((pr->doc_start == nullptr) != (pr->doc_end == nullptr)) return BFA_ERR_INVALID_ARGUMENT;
   if (pr->heads_q % pr->heads_kv != 0) return BFA_ERR_SHAPE;
   if (pr->head_dim < 1 || pr->head_dim > 256) return BFA_ERR_UNSUPPORTED;
   if (bfa::dtype_bytes(pr->dtype) == 0) return BFA_ERR_UNSUPPORTED;
@@ -56,6 +57,8 @@ Params make_params(const bfa_problem* pr) {
   p.alibi = pr->alibi_slopes;
   p.q_off = pr->q_pos_offset;
   p.k_off = pr->k_pos_offset;
+  p.doc_lo = pr->doc_start;
+  p.doc_hi = pr->doc_end;
   return p;
 }
 

@@ -38,6 +38,11 @@ struct Params {
   float scale, soft_cap;
   const float* alibi;
   int64_t q_off, k_off;
+  // Document masking (null: off): for every absolute position x, the
+  // document holding x spans positions [doc_lo[x], doc_hi[x]); pairs (i, j)
+  // are kept only inside one document.
+  const int32_t* doc_lo;
+  const int32_t* doc_hi;
   int32_t* status;
   uint64_t timeout_ns;
   uint32_t debug_flags;
@@ -56,10 +61,20 @@ template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return
 template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
 
 // Keep-mask on absolute positions.
-__device__ __forceinline__ bool keep_pair(int64_t i, int64_t j, int causal, int window) {
-  if (causal && j > i) return false;
-  if (window > 0 && i - j > window) return false;
+__device__ __forceinline__ bool keep_pair(const Params& p, int64_t i, int64_t j) {
+  if (p.causal && j > i) return false;
+  if (p.window > 0 && i - j > p.window) return false;
+  if (p.doc_lo && (j < p.doc_lo[i] || j >= p.doc_hi[i])) return false;
   return true;
+}
+
+// True when every query row of [i_min, i_max] and every key of [j_min,
+// j_max] (absolute positions) lie in one document (always without documents).
+__device__ __forceinline__ bool same_document(const Params& p, int64_t i_min, int64_t i_max, int64_t j_min,
+                                              int64_t j_max) {
+  if (!p.doc_lo) return true;
+  const int32_t lo = p.doc_lo[i_min];
+  return p.doc_lo[i_max] == lo && j_min >= lo && j_max < p.doc_hi[i_min];
 }
 
 // Logit transform (cap then ALiBi). `t_out` receives tanh(s/cap) for the
@@ -84,7 +99,8 @@ __device__ __forceinline__ float transform_logit(float dot, float scale, float c
 // alone (the forward adds it to its LSE output; the backward's row statistic
 // is lse - slope·(i - g0), formed in double). For slope > 0 (the reference's
 // sign, npu_flash_attention.py:109) g0 is the first key the row can see at
-// all, max(0, i - W) (0 without a window): the logits that carry the softmax
+// all, max(0, i - W) (0 without a window; no earlier than the start of the
+// row's document): the logits that carry the softmax
 // then stay O(1) instead of growing with i - j (an fp32 logit near 6e4,
 // slope ~1 at 64k positions, has an ulp of 4e-3, which shifts each
 // probability by up to 0.3%). g0 does not depend on the call's key offset, so
@@ -93,7 +109,9 @@ __device__ __forceinline__ float transform_logit(float dot, float scale, float c
 // bias is slope·(i - j) as written).
 __device__ __forceinline__ int64_t alibi_ref(const Params& p, float slope, int64_t gi) {
   if (!(slope > 0.f)) return gi;
-  return p.window > 0 ? max((int64_t)0, gi - (int64_t)p.window) : (int64_t)0;
+  int64_t g0 = p.window > 0 ? max((int64_t)0, gi - (int64_t)p.window) : (int64_t)0;
+  if (p.doc_lo) g0 = max(g0, (int64_t)p.doc_lo[gi]);
+  return g0;
 }
 
 // Backward row statistic from the forward LSE of query row i of head hq:
@@ -116,6 +134,10 @@ __device__ __forceinline__ void keys_for_query(const Params& p, int64_t gi, bool
   h = min(h, (int64_t)p.Sk - j0);
   if (p.causal) h = min(h, gi - p.k_off - j0 + 1);
   if (p.window > 0) l = max(l, gi - p.window - p.k_off - j0);
+  if (p.doc_lo && row_ok) {
+    l = max(l, (int64_t)p.doc_lo[gi] - p.k_off - j0);
+    h = min(h, (int64_t)p.doc_hi[gi] - p.k_off - j0);
+  }
   if (!row_ok || h < l) h = l;
   l = max((int64_t)0, min(l, (int64_t)n));
   h = max(l, min(h, (int64_t)n));
@@ -131,6 +153,10 @@ __device__ __forceinline__ void queries_for_key(const Params& p, int64_t gj, boo
   h = min(h, (int64_t)p.Sq - q0);
   if (p.causal) l = max(l, gj - p.q_off - q0);
   if (p.window > 0) h = min(h, gj + p.window - p.q_off - q0 + 1);
+  if (p.doc_lo && row_ok) {
+    l = max(l, (int64_t)p.doc_lo[gj] - p.q_off - q0);
+    h = min(h, (int64_t)p.doc_hi[gj] - p.q_off - q0);
+  }
   if (!row_ok || h < l) h = l;
   l = max((int64_t)0, min(l, (int64_t)n));
   h = max(l, min(h, (int64_t)n));
@@ -151,6 +177,10 @@ __device__ __forceinline__ void key_range(const Params& p, int r0, int r1, int* 
     int64_t lim = i_first - p.window - p.k_off;
     if (lim > l) l = lim;
   }
+  if (p.doc_lo) {  // documents are contiguous: the first row's start, the last row's end
+    l = max(l, (int64_t)p.doc_lo[i_first] - p.k_off);
+    h = min(h, (int64_t)p.doc_hi[i_last] - p.k_off);
+  }
   if (h < l) h = l;
   if (l < 0) l = 0;
   if (h < 0) h = 0;
@@ -169,6 +199,10 @@ __device__ __forceinline__ void query_range(const Params& p, int c0, int c1, int
   if (p.window > 0) {  // i <= j_last + W
     int64_t lim = j_last + p.window - p.q_off + 1;
     if (lim < h) h = lim;
+  }
+  if (p.doc_lo) {
+    l = max(l, (int64_t)p.doc_lo[j_first] - p.q_off);
+    h = min(h, (int64_t)p.doc_hi[j_last] - p.q_off);
   }
   if (h < l) h = l;
   if (l < 0) l = 0;

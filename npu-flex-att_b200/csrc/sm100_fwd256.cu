@@ -83,7 +83,7 @@ __device__ __forceinline__ bool tile_full(const Params& p, int r0, int r1, int c
   const int64_t j_min = c0 + p.k_off, j_max = c1 - 1 + p.k_off;
   if (p.causal && j_max > i_min) return false;
   if (p.window > 0 && i_max - j_min > p.window) return false;
-  return true;
+  return same_document(p, i_min, i_max, j_min, j_max);
 }
 
 template <bool BF16>

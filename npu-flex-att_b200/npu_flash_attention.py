@@ -57,7 +57,30 @@ def _fast_layout(t: torch.Tensor) -> torch.Tensor:
     return t if ok else t.contiguous()
 
 
-def _problem(query, key, causal, sliding_window, alibi, scale, soft_cap, q_pos=0, k_pos=0):
+def _documents(cu_seqlens, positions: int, device):
+    """Per-position document bounds from cumulative document lengths.
+
+    ``cu_seqlens`` (ints, non-decreasing, first 0) cuts the absolute positions
+    [0, cu_seqlens[-1]) into documents [cu_seqlens[d], cu_seqlens[d+1]). Returns
+    int32 device tensors (start, end) of the document holding each position;
+    they must cover every query and key position of the call."""
+    if cu_seqlens is None:
+        return None
+    cu = torch.as_tensor(cu_seqlens).to(device=device, dtype=torch.int64).reshape(-1)
+    if cu.numel() < 2 or int(cu[0]) != 0 or bool((cu[1:] < cu[:-1]).any()):
+        raise ValueError("cu_seqlens must start at 0 and be non-decreasing")
+    total = int(cu[-1])
+    if total < positions:
+        raise ValueError(f"cu_seqlens covers {total} positions, the call needs {positions}")
+    if total >= 2 ** 31:
+        raise ValueError("cu_seqlens must stay below 2**31 positions")
+    pos = torch.arange(total, device=device, dtype=torch.int64)
+    idx = torch.searchsorted(cu, pos, right=True) - 1
+    return cu[idx].to(torch.int32).contiguous(), cu[idx + 1].to(torch.int32).contiguous()
+
+
+def _problem(query, key, causal, sliding_window, alibi, scale, soft_cap, q_pos=0, k_pos=0,
+             docs=None):
     B, Hq, Sq, D = query.shape
     _, Hkv, Sk, _ = key.shape
     pr = _bfa.Problem()
@@ -70,6 +93,8 @@ def _problem(query, key, causal, sliding_window, alibi, scale, soft_cap, q_pos=0
     pr.soft_cap = float(soft_cap)
     pr.alibi_slopes = alibi.data_ptr() if alibi is not None else None
     pr.q_pos_offset, pr.k_pos_offset = int(q_pos), int(k_pos)
+    if docs is not None:
+        pr.doc_start, pr.doc_end = docs[0].data_ptr(), docs[1].data_ptr()
     return pr
 
 
@@ -117,13 +142,17 @@ def npu_flash_attention_forward(
     *,
     q_pos_offset=0,
     k_pos_offset=0,
+    cu_seqlens=None,
     _wait_timeout_ns=0,
     _debug_flags=0,
 ):
     """Attention forward: O (and the fp32 natural-log LSE when `return_lse`).
 
     Mirrors npu_flash_attention.py:606-656. Keyword-only extras (not in the
-    reference): absolute position offsets for context-parallel shards.
+    reference): absolute position offsets for context-parallel shards, and
+    document masking -- ``cu_seqlens`` (cumulative document lengths over the
+    absolute positions, first 0) keeps only pairs inside one document, on
+    top of the other masks (packed variable-length sequences).
     """
     B, Hq, Sq, D = query.shape
     Bk, Hkv, Sk, Dk = key.shape
@@ -141,7 +170,8 @@ def npu_flash_attention_forward(
     o_k = _fast_layout(O) if O.data_ptr() else O
     LSE = torch.empty(B, Hq, Sq, device=dev, dtype=torch.float32)
     lib = _bfa.load()
-    pr = _problem(q, k, causal, sliding_window, alibi, scale, soft_cap, q_pos_offset, k_pos_offset)
+    docs = _documents(cu_seqlens, max(q_pos_offset + Sq, k_pos_offset + Sk), dev)
+    pr = _problem(q, k, causal, sliding_window, alibi, scale, soft_cap, q_pos_offset, k_pos_offset, docs)
     args = _bfa.FwdArgs()
     args.q, args.k, args.v, args.o = _bfa.tensor(q), _bfa.tensor(k), _bfa.tensor(v), _bfa.tensor(o_k)
     args.lse = LSE.data_ptr()
@@ -176,6 +206,7 @@ def npu_flash_attention_backward(
     *,
     q_pos_offset=0,
     k_pos_offset=0,
+    cu_seqlens=None,
     _wait_timeout_ns=0,
     _debug_flags=0,
     _phases=0,
@@ -220,7 +251,8 @@ def npu_flash_attention_backward(
         DV = torch.empty(B, Hkv, Sk, D, device=dev, dtype=value.dtype)
     dq_k = _fast_layout(DQ) if DQ.data_ptr() else DQ
     lib = _bfa.load()
-    pr = _problem(q, k, causal, sliding_window, alibi, scale, soft_cap, q_pos_offset, k_pos_offset)
+    docs = _documents(cu_seqlens, max(q_pos_offset + Sq, k_pos_offset + Sk), dev)
+    pr = _problem(q, k, causal, sliding_window, alibi, scale, soft_cap, q_pos_offset, k_pos_offset, docs)
     args = _bfa.BwdArgs()
     args.q, args.k, args.v = _bfa.tensor(q), _bfa.tensor(k), _bfa.tensor(v)
     args.o, args.dout = _bfa.tensor(o), _bfa.tensor(do)
@@ -249,11 +281,14 @@ class NPUFlexAttention(torch.autograd.Function):
     v only (the mask arguments get None). Same class name, argument order and
     saved state as the reference's autograd class
     (npu_flash_attention.py:742-781), so code that calls ``.apply`` on it
-    keeps working."""
+    keeps working; one optional argument is appended, ``cu_seqlens``
+    (document masking, see npu_flash_attention_forward)."""
 
     @staticmethod
     def forward(ctx, query, key, value, causal=False, sliding_window=0,
-                alibi_slope=None, scale=None, block_m=16, block_n=64, soft_cap=0.0):
+                alibi_slope=None, scale=None, block_m=16, block_n=64, soft_cap=0.0,
+                cu_seqlens=None):
+        ctx.cu_seqlens = cu_seqlens
         ctx.causal = causal
         ctx.sliding_window = sliding_window
         ctx.alibi_slope = alibi_slope
@@ -267,7 +302,7 @@ class NPUFlexAttention(torch.autograd.Function):
                 causal=causal, sliding_window=sliding_window,
                 alibi_slope=alibi_slope, scale=scale,
                 block_m=block_m, block_n=block_n, return_lse=True,
-                soft_cap=soft_cap,
+                soft_cap=soft_cap, cu_seqlens=cu_seqlens,
             )
         ctx.save_for_backward(query, key, value, lse, out)
         return out
@@ -280,9 +315,9 @@ class NPUFlexAttention(torch.autograd.Function):
             causal=ctx.causal, sliding_window=ctx.sliding_window,
             alibi_slope=ctx.alibi_slope, scale=ctx.scale,
             block_m=ctx.block_m, block_n=ctx.block_n,
-            soft_cap=ctx.soft_cap,
+            soft_cap=ctx.soft_cap, cu_seqlens=ctx.cu_seqlens,
         )
-        return DQ, DK, DV, None, None, None, None, None, None, None
+        return DQ, DK, DV, None, None, None, None, None, None, None, None
 
 
 def npu_flex_attention(
@@ -291,12 +326,13 @@ def npu_flex_attention(
     alibi_slope=None, scale=None,
     block_m=16, block_n=64,
     soft_cap=0.0,
+    cu_seqlens=None,
 ):
     """Functional form of NPUFlexAttention.apply with keyword defaults
-    (signature of npu_flash_attention.py:784-794)."""
+    (signature of npu_flash_attention.py:784-794, plus ``cu_seqlens``)."""
     return NPUFlexAttention.apply(
         query, key, value, causal, sliding_window,
-        alibi_slope, scale, block_m, block_n, soft_cap,
+        alibi_slope, scale, block_m, block_n, soft_cap, cu_seqlens,
     )
 
 
@@ -309,6 +345,9 @@ class AttentionConfig:
     For instance a local-attention layer with capped logits:
         cfg = AttentionConfig(causal=True, sliding_window=4096, soft_cap=50.0)
         o = flex_attention(q, k, v, config=cfg)
+    ``cu_seqlens`` (appended after the reference's fields) adds document
+    masking over packed sequences:
+        cfg = AttentionConfig(causal=True, cu_seqlens=torch.tensor([0, 700, 1024]))
     """
     causal: bool = False
     sliding_window: int = 0
@@ -317,6 +356,7 @@ class AttentionConfig:
     soft_cap: float = 0.0
     block_m: int = 16
     block_n: int = 64
+    cu_seqlens: Optional[torch.Tensor] = None
 
     def __post_init__(self):
         if self.sliding_window < 0:
@@ -340,4 +380,5 @@ def flex_attention(query, key, value, config: Optional[AttentionConfig] = None, 
         block_m=config.block_m,
         block_n=config.block_n,
         soft_cap=config.soft_cap,
+        cu_seqlens=config.cu_seqlens,
     )

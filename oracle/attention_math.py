@@ -73,11 +73,15 @@ class MaskSpec:
 
 
 def keep_mask(sq: int, sk: int, causal: bool, window: int,
-              q_offset: int = 0, k_offset: int = 0) -> torch.Tensor:
+              q_offset: int = 0, k_offset: int = 0, cu_seqlens=None) -> torch.Tensor:
     """Boolean [Sq, Sk] keep-mask (npu_flash_attention.py:139,141).
 
     ``q_offset``/``k_offset`` shift the row/column positions (context-parallel
-    shards); both are 0 for the reference's own calls.
+    shards); both are 0 for the reference's own calls. ``cu_seqlens``
+    (cumulative document lengths over absolute positions, first 0) adds
+    document masking, which the reference does not have (its README lists
+    document / block masks as missing): a pair is kept only when i and j lie
+    in the same document [cu[d], cu[d+1]).
     """
     i = torch.arange(sq).view(-1, 1) + q_offset
     j = torch.arange(sk).view(1, -1) + k_offset
@@ -86,6 +90,11 @@ def keep_mask(sq: int, sk: int, causal: bool, window: int,
         keep &= i >= j
     if window > 0:
         keep &= (i - j) <= window
+    if cu_seqlens is not None:
+        cu = torch.as_tensor(cu_seqlens, dtype=torch.int64).cpu().reshape(-1)
+        doc_i = torch.searchsorted(cu, i.reshape(-1), right=True).view(-1, 1)
+        doc_j = torch.searchsorted(cu, j.reshape(-1), right=True).view(1, -1)
+        keep &= doc_i == doc_j
     return keep
 
 
@@ -121,7 +130,7 @@ def logits(q, k, *, scale, soft_cap=0.0, alibi_slope=None,
 
 def attention_forward(q, k, v, *, causal=False, sliding_window=0,
                       alibi_slope=None, scale=None, soft_cap=0.0,
-                      q_offset=0, k_offset=0, dtype=torch.float64):
+                      q_offset=0, k_offset=0, cu_seqlens=None, dtype=torch.float64):
     """Forward oracle: returns ``(O, LSE)`` in ``dtype`` (O) and ``dtype`` (LSE).
 
     npu_flash_attention.py:17-166 (kernel) and :606-656 (host wrapper:
@@ -135,7 +144,7 @@ def attention_forward(q, k, v, *, causal=False, sliding_window=0,
     u, _ = logits(qf, kf, scale=scale, soft_cap=soft_cap, alibi_slope=slope,
                   q_offset=q_offset, k_offset=k_offset)
     keep = keep_mask(q.shape[2], k.shape[2], causal, sliding_window,
-                     q_offset, k_offset)
+                     q_offset, k_offset, cu_seqlens)
     u = u.masked_fill(~keep, float("-inf"))
     lse = torch.logsumexp(u, dim=-1)
     finite = torch.isfinite(lse)
@@ -149,7 +158,7 @@ def attention_backward(q, k, v, grad_out, *, causal=False, sliding_window=0,
                        alibi_slope=None, scale=None, soft_cap=0.0,
                        q_offset=0, k_offset=0, alibi_in_backward=True,
                        out=None, lse=None, dtype=torch.float64,
-                       operand_dtype=None):
+                       operand_dtype=None, cu_seqlens=None):
     """Backward oracle: returns ``(dQ, dK, dV)`` with dK/dV per KV head.
 
     Restates npu_flash_attention.py:659-739 and the two kernels :298-560.
@@ -174,7 +183,7 @@ def attention_backward(q, k, v, grad_out, *, causal=False, sliding_window=0,
         o_ref, lse_ref = attention_forward(
             q, k, v, causal=causal, sliding_window=sliding_window,
             alibi_slope=alibi_slope, scale=scale, soft_cap=soft_cap,
-            q_offset=q_offset, k_offset=k_offset, dtype=dtype)
+            q_offset=q_offset, k_offset=k_offset, cu_seqlens=cu_seqlens, dtype=dtype)
         out = o_ref if out is None else out
         lse = lse_ref if lse is None else lse
     of, lsef = out.to(dtype), lse.to(dtype)
@@ -182,7 +191,7 @@ def attention_backward(q, k, v, grad_out, *, causal=False, sliding_window=0,
                   alibi_slope=slope if alibi_in_backward else None,
                   q_offset=q_offset, k_offset=k_offset)
     keep = keep_mask(q.shape[2], k.shape[2], causal, sliding_window,
-                     q_offset, k_offset)
+                     q_offset, k_offset, cu_seqlens)
     finite = torch.isfinite(lsef).unsqueeze(-1)
     p = torch.exp(u - torch.where(finite, lsef.unsqueeze(-1), torch.zeros_like(u[..., :1])))
     p = torch.where(keep & finite, p, torch.zeros_like(p))

@@ -34,8 +34,11 @@ def test_signatures_match_reference():
                      "sliding_window", "alibi_slope", "scale", "block_m", "block_n", "soft_cap"]
     assert sig.parameters["block_n"].default == 32
     sig = inspect.signature(nfa.npu_flex_attention)
+    # The reference's ten parameters in order, then this build's document mask.
     assert list(sig.parameters) == ["query", "key", "value", "causal", "sliding_window",
-                                    "alibi_slope", "scale", "block_m", "block_n", "soft_cap"]
+                                    "alibi_slope", "scale", "block_m", "block_n", "soft_cap",
+                                    "cu_seqlens"]
+    assert sig.parameters["cu_seqlens"].default is None
 
 
 def test_shape_assertions_fire_before_device_work():
