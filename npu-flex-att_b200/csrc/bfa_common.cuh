@@ -107,10 +107,12 @@ __device__ __forceinline__ float transform_logit(float dot, float scale, float c
 // the row statistic agrees across the calls of a blockwise (context-parallel)
 // backward. For slope <= 0 the bias peaks at the diagonal and g0 = i (the
 // bias is slope·(i - j) as written).
-__device__ __forceinline__ int64_t alibi_ref(const Params& p, float slope, int64_t gi) {
+// `row_ok` false (a padding row past Sq) skips the document lookup, whose
+// array covers only the problem's positions.
+__device__ __forceinline__ int64_t alibi_ref(const Params& p, float slope, int64_t gi, bool row_ok = true) {
   if (!(slope > 0.f)) return gi;
   int64_t g0 = p.window > 0 ? max((int64_t)0, gi - (int64_t)p.window) : (int64_t)0;
-  if (p.doc_lo) g0 = max(g0, (int64_t)p.doc_lo[gi]);
+  if (p.doc_lo && row_ok) g0 = max(g0, (int64_t)p.doc_lo[gi]);
   return g0;
 }
 

@@ -333,10 +333,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float slope = ALIBI ? p.alibi[hq] : 0.f;
       const float slope2 = slope * kLog2e;
       // ALiBi bias slope·(g0_i - j) (alibi_ref): with slope > 0, g0_i =
-      // max(0, i - W) and the bias is the larger of the two terms below;
-      // with slope <= 0, g0_i = i (the second term alone).
+      // max(0, i - W, document start) and the bias is the larger of the two
+      // terms below (every query kept with key j shares j's document); with
+      // slope <= 0, g0_i = i (the second term alone).
       const bool shifted = ALIBI && slope > 0.f;
-      const float ba = shifted ? slope2 * (float)(-gj) : neg_inf();
+      const int64_t dstart = (p.doc_lo && kj < p.Sk) ? (int64_t)p.doc_lo[gj] : 0;
+      const float ba = shifted ? slope2 * (float)(dstart - gj) : neg_inf();
       const float bq = !ALIBI ? 0.f
                        : !shifted ? slope2 * (float)((int64_t)q0 + p.q_off - gj)
                        : p.window > 0 ? slope2 * (float)((int64_t)q0 + p.q_off - p.window - gj)
@@ -627,7 +629,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float cap_out = CAP ? p.soft_cap * kLog2e : 0.f;
     const float slope = ALIBI ? p.alibi[hq] : 0.f;
     const float slope2 = slope * kLog2e;
-    const int64_t g0 = ALIBI ? alibi_ref(p, slope, gi) : gi;  // ALiBi bias slope·(g0 - j)
+    const int64_t g0 = ALIBI ? alibi_ref(p, slope, gi, qi < p.Sq) : gi;  // ALiBi bias slope·(g0 - j)
     const int64_t ridx = ((int64_t)b * p.Hq + hq) * p.Sq_pad + qi;
     const float lse2 = p.lse2[ridx];
     const float dlt = p.delta[ridx];

@@ -79,6 +79,7 @@ constexpr float kT5 = -1382.0f / 155925.0f;
 
 __device__ __forceinline__ bool tile_full(const Params& p, int r0, int r1, int c0, int c1) {
   if (c1 > p.Sk) return false;
+  if (p.doc_lo && r1 > p.Sq) return false;  // document bounds exist only for rows < Sq
   const int64_t i_min = r0 + p.q_off, i_max = r1 - 1 + p.q_off;
   const int64_t j_min = c0 + p.k_off, j_max = c1 - 1 + p.k_off;
   if (p.causal && j_max > i_min) return false;
@@ -268,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float slope = ALIBI ? p.alibi[hq] : 0.f;
     const float slope2 = slope * kLog2e;
     // ALiBi: bias slope·(g0 - j); slope·(i - g0) goes into the LSE only.
-    const int64_t g0 = ALIBI ? alibi_ref(p, slope, gi) : gi;
+    const int64_t g0 = ALIBI ? alibi_ref(p, slope, gi, r_local < p.Sq) : gi;
     // cap_out · tanh(u) = u · (c0 + z (c1 + z (c2 + ...))), z = u^2.
     const float c0 = cap_out, c1 = cap_out * kT1, c2 = cap_out * kT2, c3 = cap_out * kT3,
                 c4 = cap_out * kT4, c5 = cap_out * kT5;

@@ -26,6 +26,9 @@ CASES = [
     (torch.bfloat16, 256, 4, 2, 520, [0, 260, 520], dict(causal=True, soft_cap=30.0)),
     (torch.float32, 64, 2, 2, 300, [0, 150, 300], dict(causal=True)),
     (torch.bfloat16, 128, 4, 2, 400, [0, 10, 20, 400], dict(causal=True, alibi=True)),
+    (torch.bfloat16, 128, 4, 2, 333, [0, 100, 333], dict(causal=True, alibi=True, sliding_window=64)),
+    (torch.bfloat16, 256, 4, 2, 300, [0, 50, 300], dict(causal=True, alibi=True, sliding_window=100)),
+    (torch.float16, 64, 2, 1, 257, [0, 3, 257], dict(alibi=True)),
 ]
 
 
