@@ -91,6 +91,14 @@ typedef struct bfa_problem {
    * document are skipped like causal ones. */
   const int32_t* doc_start;
   const int32_t* doc_end;
+  /* Block-sparse mask (no reference counterpart; NULL = off): device uint8
+   * [B, Hq, ceil(Sq/128), ceil(Sk/128)] at element strides block_mask_stride
+   * (batch, q-head, query block; the key-block stride is 1; a stride of 0
+   * broadcasts). Query row r and key row c of the call (local indices) fall in
+   * block (r / 128, c / 128); a zero byte drops the whole block, on top of the
+   * other masks. Dropped blocks are skipped, not computed. */
+  const uint8_t* block_mask;
+  int64_t block_mask_stride[3];
 } bfa_problem;
 
 /* A strided 4-D device tensor [B, H, S, D]; strides are in elements. */

@@ -39,7 +39,8 @@ class Problem(ctypes.Structure):
                 ("sliding_window", ctypes.c_int32), ("scale", ctypes.c_float),
                 ("soft_cap", ctypes.c_float), ("alibi_slopes", ctypes.c_void_p),
                 ("q_pos_offset", ctypes.c_int64), ("k_pos_offset", ctypes.c_int64),
-                ("doc_start", ctypes.c_void_p), ("doc_end", ctypes.c_void_p)]
+                ("doc_start", ctypes.c_void_p), ("doc_end", ctypes.c_void_p),
+                ("block_mask", ctypes.c_void_p), ("block_mask_stride", ctypes.c_int64 * 3)]
 
 
 class Tensor(ctypes.Structure):

@@ -59,6 +59,8 @@ Params make_params(const bfa_problem* pr) {
   p.k_off = pr->k_pos_offset;
   p.doc_lo = pr->doc_start;
   p.doc_hi = pr->doc_end;
+  p.blk = pr->block_mask;
+  for (int i = 0; i < 3; ++i) p.blk_s[i] = pr->block_mask_stride[i];
   return p;
 }
 

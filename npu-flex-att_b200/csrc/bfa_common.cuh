@@ -43,6 +43,10 @@ struct Params {
   // are kept only inside one document.
   const int32_t* doc_lo;
   const int32_t* doc_hi;
+  // Block-sparse mask (null: off): byte [b, hq, r / 128, c / 128] at strides
+  // blk_s (batch, q-head, query block; key block stride 1), r and c local.
+  const uint8_t* blk;
+  int64_t blk_s[3];
   int32_t* status;
   uint64_t timeout_ns;
   uint32_t debug_flags;
@@ -66,6 +70,41 @@ __device__ __forceinline__ bool keep_pair(const Params& p, int64_t i, int64_t j)
   if (p.window > 0 && i - j > p.window) return false;
   if (p.doc_lo && (j < p.doc_lo[i] || j >= p.doc_hi[i])) return false;
   return true;
+}
+
+constexpr int kMaskBlock = 128;  // block-sparse mask granularity (rows and keys)
+
+// Whether block (qb, kb) of (b, hq) is computed (always without a mask).
+__device__ __forceinline__ bool block_on(const Params& p, int b, int hq, int qb, int kb) {
+  return !p.blk || p.blk[(int64_t)b * p.blk_s[0] + (int64_t)hq * p.blk_s[1] + (int64_t)qb * p.blk_s[2] + kb] != 0;
+}
+
+// Visits the steps of a loop that a block-sparse mask leaves on: step(j)
+// returns the j-th visited step for nondecreasing j, where next(s) gives the
+// first visited step after s. A kernel whose roles consume steps out of order
+// keeps one walker per kind of consumer.
+template <typename Next>
+struct StepWalker {
+  Next next;
+  int j, s;
+  __device__ __forceinline__ StepWalker(Next n, int start) : next(n), j(-1), s(start) {}
+  __device__ __forceinline__ int step(int want) {
+    while (j < want) {
+      s = next(s);
+      ++j;
+    }
+    return s;
+  }
+};
+template <typename Next>
+__device__ __forceinline__ StepWalker<Next> make_walker(Next n, int start) {
+  return StepWalker<Next>(n, start);
+}
+
+// keep_pair plus the block-sparse mask of (b, hq); positions absolute.
+__device__ __forceinline__ bool keep_elem(const Params& p, int b, int hq, int64_t gi, int64_t gj) {
+  return keep_pair(p, gi, gj) &&
+         block_on(p, b, hq, (int)((gi - p.q_off) / kMaskBlock), (int)((gj - p.k_off) / kMaskBlock));
 }
 
 // True when every query row of [i_min, i_max] and every key of [j_min,

@@ -230,7 +230,7 @@ __global__ void __launch_bounds__(kDecThreads)
         if (r < R) {
           const int g = (row0 + r) / p.Sq, s = (row0 + r) - g * p.Sq;
           const int64_t gi = (int64_t)s + p.q_off, gj = (int64_t)key + p.k_off;
-          const bool keep = key < ke && keep_pair(p, gi, gj);
+          const bool keep = key < ke && keep_elem(p, b, hkv * p.G + g, gi, gj);
           float x = acc[j];
           if (!PLAIN) {
             const float slope = p.alibi ? p.alibi[hkv * p.G + g] : 0.f;
@@ -480,7 +480,7 @@ __global__ void __launch_bounds__(kDecThreads)
           const int key = kb + c * kChunk + n;
           const int gg = (row0 + r) / p.Sq, s = (row0 + r) - gg * p.Sq;
           const int64_t gi = (int64_t)s + p.q_off, gj = (int64_t)key + p.k_off;
-          const bool keep = key < ke && keep_pair(p, gi, gj);
+          const bool keep = key < ke && keep_elem(p, b, hkv * p.G + gg, gi, gj);
           float x;
           if (PLAIN) {
             x = acc[e] * sl2;

@@ -92,7 +92,7 @@ __global__ void __launch_bounds__(NT) simt_fwd_kernel(Params p) {
       const int64_t gj = (int64_t)k0 + jj + p.k_off;
       const float dot = dot_rows<DP>(sQ + r * (DP + 1), sK + jj * (DP + 1));
       const float val = transform_logit(dot, p.scale, p.soft_cap, slope, gi, gj, nullptr);
-      const bool ok = (jj < kn) && (r < rows) && keep_pair(p, gi, gj);
+      const bool ok = (jj < kn) && (r < rows) && keep_elem(p, b, hq, gi, gj);
       s[u] = ok ? val : neg_inf();
       mx = fmaxf(mx, s[u]);
     }
@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(NT) simt_bwd_dq_kernel(Params p) {
       const int jj = c + 4 * u;
       const int64_t gj = (int64_t)k0 + jj + p.k_off;
       float ds = 0.f;
-      if (row_live && jj < kn && keep_pair(p, gi, gj)) {
+      if (row_live && jj < kn && keep_elem(p, b, hq, gi, gj)) {
         float t;
         const float dot = dot_rows<DP>(sQ + r * (DP + 1), sK + jj * (DP + 1));
         const float val = transform_logit(dot, p.scale, p.soft_cap, slope, gi, gj, &t);
@@ -257,7 +257,7 @@ __global__ void __launch_bounds__(NT) simt_bwd_dkdv_kernel(Params p) {
         const int64_t gi = (int64_t)q0 + ii + p.q_off;
         float pr = 0.f, ds = 0.f;
         const float lse = sL[ii];
-        if (r < cols && ii < qn && lse != neg_inf() && keep_pair(p, gi, gj)) {
+        if (r < cols && ii < qn && lse != neg_inf() && keep_elem(p, b, hq, gi, gj)) {
           float t;
           const float dot = dot_rows<DP>(sQ + ii * (DP + 1), sK + r * (DP + 1));
           const float val = transform_logit(dot, p.scale, p.soft_cap, slope, gi, gj, &t);

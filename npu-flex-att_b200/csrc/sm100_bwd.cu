@@ -121,7 +121,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   query_range(p, c0, min(c0 + kRows, p.Sk), &qlo, &qhi);
   const int qt0 = qlo / kInner;
   const int n_qt = (qhi > qlo) ? (qhi + kInner - 1) / kInner - qt0 : 0;
-  const int n_iter = n_qt * p.G;
+  // Steps s in [0, n_qt * G): q-head hkv * G + s / n_qt, 64-row query tile
+  // qt0 + s % n_qt. With a block-sparse mask a step is visited only when its
+  // (query block, key block) is on; every role walks the visited steps in
+  // the same order with next_step().
+  auto step_hq = [&](int s) { return hkv * p.G + s / n_qt; };
+  auto step_q0 = [&](int s) { return (qt0 + s % n_qt) * kInner; };
+  auto step_on = [&](int s) { return block_on(p, b, step_hq(s), step_q0(s) / kMaskBlock, kt); };
+  int n_iter = n_qt * p.G;
+  if (p.blk) {
+    n_iter = 0;
+    for (int s = 0; s < n_qt * p.G; ++s) n_iter += step_on(s) ? 1 : 0;
+  }
+  auto next_step = [&](int s) {
+    do { ++s; } while (p.blk && s < n_qt * p.G && !step_on(s));
+    return s;
+  };
 
   WaitCtl ctl{abort_flag, p.status, p.timeout_ns};
 
@@ -153,12 +168,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       int issued = 0;
+      int sv = -1;
       for (int i = 0; i < n_iter; ++i) {
         const int st = i % NS;
         if (i >= NS && !mbar_wait(bar(kQEmpty + st), ((i / NS) & 1) ^ 1, ctl, BFA_ERR_DEVICE_TIMEOUT))
           break;
-        const int hq = hkv * p.G + i / n_qt;
-        const int q0 = (qt0 + i % n_qt) * kInner;
+        sv = next_step(sv);
+        const int hq = step_hq(sv);
+        const int q0 = step_q0(sv);
         const uint32_t qs = sbase + L::kOffStage + st * L::kStageBytes;
         const int64_t rrow = ((int64_t)b * p.Hq + hq) * p.Sq_pad + q0;
         const uint32_t rs = sbase + L::kOffRow + st * 512;
@@ -250,10 +267,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float cap_in = CAP ? p.scale / p.soft_cap : 0.f;
     const float cap_out = CAP ? p.soft_cap * kLog2e : 0.f;
     bool ok = true;
+    int sv = -1;
     for (int i = 0; i < n_iter; ++i) {
       const int bf = i & 1, k = i >> 1, st = i % NS;
-      const int hq = hkv * p.G + i / n_qt;
-      const int q0 = (qt0 + i % n_qt) * kInner;
+      sv = next_step(sv);
+      const int hq = step_hq(sv);
+      const int q0 = step_q0(sv);
       uint32_t wbar = bar(kSPFull + bf), wpar = (uint32_t)(k & 1);
       if ((p.debug_flags & BFA_DEBUG_INJECT_STALL) && i == 0) {
         wbar = bar(kNever);
@@ -504,7 +523,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   int klo, khi;
   key_range(p, q0, min(q0 + kRows, p.Sq), &klo, &khi);
   const int jt0 = klo / NK;
-  const int n_iter = (khi > klo) ? (khi + NK - 1) / NK - jt0 : 0;
+  const int jend = (khi > klo) ? (khi + NK - 1) / NK : jt0;
+  // Block-sparse mask: key tile j (one 128-key block) is visited only when
+  // block (q0 / 128, j) is on; producer and elementwise warps walk the
+  // visited tiles with next_tile().
+  int n_iter = jend - jt0;
+  if (p.blk) {
+    n_iter = 0;
+    for (int j = jt0; j < jend; ++j) n_iter += block_on(p, b, hq, q0 / kMaskBlock, j) ? 1 : 0;
+  }
+  auto next_tile = [&](int j) {
+    do { ++j; } while (p.blk && j < jend && !block_on(p, b, hq, q0 / kMaskBlock, j));
+    return j;
+  };
 
   WaitCtl ctl{abort_flag, p.status, p.timeout_ns};
 
@@ -536,12 +567,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       int n = 0;
       bool ok = true;
+      int jv = jt0 - 1;
       for (int i = 0; i < n_iter && ok; ++i) {
         const int st = i % NS;
         if (i >= NS) ok = mbar_wait(bar(kKVEmpty + st), ((i / NS) & 1) ^ 1, ctl, BFA_ERR_DEVICE_TIMEOUT);
         else if (st == NS - 1) ok = mbar_wait(bar(kOpsReady), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
         if (!ok) break;
-        const int j0 = (jt0 + i) * NK;
+        jv = next_tile(jv);
+        const int j0 = jv * NK;
         const uint32_t ks = sbase + L::stage_off(st);
         mbar_arrive_expect_tx(bar(kKVFull + st), L::kStageBytes);
         for (int s = 0; s < L::kSub; ++s) {
@@ -655,8 +688,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(bar(kOpsReady));
       }
     }
+    int jv = jt0 - 1;
     for (int i = 0; i < n_iter && ok; ++i) {
-      const int j0 = (jt0 + i) * NK;
+      jv = next_tile(jv);
+      const int j0 = jv * NK;
       uint32_t wbar = bar(kSPFull), wpar = (uint32_t)(i & 1);
       if ((p.debug_flags & BFA_DEBUG_INJECT_STALL) && i == 0) {
         wbar = bar(kNever);

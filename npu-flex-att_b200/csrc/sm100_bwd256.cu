@@ -182,7 +182,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   query_range(p, c0, min(c0 + kRows, p.Sk), &qlo, &qhi);
   const int qt0 = qlo / kInner;
   const int n_qt = (qhi > qlo) ? (qhi + kInner - 1) / kInner - qt0 : 0;
-  const int n_iter = n_qt * p.G;
+  // Steps s in [0, n_qt * G): q-head hkv * G + s / n_qt, 64-row query tile
+  // qt0 + s % n_qt. With a block-sparse mask a step is visited only when its
+  // (query block, key block) is on; step i of the loops below is the i-th
+  // visited step, which each consumer finds with its own walker.
+  auto step_head = [&](int s) { return hkv * p.G + s / n_qt; };
+  auto step_q0 = [&](int s) { return (qt0 + s % n_qt) * kInner; };
+  auto step_on = [&](int s) { return block_on(p, b, step_head(s), step_q0(s) / kMaskBlock, kt); };
+  int n_iter = n_qt * p.G;
+  if (p.blk) {
+    n_iter = 0;
+    for (int s = 0; s < n_qt * p.G; ++s) n_iter += step_on(s) ? 1 : 0;
+  }
+  auto next_step = [&](int s) {
+    do { ++s; } while (p.blk && s < n_qt * p.G && !step_on(s));
+    return s;
+  };
 
   WaitCtl ctl{abort_flag, p.status, p.timeout_ns};
 
@@ -203,8 +218,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   auto unit_addr = [&](int n) -> uint32_t { return sbase + L::kOffRing + (uint32_t)(n % NS) * kUnit; };
-  auto step_head = [&](int i) { return hkv * p.G + i / n_qt; };
-  auto step_q0 = [&](int i) { return (qt0 + i % n_qt) * kInner; };
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -218,14 +231,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       int n = 0;
       int nr = 0;
+      auto w0 = make_walker(next_step, -1), w1 = make_walker(next_step, -1), w2 = make_walker(next_step, -1);
       kv_ops<MODE>(n_iter, [&](int op, int i) -> bool {
+        const int sv = op == 0 ? w0.step(i) : (op == 1 || op == 2) ? w1.step(i) : w2.step(i);
         if (op == 1 && !DK) {
           // dV(i) needs dO_i; nothing else to load here.
         }
         const int slot = n % NS;
         if (n >= NS && !mbar_wait(bar(kEmpty + slot), ((n / NS) & 1) ^ 1, ctl, BFA_ERR_DEVICE_TIMEOUT))
           return false;
-        const int hq = step_head(i), q0 = step_q0(i);
+        const int hq = step_head(sv), q0 = step_q0(sv);
         const bool is_do = DK ? op == 2 : op == 1;
         mbar_arrive_expect_tx(bar(kFull + slot), kUnit);
         for (int s = 0; s < 4; ++s)
@@ -315,9 +330,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float cap_in = CAP ? p.scale / p.soft_cap : 0.f;
     const float cap_out = CAP ? p.soft_cap * kLog2e : 0.f;
     bool ok = true;
+    int sv = -1;
     for (int i = 0; i < n_iter; ++i) {
       const int bf = i & 1, e = i % NR;
-      const int hq = step_head(i), q0 = step_q0(i);
+      sv = next_step(sv);
+      const int hq = step_head(sv), q0 = step_q0(sv);
       uint32_t wbar = bar(kSFull + bf), wpar = (uint32_t)((i >> 1) & 1);
       if ((p.debug_flags & BFA_DEBUG_INJECT_STALL) && i == 0) {
         wbar = bar(kNever);
@@ -515,7 +532,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   int klo, khi;
   key_range(p, q0, min(q0 + kRows, p.Sq), &klo, &khi);
   const int jt0 = klo / NK;
-  const int n_iter = (khi > klo) ? (khi + NK - 1) / NK - jt0 : 0;
+  const int jend = (khi > klo) ? (khi + NK - 1) / NK : jt0;
+  // Block-sparse mask: 64-key step j is visited only when block
+  // (q0 / 128, 64 j / 128) is on; each consumer walks the visited steps.
+  auto step_on = [&](int j) { return block_on(p, b, hq, q0 / kMaskBlock, j * NK / kMaskBlock); };
+  int n_iter = jend - jt0;
+  if (p.blk) {
+    n_iter = 0;
+    for (int j = jt0; j < jend; ++j) n_iter += step_on(j) ? 1 : 0;
+  }
+  auto next_tile = [&](int j) {
+    do { ++j; } while (p.blk && j < jend && !step_on(j));
+    return j;
+  };
 
   WaitCtl ctl{abort_flag, p.status, p.timeout_ns};
 
@@ -546,6 +575,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       int n = 0;
+      auto w0 = make_walker(next_tile, jt0 - 1), w1 = make_walker(next_tile, jt0 - 1),
+           w2 = make_walker(next_tile, jt0 - 1);
       dq_ops(n_iter, [&](int op, int j) -> bool {
         const int slot = n % NS;
         bool ok = true;
@@ -553,7 +584,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         else if (slot >= 2) ok = mbar_wait(bar(kOpsReady), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);  // Q staging free
         if (!ok) return false;
         mbar_arrive_expect_tx(bar(kFull + slot), kUnit);
-        const int key0 = (jt0 + j) * NK;
+        const int key0 = (op == 0 ? w0.step(j) : op == 1 ? w1.step(j) : w2.step(j)) * NK;
         for (int s = 0; s < 4; ++s)
           tma_load_4d(unit_addr(n) + s * kSub64, op == 1 ? &tmV : &tmK, bar(kFull + slot), s * 64, key0, hkv, b);
         ++n;
@@ -656,8 +687,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     uint8_t* ds_base = smem + L::kOffDS;
+    int jv = jt0 - 1;
     for (int j = 0; j < n_iter && ok; ++j) {
-      const int j0 = (jt0 + j) * NK;
+      jv = next_tile(jv);
+      const int j0 = jv * NK;
       uint32_t wbar = bar(kSPFull), wpar = (uint32_t)(j & 1);
       if ((p.debug_flags & BFA_DEBUG_INJECT_STALL) && j == 0) {
         wbar = bar(kNever);

@@ -118,7 +118,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   int klo, khi;
   key_range(p, q0, min(q0 + 2 * kBM, p.Sq), &klo, &khi);
   const int jlo = klo / kBN;
-  const int n_iter = (khi > klo) ? (khi + kBN - 1) / kBN - jlo : 0;
+  const int jend = (khi > klo) ? (khi + kBN - 1) / kBN : jlo;
+  // Block-sparse mask: key tile j (one 128-key block) is visited when either
+  // query tile's block (q0 / 128 + t, j) is on; a tile off for one query tile
+  // only is masked whole in that tile's softmax. Every role walks the visited
+  // tiles in the same order with next_tile().
+  const int qb0 = q0 / kMaskBlock;
+  const bool two_tiles = q0 + kBM < p.Sq;
+  auto tile_on = [&](int j) {
+    return block_on(p, b, hq, qb0, j) || (two_tiles && block_on(p, b, hq, qb0 + 1, j));
+  };
+  int n_iter = jend - jlo;
+  if (p.blk) {
+    n_iter = 0;
+    for (int j = jlo; j < jend; ++j) n_iter += tile_on(j) ? 1 : 0;
+  }
+  auto next_tile = [&](int j) {  // the first visited tile after j
+    do { ++j; } while (p.blk && j < jend && !tile_on(j));
+    return j;
+  };
 
   WaitCtl ctl{abort_flag, p.status, p.timeout_ns};
 
@@ -154,8 +172,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       int n = 0;
       bool ok = true;
+      int j = jlo - 1;
       for (int it = 0; it < n_iter && ok; ++it) {
-        const int j = jlo + it;
+        j = next_tile(j);
         for (int kv = 0; kv < 2; ++kv) {
           const int slot = n % NS;
           if (n >= NS) {
@@ -266,8 +285,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m = neg_inf(), l = 0.f;
     bool ok = true;
 
+    int jt = jlo - 1;
     for (int it = 0; it < n_iter; ++it) {
-      const int c0 = (jlo + it) * kBN;
+      jt = next_tile(jt);
+      const int c0 = jt * kBN;
+      const bool blk_on = (t == 0 || two_tiles) && block_on(p, b, hq, qb0 + t, jt);  // this query tile's block
       uint32_t wbar = bar(kSFull + t), wpar = (uint32_t)(it & 1);
       if ((p.debug_flags & BFA_DEBUG_INJECT_STALL) && t == 0 && it == 0) {
         wbar = bar(kNever);
@@ -283,11 +305,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // scale is > 0) and folds the scale into the exponent with one FMA.
       // Four independent max accumulators (three-input max) and two packed
       // sum accumulators break the dependency chains.
-      const bool full = tile_full(p, tr0, tr0 + kBM, c0, c0 + kBN);
+      const bool full = blk_on && tile_full(p, tr0, tr0 + kBM, c0, c0 + kBN);
       const bool store_x = CAP || ALIBI || !full || !(sl2 > 0.f);  // x != S * sl2
       const float abase = ALIBI ? slope2 * (float)(g0 - (int64_t)c0 - p.k_off) : 0.f;
       int clo, chi;  // kept key columns [clo, chi) of this row (all of them on a full tile)
-      keys_for_query(p, gi, r_local < p.Sq, c0, kBN, &clo, &chi);
+      keys_for_query(p, gi, r_local < p.Sq && blk_on, c0, kBN, &clo, &chi);
       if (full) {
         clo = 0;
         chi = kBN;

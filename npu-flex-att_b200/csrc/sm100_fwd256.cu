@@ -145,7 +145,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   int klo, khi;
   key_range(p, q0, min(q0 + kBM, p.Sq), &klo, &khi);
   const int jlo = klo / kBN;
-  const int n_iter = (khi > klo) ? (khi + kBN - 1) / kBN - jlo : 0;
+  const int jend = (khi > klo) ? (khi + kBN - 1) / kBN : jlo;
+  // Block-sparse mask: key tile j (one 128-key block) is visited only when
+  // block (q0 / 128, j) is on. Step j of the loops below is the j-th visited
+  // tile; each consumer walks them with its own walker.
+  int n_iter = jend - jlo;
+  if (p.blk) {
+    n_iter = 0;
+    for (int j = jlo; j < jend; ++j) n_iter += block_on(p, b, hq, q0 / kMaskBlock, j) ? 1 : 0;
+  }
+  auto next_tile = [&](int j) {
+    do { ++j; } while (p.blk && j < jend && !block_on(p, b, hq, q0 / kMaskBlock, j));
+    return j;
+  };
 
   WaitCtl ctl{abort_flag, p.status, p.timeout_ns};
 
@@ -179,8 +191,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_4d(sbase + kOffQ + s * kQSub, &tmQ, bar(kQFull), s * 64, q0, hq, b);
       }
       int n = 0;
+      auto walk_s = make_walker(next_tile, jlo - 1), walk_pv = make_walker(next_tile, jlo - 1);
       for_each_op(n_iter, [&](int op, int j) -> bool {
-        const int key0 = (jlo + j) * kBN;
+        const int key0 = (op == 0 ? walk_s.step(j) : walk_pv.step(j)) * kBN;
         for (int h = 0; h < 2; ++h, ++n) {
           const int slot = n % NS;
           if (n >= NS && !mbar_wait(bar(kEmpty + slot), ((n / NS) & 1) ^ 1, ctl, BFA_ERR_DEVICE_TIMEOUT))
@@ -276,9 +289,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m = neg_inf(), l = 0.f;
     bool ok = true;
 
+    int jt = jlo - 1;
     for (int it = 0; it < n_iter; ++it) {
       const int bf = it & 1;
-      const int c0k = (jlo + it) * kBN;
+      jt = next_tile(jt);
+      const int c0k = jt * kBN;
       const uint32_t tS = tmem + lane_base + kTmemS + bf * kBN;
       uint32_t wbar = bar(kSFull + bf), wpar = (uint32_t)((it >> 1) & 1);
       if ((p.debug_flags & BFA_DEBUG_INJECT_STALL) && it == 0) {

@@ -79,8 +79,34 @@ def _documents(cu_seqlens, positions: int, device):
     return cu[idx].to(torch.int32).contiguous(), cu[idx + 1].to(torch.int32).contiguous()
 
 
+BLOCK = 128  # block-sparse mask granularity: 128 query rows x 128 keys
+
+
+def _block_mask(block_mask, B: int, Hq: int, Sq: int, Sk: int, device):
+    """Validated block-sparse mask as a uint8 device tensor of shape
+    [B, Hq, ceil(Sq/128), ceil(Sk/128)], batch and head dims possibly broadcast
+    (stride 0). Accepts bool or integer tensors of shape [nq, nk], [Hq, nq, nk]
+    or [B or 1, Hq or 1, nq, nk]; nonzero means the block is computed. The
+    tensor must stay alive until the call's kernels have run (the functions
+    below keep it referenced for the call)."""
+    if block_mask is None:
+        return None
+    m = torch.as_tensor(block_mask)
+    nq, nk = -(-Sq // BLOCK), -(-Sk // BLOCK)
+    while m.dim() < 4:
+        m = m.unsqueeze(0)
+    if m.dim() != 4 or tuple(m.shape[2:]) != (nq, nk) or m.shape[0] not in (1, B) or m.shape[1] not in (1, Hq):
+        raise ValueError(f"block_mask must have shape [B|1, Hq|1, {nq}, {nk}] "
+                         f"(128x128 blocks of a {Sq}x{Sk} score matrix), got {tuple(torch.as_tensor(block_mask).shape)}")
+    m = (m != 0).to(device=device, dtype=torch.uint8)
+    m = m.expand(B, Hq, nq, nk)
+    if m.stride(3) != 1:
+        m = m.contiguous()
+    return m
+
+
 def _problem(query, key, causal, sliding_window, alibi, scale, soft_cap, q_pos=0, k_pos=0,
-             docs=None):
+             docs=None, blk=None):
     B, Hq, Sq, D = query.shape
     _, Hkv, Sk, _ = key.shape
     pr = _bfa.Problem()
@@ -95,6 +121,10 @@ def _problem(query, key, causal, sliding_window, alibi, scale, soft_cap, q_pos=0
     pr.q_pos_offset, pr.k_pos_offset = int(q_pos), int(k_pos)
     if docs is not None:
         pr.doc_start, pr.doc_end = docs[0].data_ptr(), docs[1].data_ptr()
+    if blk is not None:
+        pr.block_mask = blk.data_ptr()
+        for d in range(3):
+            pr.block_mask_stride[d] = blk.stride(d)
     return pr
 
 
@@ -143,6 +173,7 @@ def npu_flash_attention_forward(
     q_pos_offset=0,
     k_pos_offset=0,
     cu_seqlens=None,
+    block_mask=None,
     _wait_timeout_ns=0,
     _debug_flags=0,
 ):
@@ -152,7 +183,11 @@ def npu_flash_attention_forward(
     reference): absolute position offsets for context-parallel shards, and
     document masking -- ``cu_seqlens`` (cumulative document lengths over the
     absolute positions, first 0) keeps only pairs inside one document, on
-    top of the other masks (packed variable-length sequences).
+    top of the other masks (packed variable-length sequences) -- and a
+    block-sparse mask: ``block_mask`` (bool/int, [B|1, Hq|1, ceil(Sq/128),
+    ceil(Sk/128)]) computes only the 128x128 blocks of the score matrix it
+    marks, again on top of the other masks; the kernels skip the other
+    blocks. Rows left with no key give O = 0 and LSE = -inf.
     """
     B, Hq, Sq, D = query.shape
     Bk, Hkv, Sk, Dk = key.shape
@@ -171,7 +206,9 @@ def npu_flash_attention_forward(
     LSE = torch.empty(B, Hq, Sq, device=dev, dtype=torch.float32)
     lib = _bfa.load()
     docs = _documents(cu_seqlens, max(q_pos_offset + Sq, k_pos_offset + Sk), dev)
-    pr = _problem(q, k, causal, sliding_window, alibi, scale, soft_cap, q_pos_offset, k_pos_offset, docs)
+    blk = _block_mask(block_mask, B, Hq, Sq, Sk, dev)
+    pr = _problem(q, k, causal, sliding_window, alibi, scale, soft_cap, q_pos_offset, k_pos_offset, docs,
+                  blk)
     args = _bfa.FwdArgs()
     args.q, args.k, args.v, args.o = _bfa.tensor(q), _bfa.tensor(k), _bfa.tensor(v), _bfa.tensor(o_k)
     args.lse = LSE.data_ptr()
@@ -207,6 +244,7 @@ def npu_flash_attention_backward(
     q_pos_offset=0,
     k_pos_offset=0,
     cu_seqlens=None,
+    block_mask=None,
     _wait_timeout_ns=0,
     _debug_flags=0,
     _phases=0,
@@ -252,7 +290,9 @@ def npu_flash_attention_backward(
     dq_k = _fast_layout(DQ) if DQ.data_ptr() else DQ
     lib = _bfa.load()
     docs = _documents(cu_seqlens, max(q_pos_offset + Sq, k_pos_offset + Sk), dev)
-    pr = _problem(q, k, causal, sliding_window, alibi, scale, soft_cap, q_pos_offset, k_pos_offset, docs)
+    blk = _block_mask(block_mask, B, Hq, Sq, Sk, dev)
+    pr = _problem(q, k, causal, sliding_window, alibi, scale, soft_cap, q_pos_offset, k_pos_offset, docs,
+                  blk)
     args = _bfa.BwdArgs()
     args.q, args.k, args.v = _bfa.tensor(q), _bfa.tensor(k), _bfa.tensor(v)
     args.o, args.dout = _bfa.tensor(o), _bfa.tensor(do)
@@ -281,14 +321,16 @@ class NPUFlexAttention(torch.autograd.Function):
     v only (the mask arguments get None). Same class name, argument order and
     saved state as the reference's autograd class
     (npu_flash_attention.py:742-781), so code that calls ``.apply`` on it
-    keeps working; one optional argument is appended, ``cu_seqlens``
-    (document masking, see npu_flash_attention_forward)."""
+    keeps working; two optional arguments are appended, ``cu_seqlens`` and
+    ``block_mask`` (document and block-sparse masking, see
+    npu_flash_attention_forward)."""
 
     @staticmethod
     def forward(ctx, query, key, value, causal=False, sliding_window=0,
                 alibi_slope=None, scale=None, block_m=16, block_n=64, soft_cap=0.0,
-                cu_seqlens=None):
+                cu_seqlens=None, block_mask=None):
         ctx.cu_seqlens = cu_seqlens
+        ctx.block_mask = block_mask
         ctx.causal = causal
         ctx.sliding_window = sliding_window
         ctx.alibi_slope = alibi_slope
@@ -302,7 +344,7 @@ class NPUFlexAttention(torch.autograd.Function):
                 causal=causal, sliding_window=sliding_window,
                 alibi_slope=alibi_slope, scale=scale,
                 block_m=block_m, block_n=block_n, return_lse=True,
-                soft_cap=soft_cap, cu_seqlens=cu_seqlens,
+                soft_cap=soft_cap, cu_seqlens=cu_seqlens, block_mask=block_mask,
             )
         ctx.save_for_backward(query, key, value, lse, out)
         return out
@@ -315,9 +357,9 @@ class NPUFlexAttention(torch.autograd.Function):
             causal=ctx.causal, sliding_window=ctx.sliding_window,
             alibi_slope=ctx.alibi_slope, scale=ctx.scale,
             block_m=ctx.block_m, block_n=ctx.block_n,
-            soft_cap=ctx.soft_cap, cu_seqlens=ctx.cu_seqlens,
+            soft_cap=ctx.soft_cap, cu_seqlens=ctx.cu_seqlens, block_mask=ctx.block_mask,
         )
-        return DQ, DK, DV, None, None, None, None, None, None, None, None
+        return DQ, DK, DV, None, None, None, None, None, None, None, None, None
 
 
 def npu_flex_attention(
@@ -327,12 +369,14 @@ def npu_flex_attention(
     block_m=16, block_n=64,
     soft_cap=0.0,
     cu_seqlens=None,
+    block_mask=None,
 ):
     """Functional form of NPUFlexAttention.apply with keyword defaults
-    (signature of npu_flash_attention.py:784-794, plus ``cu_seqlens``)."""
+    (signature of npu_flash_attention.py:784-794, plus ``cu_seqlens`` and
+    ``block_mask``)."""
     return NPUFlexAttention.apply(
         query, key, value, causal, sliding_window,
-        alibi_slope, scale, block_m, block_n, soft_cap, cu_seqlens,
+        alibi_slope, scale, block_m, block_n, soft_cap, cu_seqlens, block_mask,
     )
 
 
@@ -348,6 +392,8 @@ class AttentionConfig:
     ``cu_seqlens`` (appended after the reference's fields) adds document
     masking over packed sequences:
         cfg = AttentionConfig(causal=True, cu_seqlens=torch.tensor([0, 700, 1024]))
+    and ``block_mask`` a block-sparse mask (128x128 blocks of the score
+    matrix, see npu_flash_attention_forward).
     """
     causal: bool = False
     sliding_window: int = 0
@@ -357,6 +403,7 @@ class AttentionConfig:
     block_m: int = 16
     block_n: int = 64
     cu_seqlens: Optional[torch.Tensor] = None
+    block_mask: Optional[torch.Tensor] = None
 
     def __post_init__(self):
         if self.sliding_window < 0:
@@ -381,4 +428,5 @@ def flex_attention(query, key, value, config: Optional[AttentionConfig] = None, 
         block_n=config.block_n,
         soft_cap=config.soft_cap,
         cu_seqlens=config.cu_seqlens,
+        block_mask=config.block_mask,
     )

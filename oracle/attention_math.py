@@ -98,6 +98,20 @@ def keep_mask(sq: int, sk: int, causal: bool, window: int,
     return keep
 
 
+def block_keep(block_mask, b: int, hq: int, sq: int, sk: int, block: int = 128) -> torch.Tensor:
+    """Element keep-mask [B, Hq, Sq, Sk] of a block-sparse mask: pair (i, j) of
+    (b, h) is kept when block (i // 128, j // 128) is nonzero; ``block_mask``
+    is [nq, nk], [Hq, nq, nk] or [B|1, Hq|1, nq, nk] over the call's own row
+    and key indices. The reference has no block masks (its README lists them
+    as missing); this restates the rule the build adds."""
+    m = torch.as_tensor(block_mask).cpu() != 0
+    while m.dim() < 4:
+        m = m.unsqueeze(0)
+    m = m.expand(b, hq, m.shape[2], m.shape[3])
+    m = m.repeat_interleave(block, dim=2).repeat_interleave(block, dim=3)
+    return m[:, :, :sq, :sk]
+
+
 def _expand_kv(x: torch.Tensor, hq: int) -> torch.Tensor:
     """GQA head map hkv = hq // G (npu_flash_attention.py:42), as repeat_interleave."""
     hkv = x.shape[1]
@@ -130,7 +144,8 @@ def logits(q, k, *, scale, soft_cap=0.0, alibi_slope=None,
 
 def attention_forward(q, k, v, *, causal=False, sliding_window=0,
                       alibi_slope=None, scale=None, soft_cap=0.0,
-                      q_offset=0, k_offset=0, cu_seqlens=None, dtype=torch.float64):
+                      q_offset=0, k_offset=0, cu_seqlens=None, block_mask=None,
+                      dtype=torch.float64):
     """Forward oracle: returns ``(O, LSE)`` in ``dtype`` (O) and ``dtype`` (LSE).
 
     npu_flash_attention.py:17-166 (kernel) and :606-656 (host wrapper:
@@ -145,6 +160,8 @@ def attention_forward(q, k, v, *, causal=False, sliding_window=0,
                   q_offset=q_offset, k_offset=k_offset)
     keep = keep_mask(q.shape[2], k.shape[2], causal, sliding_window,
                      q_offset, k_offset, cu_seqlens)
+    if block_mask is not None:
+        keep = keep & block_keep(block_mask, q.shape[0], q.shape[1], q.shape[2], k.shape[2])
     u = u.masked_fill(~keep, float("-inf"))
     lse = torch.logsumexp(u, dim=-1)
     finite = torch.isfinite(lse)
@@ -158,7 +175,7 @@ def attention_backward(q, k, v, grad_out, *, causal=False, sliding_window=0,
                        alibi_slope=None, scale=None, soft_cap=0.0,
                        q_offset=0, k_offset=0, alibi_in_backward=True,
                        out=None, lse=None, dtype=torch.float64,
-                       operand_dtype=None, cu_seqlens=None):
+                       operand_dtype=None, cu_seqlens=None, block_mask=None):
     """Backward oracle: returns ``(dQ, dK, dV)`` with dK/dV per KV head.
 
     Restates npu_flash_attention.py:659-739 and the two kernels :298-560.
@@ -183,7 +200,8 @@ def attention_backward(q, k, v, grad_out, *, causal=False, sliding_window=0,
         o_ref, lse_ref = attention_forward(
             q, k, v, causal=causal, sliding_window=sliding_window,
             alibi_slope=alibi_slope, scale=scale, soft_cap=soft_cap,
-            q_offset=q_offset, k_offset=k_offset, cu_seqlens=cu_seqlens, dtype=dtype)
+            q_offset=q_offset, k_offset=k_offset, cu_seqlens=cu_seqlens,
+            block_mask=block_mask, dtype=dtype)
         out = o_ref if out is None else out
         lse = lse_ref if lse is None else lse
     of, lsef = out.to(dtype), lse.to(dtype)
@@ -192,6 +210,8 @@ def attention_backward(q, k, v, grad_out, *, causal=False, sliding_window=0,
                   q_offset=q_offset, k_offset=k_offset)
     keep = keep_mask(q.shape[2], k.shape[2], causal, sliding_window,
                      q_offset, k_offset, cu_seqlens)
+    if block_mask is not None:
+        keep = keep & block_keep(block_mask, q.shape[0], q.shape[1], q.shape[2], k.shape[2])
     finite = torch.isfinite(lsef).unsqueeze(-1)
     p = torch.exp(u - torch.where(finite, lsef.unsqueeze(-1), torch.zeros_like(u[..., :1])))
     p = torch.where(keep & finite, p, torch.zeros_like(p))

@@ -106,3 +106,30 @@ def test_seqlen_q_bound():
     pr = _problem(seqlen_q=2 ** 31 - 1)
     assert lib.bfa_fwd(ctypes.byref(pr), ctypes.byref(bfa_lib.FwdArgs()), None) == -1
     assert lib.bfa_bwd_workspace_bytes(ctypes.byref(pr)) == 0
+
+
+def test_ctypes_structures_match_header_layout(tmp_path):
+    """Size and every field offset of the ctypes mirrors equal the C
+    structures of include/bfa.h, compiled here with gcc."""
+    import shutil
+    import subprocess
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    structs = {"bfa_problem": bfa_lib.Problem, "bfa_tensor": bfa_lib.Tensor,
+               "bfa_fwd_args": bfa_lib.FwdArgs, "bfa_bwd_args": bfa_lib.BwdArgs}
+    lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "bfa.h"', "int main(void) {"]
+    for cname, cls in structs.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for field, _ in cls._fields_:
+            lines.append(f'  printf("{cname} {field} %zu\\n", offsetof({cname}, {field}));')
+    lines += ["  return 0;", "}"]
+    src, exe = tmp_path / "layout.c", tmp_path / "layout"
+    src.write_text("\n".join(lines) + "\n")
+    subprocess.run(["gcc", "-std=c11", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)],
+                   check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    got = {tuple(l.split()[:2]): int(l.split()[2]) for l in out if l.strip()}
+    for cname, cls in structs.items():
+        assert got[(cname, "size")] == ctypes.sizeof(cls), cname
+        for field, _ in cls._fields_:
+            assert got[(cname, field)] == getattr(cls, field).offset, (cname, field)

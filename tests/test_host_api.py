@@ -34,11 +34,27 @@ def test_signatures_match_reference():
                      "sliding_window", "alibi_slope", "scale", "block_m", "block_n", "soft_cap"]
     assert sig.parameters["block_n"].default == 32
     sig = inspect.signature(nfa.npu_flex_attention)
-    # The reference's ten parameters in order, then this build's document mask.
+    # The reference's ten parameters in order, then this build's document and
+    # block-sparse masks.
     assert list(sig.parameters) == ["query", "key", "value", "causal", "sliding_window",
                                     "alibi_slope", "scale", "block_m", "block_n", "soft_cap",
-                                    "cu_seqlens"]
+                                    "cu_seqlens", "block_mask"]
     assert sig.parameters["cu_seqlens"].default is None
+    assert sig.parameters["block_mask"].default is None
+
+
+def test_block_mask_validation_and_broadcast():
+    m = nfa._block_mask(torch.tensor([[1, 0], [1, 1]], dtype=torch.bool), 2, 4, 200, 129, "cpu")
+    assert m.shape == (2, 4, 2, 2) and m.dtype == torch.uint8
+    assert m.stride(0) == 0 and m.stride(1) == 0 and m.stride(3) == 1
+    assert m[1, 3].tolist() == [[1, 0], [1, 1]]
+    m = nfa._block_mask(torch.ones(4, 1, 1, dtype=torch.int32), 2, 4, 100, 100, "cpu")
+    assert m.shape == (2, 4, 1, 1) and m.stride(0) == 0 and m.stride(1) == 1
+    with pytest.raises(ValueError):
+        nfa._block_mask(torch.ones(2, 3), 1, 1, 256, 256, "cpu")
+    with pytest.raises(ValueError):
+        nfa._block_mask(torch.ones(3, 4, 2, 2), 2, 4, 256, 256, "cpu")
+    assert nfa._block_mask(None, 1, 1, 1, 1, "cpu") is None
 
 
 def test_shape_assertions_fire_before_device_work():
