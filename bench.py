@@ -86,7 +86,8 @@ def peaks():
 
 def committed_traffic(phase: str, workload: str = "c3"):
     """DRAM bytes per launch of a kernel from the committed ncu capture, or None."""
-    kernel = {"fwd": "fwd_kernel", "dkdv": "dkdv_kernel", "dq": "dq_kernel"}.get(phase)
+    kernel = {"fwd": "fwd_kernel", "dkdv": "dkdv_kernel", "dq": "dq_kernel",
+              "dq_delta": "dq_kernel"}.get(phase)
     try:
         with open(os.path.join(ROOT, "profiles", f"{workload}_dram_traffic.json")) as f:
             return json.load(f)["kernels"][kernel]["dram_bytes_per_launch"]
@@ -278,7 +279,10 @@ def run_ours(args):
         out, l_ = nfa.npu_flash_attention_forward(q, k, v, return_lse=True, **kw)
         if ev:
             ev[1].record()
-        nfa.npu_flash_attention_backward(q, k, v, out, l_, do, _phases=bfa_lib.PHASE_DELTA,
+        # Δ and dQ in one call: for head dims 64/128 the dQ kernel forms Δ
+        # itself and runs first; dK/dV then reads Δ from the workspace.
+        nfa.npu_flash_attention_backward(q, k, v, out, l_, do,
+                                         _phases=bfa_lib.PHASE_DELTA | bfa_lib.PHASE_DQ,
                                          _workspace=ws, _outputs=grads, **kw)
         if ev:
             ev[2].record()
@@ -286,17 +290,13 @@ def run_ours(args):
                                          _workspace=ws, _outputs=grads, **kw)
         if ev:
             ev[3].record()
-        nfa.npu_flash_attention_backward(q, k, v, out, l_, do, _phases=bfa_lib.PHASE_DQ,
-                                         _workspace=ws, _outputs=grads, **kw)
-        if ev:
-            ev[4].record()
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     nfa.check_device_status(dev)
 
-    events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
@@ -318,7 +318,7 @@ def run_ours(args):
     nfa.check_device_status(dev)
     total_ms = max_over_ranks(start.elapsed_time(end), dev, world)
     phase_ms = [sum(events[i][j].elapsed_time(events[i][j + 1]) for i in range(args.steps)) / args.steps
-                for j in range(4)]
+                for j in range(3)]
     ms_step = total_ms / args.steps
     flops = step_flops(cfg)
     value = world * flops / (ms_step * 1e-3) / 1e12
@@ -331,9 +331,11 @@ def run_ours(args):
 
     peak_tf, _, peak_kind = peaks()
     pairs = pairs_per_head(cfg) * B * Hq
-    kern_flops = {"fwd": 4.0 * D * pairs, "delta": 0.0, "dkdv": 8.0 * D * pairs, "dq": 6.0 * D * pairs}
-    names = ["fwd", "delta", "dkdv", "dq"]
-    dom = max(range(4), key=lambda j: phase_ms[j])
+    # "dq_delta": the dQ kernel with Δ formed in its prologue (head dims
+    # 64/128), or the Δ pass then dQ (head dim 256); its FLOPs are dQ's.
+    kern_flops = {"fwd": 4.0 * D * pairs, "dq_delta": 6.0 * D * pairs, "dkdv": 8.0 * D * pairs}
+    names = ["fwd", "dq_delta", "dkdv"]
+    dom = max(range(3), key=lambda j: phase_ms[j])
     achieved = kern_flops[names[dom]] / (phase_ms[dom] * 1e-3) / 1e12
     kernel_frac = {n: round(kern_flops[n] / (phase_ms[j] * 1e-3) / 1e12 / peak_tf, 4)
                    for j, n in enumerate(names) if kern_flops[n] > 0}

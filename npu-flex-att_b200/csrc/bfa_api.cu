@@ -194,7 +194,11 @@ int bfa_bwd(const bfa_problem* pr, const bfa_bwd_args* a, void* workspace, size_
   p.delta = (float*)ws;
   p.lse2 = (float*)(ws + rowstat_bytes(pr));
   p.Sq_pad = (int32_t)padded_rows(pr->seqlen_q);
-  if (!empty_q(pr) && (p.phases & BFA_BWD_PHASE_DELTA)) {
+  // With Δ and dQ in one call the tcgen05 dQ kernel forms Δ in its prologue
+  // and runs before dK/dV, which reads it.
+  p.fuse_delta = (p.phases & BFA_BWD_PHASE_DELTA) && (p.phases & BFA_BWD_PHASE_DQ) &&
+                 !empty_q(pr) && bfa::sm100_bwd_fuses_delta(p, pr->dtype);
+  if (!empty_q(pr) && (p.phases & BFA_BWD_PHASE_DELTA) && !p.fuse_delta) {
     rc = bfa::launch_delta(p, pr->dtype, st);
     if (rc) return rc;
   }

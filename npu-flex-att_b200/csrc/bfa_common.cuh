@@ -52,6 +52,9 @@ struct Params {
   uint32_t debug_flags;
   uint32_t phases;  // backward: mask of BFA_BWD_PHASE_* (never 0 here)
   uint32_t grad_acc;  // backward: dq/dk/dv are fp32 accumulators (add, don't store)
+  // backward: the dQ kernel forms Δ and lse2 of its rows itself and writes
+  // them for the dK/dV kernel that runs after it (no separate Δ pass).
+  uint32_t fuse_delta;
 };
 
 template <typename T> __device__ __forceinline__ float to_f32(T x);

@@ -28,6 +28,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <type_traits>
 
@@ -468,7 +469,8 @@ struct DqLayout {
   static constexpr uint32_t kOffStage = kOffDO + kQBytes;
   static constexpr uint32_t kOffDS = kOffStage + (kStages - 1) * kStageBytes;
   static constexpr uint32_t kOffBar = kOffDS + kDSBytes;
-  static constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
+  static constexpr uint32_t kOffDlt = kOffBar + 512;  // Δ of the 128 rows (fused Δ)
+  static constexpr uint32_t kSmemBytes = kOffDlt + kRows * 4 + 1024;
   static constexpr uint32_t kTmemS = 0, kTmemDP = 128, kTmemDQ = 256;
   static constexpr uint32_t kTmemQ = kTmemDQ + D, kTmemDO = kTmemQ + D / 2;
   static __host__ __device__ constexpr uint32_t stage_off(int st) {
@@ -484,7 +486,8 @@ template <int D, bool BF16, bool CAP, bool ALIBI>
 __global__ void __launch_bounds__(kThreads, 1)
     dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
               const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-              const __grid_constant__ CUtensorMap tmDQ, const Params p) {
+              const __grid_constant__ CUtensorMap tmDQ, const __grid_constant__ CUtensorMap tmO,
+              const Params p) {
   using L = DqLayout<D>;
   constexpr int NS = L::kStages;
   constexpr int NK = L::kKeys;
@@ -559,10 +562,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // A query tile that sees no key loads nothing: its epilogue stages zeros
       // in the Q tile, which must not have a TMA write in flight.
       if (n_iter > 0) {
-        mbar_arrive_expect_tx(bar(kQFull), 2 * L::kQBytes);
+        const bool fuse = p.fuse_delta != 0;
+        mbar_arrive_expect_tx(bar(kQFull), (fuse ? 3 : 2) * L::kQBytes);
         for (int s = 0; s < L::kSub; ++s) {
           tma_load_4d(sbase + L::kOffQ + s * (kRows * 128), &tmQ, bar(kQFull), s * 64, q0, hq, b);
           tma_load_4d(sbase + L::kOffDO + s * (kRows * 128), &tmDO, bar(kQFull), s * 64, q0, hq, b);
+          // Fused Δ: the O tile goes to the dS tile, free until the first dS.
+          if (fuse) tma_load_4d(sbase + L::kOffDS + s * (kRows * 128), &tmO, bar(kQFull), s * 64, q0, hq, b);
         }
       }
       int n = 0;
@@ -662,8 +668,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float slope2 = slope * kLog2e;
     const int64_t g0 = ALIBI ? alibi_ref(p, slope, gi, qi < p.Sq) : gi;  // ALiBi bias slope·(g0 - j)
     const int64_t ridx = ((int64_t)b * p.Hq + hq) * p.Sq_pad + qi;
-    const float lse2 = p.lse2[ridx];
-    const float dlt = p.delta[ridx];
+    const bool fuse = p.fuse_delta != 0;
+    float lse2, dlt = 0.f;
+    if (!fuse) {
+      lse2 = p.lse2[ridx];
+      dlt = p.delta[ridx];
+    } else {
+      // lse2 as the Δ pass forms it: +inf past Sq and for rows that see no key.
+      lse2 = __int_as_float(0x7f800000);
+      if (qi < p.Sq) {
+        const float lse = p.lse[((int64_t)b * p.Hq + hq) * p.Sq + qi];
+        if (lse != neg_inf()) lse2 = row_lse2(p, lse, hq, qi);
+      }
+    }
+    // Fused Δ: warpgroup 1 forms Δ = Σ O·dO of its row from the O tile (TMA-
+    // loaded with Q and dO into the dS tile, which is free until the first
+    // dS) and the dO row it copies into TMEM below. A tile that sees no key
+    // has Δ = 0 (its P is 0). TMA fills rows past Sq with zeros.
+    const bool form_delta = fuse && eg == 1 && n_iter > 0;
     bool ok = true;
     // Warpgroup 0 moves this thread's Q row, warpgroup 1 its dO row, from the
     // swizzled shared tile into TMEM (lane = row, two elements per column).
@@ -672,7 +694,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) {
         const uint8_t* tile = smem + (eg == 0 ? L::kOffQ : L::kOffDO);
         const uint32_t tcol = tmem + lane_base + (eg == 0 ? L::kTmemQ : L::kTmemDO);
-#pragma unroll 1
+        float2 acc2 = make_float2(0.f, 0.f);
+#pragma unroll
         for (int s = 0; s < L::kSub; ++s) {
           uint32_t r[32];
 #pragma unroll
@@ -681,12 +704,35 @@ __global__ void __launch_bounds__(kThreads, 1)
             r[4 * c] = w.x; r[4 * c + 1] = w.y; r[4 * c + 2] = w.z; r[4 * c + 3] = w.w;
           }
           tmem_st32(tcol + 32 * s, r);
+          if (form_delta) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const uint4 o4 =
+                  *reinterpret_cast<const uint4*>(smem + L::kOffDS + s * (kRows * 128) + sw128_offset(row, c));
+              const uint32_t ow[4] = {o4.x, o4.y, o4.z, o4.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                acc2 = __ffma2_rn(unpack2<BF16>(ow[e]), unpack2<BF16>(r[4 * c + e]), acc2);
+            }
+          }
+        }
+        if (form_delta) {
+          dlt = acc2.x + acc2.y;
+          reinterpret_cast<float*>(smem + L::kOffDlt)[row] = dlt;
         }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(kOpsReady));
+        // Warpgroup 0 takes its row's Δ from warpgroup 1 (the arrivals on
+        // kOpsReady release the shared stores).
+        if (fuse && eg == 0 && (ok = warp_wait(bar(kOpsReady), 0, ctl)))
+          dlt = reinterpret_cast<const float*>(smem + L::kOffDlt)[row];
       }
+    }
+    if (fuse && eg == 1 && qi < p.Sq_pad) {
+      p.delta[ridx] = dlt;
+      p.lse2[ridx] = lse2;
     }
     int jv = jt0 - 1;
     for (int i = 0; i < n_iter && ok; ++i) {
@@ -839,7 +885,7 @@ bool set_smem(K kern, uint32_t bytes) {
 template <int D, bool BF16, bool CAP, bool ALIBI>
 int launch_bwd(const Params& p, int dtype, cudaStream_t st) {
   const int gdt = p.grad_acc ? BFA_DTYPE_F32 : dtype;  // dtype of dq/dk/dv
-  if (p.phases & BFA_BWD_PHASE_DKDV) {
+  auto run_dkdv = [&]() -> int {
     using L = DkdvLayout<D>;
     auto kern = dkdv_kernel<D, BF16, CAP, ALIBI>;
     static std::once_flag once;
@@ -857,28 +903,44 @@ int launch_bwd(const Params& p, int dtype, cudaStream_t st) {
     const unsigned grid = (unsigned)((p.Sk + kRows - 1) / kRows) * p.Hkv * p.B;
     kern<<<grid, kThreads, L::kSmemBytes, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], p);
     note_launch();
-    if (cudaGetLastError() != cudaSuccess) return BFA_ERR_CUDA;
-  }
-  if (p.phases & BFA_BWD_PHASE_DQ) {
+    return cudaGetLastError() == cudaSuccess ? BFA_OK : BFA_ERR_CUDA;
+  };
+  auto run_dq = [&]() -> int {
     using L = DqLayout<D>;
     auto kern = dq_kernel<D, BF16, CAP, ALIBI>;
     static std::once_flag once;
     static bool attr_ok = false;
     std::call_once(once, [&] { attr_ok = set_smem(kern, L::kSmemBytes); });
     if (!attr_ok) return BFA_ERR_CUDA;
-    CUtensorMap m[5];
+    CUtensorMap m[6];
     if (!make_tmap_bhsd(&m[0], p.q, dtype, D, p.Sq, p.Hq, p.B, p.sq_, kRows) ||
         !make_tmap_bhsd(&m[1], p.dout, dtype, D, p.Sq, p.Hq, p.B, p.sdo_, kRows) ||
         !make_tmap_bhsd(&m[2], p.k, dtype, D, p.Sk, p.Hkv, p.B, p.sk_, L::kKeys) ||
         !make_tmap_bhsd(&m[3], p.v, dtype, D, p.Sk, p.Hkv, p.B, p.sv_, L::kKeys) ||
         !make_tmap_bhsd(&m[4], p.dq, gdt, D, p.Sq, p.Hq, p.B, p.sdq_, kRows))
       return BFA_ERR_CUDA;
+    // O (fused Δ only; otherwise a copy of the Q map that is never read).
+    if (p.fuse_delta) {
+      if (!make_tmap_bhsd(&m[5], p.o, dtype, D, p.Sq, p.Hq, p.B, p.so_, kRows)) return BFA_ERR_CUDA;
+    } else {
+      m[5] = m[0];
+    }
     const unsigned grid = (unsigned)((p.Sq + kRows - 1) / kRows) * p.Hq * p.B;
-    kern<<<grid, kThreads, L::kSmemBytes, st>>>(m[0], m[1], m[2], m[3], m[4], p);
+    kern<<<grid, kThreads, L::kSmemBytes, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], p);
     note_launch();
-    if (cudaGetLastError() != cudaSuccess) return BFA_ERR_CUDA;
+    return cudaGetLastError() == cudaSuccess ? BFA_OK : BFA_ERR_CUDA;
+  };
+  // With a fused Δ the dQ kernel writes the row statistics dK/dV reads, so
+  // it runs first.
+  int rc = BFA_OK;
+  if (p.fuse_delta) {
+    rc = run_dq();
+    if (rc == BFA_OK && (p.phases & BFA_BWD_PHASE_DKDV)) rc = run_dkdv();
+    return rc;
   }
-  return BFA_OK;
+  if (p.phases & BFA_BWD_PHASE_DKDV) rc = run_dkdv();
+  if (rc == BFA_OK && (p.phases & BFA_BWD_PHASE_DQ)) rc = run_dq();
+  return rc;
 }
 
 template <int D, bool BF16>
@@ -902,6 +964,16 @@ bool sm100_bwd_eligible(const Params& p, int dtype) {
          tma_layout_ok(p.v, p.sv_, 2) && tma_layout_ok(p.dout, p.sdo_, 2) &&
          tma_layout_ok(p.dq, p.sdq_, ges) && tma_layout_ok(p.dk, p.sdk_, ges) &&
          tma_layout_ok(p.dv, p.sdv_, ges);
+}
+
+bool sm100_bwd_fuses_delta(const Params& p, int dtype) {
+  static const bool enabled = [] {
+    const char* e = std::getenv("BFA_BWD_FUSE_DELTA");
+    return !(e && e[0] == '0');
+  }();
+  if (!enabled || (p.D != 64 && p.D != 128) || !p.lse || !p.lse2 || !sm100_bwd_eligible(p, dtype))
+    return false;
+  return tma_layout_ok(p.o, p.so_, 2);  // the dQ kernel TMA-loads the O tile
 }
 
 int sm100_bwd(const Params& p, int dtype, cudaStream_t st) {

@@ -30,6 +30,13 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   return BF16 ? pack_bf16(a, b) : pack_f16(a, b);
 }
 
+// The two 16-bit values of a packed word (low half first) as floats.
+template <bool BF16>
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+  if (BF16) return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+
 // Logit in the base-2 domain: (cap·tanh(s·scale/cap) or s·scale)·log2(e).
 // `t` receives tanh(s·scale/cap) for the soft-cap chain. SMALL selects
 // tanh_small (every |s·scale/cap| of the warp's step is <= 1/2, see

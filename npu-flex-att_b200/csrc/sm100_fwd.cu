@@ -80,7 +80,9 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   return BF16 ? pack_bf16(a, b) : pack_f16(a, b);
 }
 
-template <int D, bool BF16, bool CAP, bool ALIBI>
+// BLK: a block-sparse mask is given (p.blk); without it the tile walk is the
+// plain range [jlo, jend), resolved at compile time.
+template <int D, bool BF16, bool CAP, bool ALIBI, bool BLK>
 __global__ void __launch_bounds__(kThreads, 1)
     fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
@@ -126,15 +128,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int qb0 = q0 / kMaskBlock;
   const bool two_tiles = q0 + kBM < p.Sq;
   auto tile_on = [&](int j) {
-    return block_on(p, b, hq, qb0, j) || (two_tiles && block_on(p, b, hq, qb0 + 1, j));
+    return !BLK || block_on(p, b, hq, qb0, j) || (two_tiles && block_on(p, b, hq, qb0 + 1, j));
   };
   int n_iter = jend - jlo;
-  if (p.blk) {
+  if (BLK) {
     n_iter = 0;
     for (int j = jlo; j < jend; ++j) n_iter += tile_on(j) ? 1 : 0;
   }
   auto next_tile = [&](int j) {  // the first visited tile after j
-    do { ++j; } while (p.blk && j < jend && !tile_on(j));
+    do { ++j; } while (BLK && j < jend && !tile_on(j));
     return j;
   };
 
@@ -289,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int it = 0; it < n_iter; ++it) {
       jt = next_tile(jt);
       const int c0 = jt * kBN;
-      const bool blk_on = (t == 0 || two_tiles) && block_on(p, b, hq, qb0 + t, jt);  // this query tile's block
+      const bool blk_on = !BLK || ((t == 0 || two_tiles) && block_on(p, b, hq, qb0 + t, jt));  // this query tile's block
       uint32_t wbar = bar(kSFull + t), wpar = (uint32_t)(it & 1);
       if ((p.debug_flags & BFA_DEBUG_INJECT_STALL) && t == 0 && it == 0) {
         wbar = bar(kNever);
@@ -482,10 +484,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int D, bool BF16, bool CAP, bool ALIBI>
+template <int D, bool BF16, bool CAP, bool ALIBI, bool BLK>
 int launch_fwd(const Params& p, const Tmaps4& tm, cudaStream_t st) {
   using L = FwdLayout<D>;
-  auto kern = fwd_kernel<D, BF16, CAP, ALIBI>;
+  auto kern = fwd_kernel<D, BF16, CAP, ALIBI, BLK>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
@@ -500,13 +502,18 @@ int launch_fwd(const Params& p, const Tmaps4& tm, cudaStream_t st) {
   return cudaGetLastError() == cudaSuccess ? BFA_OK : BFA_ERR_CUDA;
 }
 
+template <int D, bool BF16, bool BLK>
+int dispatch_cap(const Params& p, const Tmaps4& tm, cudaStream_t st) {
+  const bool cap = p.soft_cap > 0.f, alibi = p.alibi != nullptr;
+  if (cap && alibi) return launch_fwd<D, BF16, true, true, BLK>(p, tm, st);
+  if (cap) return launch_fwd<D, BF16, true, false, BLK>(p, tm, st);
+  if (alibi) return launch_fwd<D, BF16, false, true, BLK>(p, tm, st);
+  return launch_fwd<D, BF16, false, false, BLK>(p, tm, st);
+}
+
 template <int D, bool BF16>
 int dispatch_flags(const Params& p, const Tmaps4& tm, cudaStream_t st) {
-  const bool cap = p.soft_cap > 0.f, alibi = p.alibi != nullptr;
-  if (cap && alibi) return launch_fwd<D, BF16, true, true>(p, tm, st);
-  if (cap) return launch_fwd<D, BF16, true, false>(p, tm, st);
-  if (alibi) return launch_fwd<D, BF16, false, true>(p, tm, st);
-  return launch_fwd<D, BF16, false, false>(p, tm, st);
+  return p.blk ? dispatch_cap<D, BF16, true>(p, tm, st) : dispatch_cap<D, BF16, false>(p, tm, st);
 }
 
 }  // namespace
