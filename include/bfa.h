@@ -161,6 +161,12 @@ uint64_t bfa_launch_count(void);
 /* Static message for a bfa_status value. */
 const char* bfa_strerror(int status);
 
+/* Detail of the last BFA_ERR_CUDA this thread got from the library: the
+ * failing call (kernel launch, shared-memory attribute, tensor-map encode,
+ * ...) and the CUDA error name, e.g. "dq_kernel launch: cudaErrorInvalidValue".
+ * "" when none; valid until the thread's next library call fails. */
+const char* bfa_last_error(void);
+
 /* Forward: O and LSE. Replaces the launch at npu_flash_attention.py:631-652. */
 int bfa_fwd(const bfa_problem* problem, const bfa_fwd_args* args, void* stream);
 

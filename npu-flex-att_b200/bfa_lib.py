@@ -20,7 +20,7 @@ DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 DEBUG_INJECT_STALL = 1
 ERR_DEVICE_TIMEOUT = -6
 
-EXPORTED = ("bfa_abi_version", "bfa_launch_count", "bfa_strerror", "bfa_fwd",
+EXPORTED = ("bfa_abi_version", "bfa_launch_count", "bfa_strerror", "bfa_last_error", "bfa_fwd",
             "bfa_fwd_workspace_bytes", "bfa_bwd_workspace_bytes", "bfa_bwd_delta", "bfa_bwd", "bfa_bwd_noalloc",
             "bfa_merge_partial")
 ERR_SCRATCH_LIMIT = -7
@@ -83,6 +83,8 @@ def load() -> ctypes.CDLL:
         lib.bfa_launch_count.argtypes = []
         lib.bfa_strerror.restype = ctypes.c_char_p
         lib.bfa_strerror.argtypes = [ctypes.c_int]
+        lib.bfa_last_error.restype = ctypes.c_char_p
+        lib.bfa_last_error.argtypes = []
         lib.bfa_fwd.restype = ctypes.c_int
         lib.bfa_fwd.argtypes = [ctypes.POINTER(Problem), ctypes.POINTER(FwdArgs), ctypes.c_void_p]
         lib.bfa_fwd_workspace_bytes.restype = ctypes.c_size_t
@@ -109,9 +111,18 @@ def load() -> ctypes.CDLL:
     return _lib
 
 
+ERR_CUDA = -5
+
+
 def check(rc: int) -> None:
     if rc != 0:
-        raise RuntimeError(load().bfa_strerror(rc).decode())
+        lib = load()
+        msg = lib.bfa_strerror(rc).decode()
+        if rc == ERR_CUDA:
+            detail = lib.bfa_last_error().decode()
+            if detail:
+                msg = f"{msg} ({detail})"
+        raise RuntimeError(msg)
 
 
 def bfa_dtype(dt: torch.dtype) -> int:

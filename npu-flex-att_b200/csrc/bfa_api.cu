@@ -4,6 +4,7 @@
 // :669-673): head dims must agree and Hq must be a multiple of Hkv. The fast
 // tcgen05/TMA kernels take bf16/fp16 problems whose layout TMA can read; every
 // other problem runs on the generic CUDA-core kernels. There is no CPU path.
+#include <cstdio>
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -17,6 +18,21 @@ namespace {
 std::atomic<uint64_t> g_launches{0};
 }
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+namespace {
+thread_local char g_last_error[192];
+}
+
+int cuda_fail(const char* what, cudaError_t e) {
+  std::snprintf(g_last_error, sizeof(g_last_error), "%s: %s", what,
+                e == cudaSuccess ? "failed" : cudaGetErrorName(e));
+  return BFA_ERR_CUDA;
+}
+
+int launch_status(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? BFA_OK : cuda_fail(what, e);
+}
 }  // namespace bfa
 
 namespace {
@@ -75,6 +91,8 @@ extern "C" {
 int bfa_abi_version(void) { return BFA_ABI_VERSION; }
 
 uint64_t bfa_launch_count(void) { return bfa::g_launches.load(std::memory_order_relaxed); }
+
+const char* bfa_last_error(void) { return bfa::g_last_error; }
 
 const char* bfa_strerror(int status) {
   switch (status) {

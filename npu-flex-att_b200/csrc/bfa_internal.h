@@ -43,6 +43,11 @@ int launch_merge(int B, int H, int S, int D, const bfa_tensor& oa, int adt, floa
 // Count one kernel launch (bfa_launch_count).
 void note_launch();
 
+// Record `what` and the CUDA error for bfa_last_error() and return
+// BFA_ERR_CUDA. launch_status() does so for the last launch's error, if any.
+int cuda_fail(const char* what, cudaError_t e);
+int launch_status(const char* what);
+
 // Bytes of one element of a bfa_dtype (0 when invalid).
 inline int dtype_bytes(int dt) {
   return dt == BFA_DTYPE_F32 ? 4 : (dt == BFA_DTYPE_F16 || dt == BFA_DTYPE_BF16) ? 2 : 0;

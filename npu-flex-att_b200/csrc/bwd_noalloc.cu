@@ -47,11 +47,13 @@ float* g_addr[kMaxDevices] = {};
 // Device address of g_delta_scratch on the current device (looked up once).
 int scratch_address(float** out) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return BFA_ERR_CUDA;
+  if (cudaError_t e = cudaGetDevice(&dev)) return bfa::cuda_fail("cudaGetDevice", e);
+  if (dev < 0 || dev >= kMaxDevices) return bfa::cuda_fail("bfa_bwd_noalloc: device index out of range", cudaSuccess);
   std::lock_guard<std::mutex> lock(g_mu);
   if (!g_addr[dev]) {
     void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_delta_scratch) != cudaSuccess || !ptr) return BFA_ERR_CUDA;
+    if (cudaError_t e = cudaGetSymbolAddress(&ptr, g_delta_scratch)) return bfa::cuda_fail("cudaGetSymbolAddress", e);
+    if (!ptr) return bfa::cuda_fail("cudaGetSymbolAddress", cudaSuccess);
     g_addr[dev] = static_cast<float*>(ptr);
   }
   *out = g_addr[dev];

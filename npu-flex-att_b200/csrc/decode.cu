@@ -732,7 +732,7 @@ bool plan_decode(const Params& p, DecodePlan* pl) {
 template <typename T, int D>
 int launch_decode(const Params& p, void* ws, size_t ws_bytes, cudaStream_t st) {
   DecodePlan pl;
-  if (!plan_decode<T, D>(p, &pl)) return BFA_ERR_CUDA;
+  if (!plan_decode<T, D>(p, &pl)) return cuda_fail("decode plan (device query)", cudaSuccess);
   if (!ws || ((uintptr_t)ws & 255u) != 0 || ws_bytes < pl.o_bytes + pl.l_bytes) return -1;
   float* part_o = static_cast<float*>(ws);
   float* part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + pl.o_bytes);
@@ -747,7 +747,7 @@ int launch_decode(const Params& p, void* ws, size_t ws_bytes, cudaStream_t st) {
     note_launch();
     err = cudaGetLastError();
   }
-  return err == cudaSuccess ? BFA_OK : BFA_ERR_CUDA;
+  return err == cudaSuccess ? BFA_OK : cuda_fail("decode kernels launch", err);
 }
 
 template <typename T, int D>

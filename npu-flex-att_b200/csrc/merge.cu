@@ -51,7 +51,7 @@ int launch_a(int B, int H, int S, int D, const bfa_tensor& oa, float* la, const 
     default: return BFA_ERR_UNSUPPORTED;
   }
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? BFA_OK : BFA_ERR_CUDA;
+  return launch_status("merge kernel launch");
 }
 
 }  // namespace

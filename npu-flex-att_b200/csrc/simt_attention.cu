@@ -390,13 +390,13 @@ template <typename T, int DP>
 int launch_fwd_t(const Params& p, cudaStream_t st) {
   const size_t smem = (size_t)(TM + 2 * TN) * (DP + 1) * 4 + (size_t)TM * (TN + 1) * 4;
   auto kern = simt_fwd_kernel<T, DP>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return BFA_ERR_CUDA;
+  if (cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))
+    return cuda_fail("simt_fwd_kernel shared-memory attribute", e);
   dim3 grid((p.Sq + TM - 1) / TM, p.Hq, p.B);
   if (grid.x == 0 || grid.y == 0 || grid.z == 0) return BFA_OK;
   kern<<<grid, NT, smem, st>>>(p);
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? BFA_OK : BFA_ERR_CUDA;
+  return launch_status("simt_fwd_kernel launch");
 }
 
 template <typename T, int DP>
@@ -404,25 +404,25 @@ int launch_bwd_t(const Params& p, cudaStream_t st) {
   if (p.phases & BFA_BWD_PHASE_DQ) {
     const size_t smem = (size_t)(2 * TM + 2 * TN) * (DP + 1) * 4 + (size_t)TM * (TN + 1) * 4;
     auto kern = simt_bwd_dq_kernel<T, DP>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return BFA_ERR_CUDA;
+    if (cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))
+      return cuda_fail("simt backward shared-memory attribute", e);
     dim3 grid((p.Sq + TM - 1) / TM, p.Hq, p.B);
     if (grid.x && grid.y && grid.z) {
       kern<<<grid, NT, smem, st>>>(p);
       note_launch();
-      if (cudaGetLastError() != cudaSuccess) return BFA_ERR_CUDA;
+      if (int rc = launch_status("simt backward kernel launch")) return rc;
     }
   }
   if (p.phases & BFA_BWD_PHASE_DKDV) {
     const size_t smem = (size_t)(2 * TM + 2 * TN) * (DP + 1) * 4 + (size_t)2 * TN * (TM + 1) * 4 + 2 * TM * 4;
     auto kern = simt_bwd_dkdv_kernel<T, DP>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return BFA_ERR_CUDA;
+    if (cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))
+      return cuda_fail("simt backward shared-memory attribute", e);
     dim3 grid((p.Sk + TN - 1) / TN, p.Hkv, p.B);
     if (grid.x && grid.y && grid.z) {
       kern<<<grid, NT, smem, st>>>(p);
       note_launch();
-      if (cudaGetLastError() != cudaSuccess) return BFA_ERR_CUDA;
+      if (int rc = launch_status("simt backward kernel launch")) return rc;
     }
   }
   return BFA_OK;
@@ -483,7 +483,7 @@ int launch_delta(const Params& p, int dtype, cudaStream_t st) {
       else delta_vec_kernel<__half, 8><<<vblocks, 256, 0, st>>>(p);
     }
     note_launch();
-    return cudaGetLastError() == cudaSuccess ? BFA_OK : BFA_ERR_CUDA;
+    return launch_status("delta_vec_kernel launch");
   }
   const unsigned blocks = (unsigned)((rows + 7) / 8);
   switch (dtype) {
@@ -493,7 +493,7 @@ int launch_delta(const Params& p, int dtype, cudaStream_t st) {
     default: return BFA_ERR_UNSUPPORTED;
   }
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? BFA_OK : BFA_ERR_CUDA;
+  return launch_status("delta_kernel launch");
 }
 
 }  // namespace bfa

@@ -88,9 +88,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     kQEmpty = 1 + NS,
     kSPFull = 1 + 2 * NS,
     kDSFull = kSPFull + 2,
-    kAccDone = kDSFull + 2,
+    kDDDone = kDSFull + 2,  // dV/dK(i) complete (parity i % 2): Pᵀ/dSᵀ(i) read
+    kAccDone = kDDDone + 2,
     kDrain = kAccDone + 1,
-    kNever = kDrain + 1,
+    kDrainSP = kDrain + 1,
+    kNever = kDrainSP + 1,
     kNumBars = kNever + 1
   };
 
@@ -193,65 +195,66 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = (issued > NS ? issued - NS : 0); i < issued; ++i)
         drain_wait(bar(kQFull + i % NS), (i / NS) & 1, p.timeout_ns);
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    // Per step i: S/dP(i+1) are issued before dV/dK(i) so that they overlap
-    // the elementwise work of step i. S/dP(i+2) reuse the TMEM of Pᵀ/dSᵀ(i);
-    // they are issued after dV/dK(i), and one thread's MMAs run in order.
+  } else if (warp == 1 || warp == 3) {
+    // ------------------------------------------------------------ MMA issuers
+    // Two threads issue the MMAs: warp 1 Sᵀ/dPᵀ(i), warp 3 dV/dK(i). A
+    // thread whose MMA queue is full blocks at the next issue, so with one
+    // issuer dV/dK(i) queued behind Sᵀ/dPᵀ(i+1) and reached the tensor pipe
+    // several hundred cycles after dSᵀ(i) was ready. Split, dV/dK(i) is issued
+    // as soon as the elementwise warps release it. Ordering between the two
+    // comes from mbarriers: Sᵀ/dPᵀ(i+2) overwrite the TMEM of Pᵀ/dSᵀ(i), so
+    // they wait for dV/dK(i) to complete (kDDDone), and dV/dK(i) follows the
+    // elementwise step, which waited for Sᵀ/dPᵀ(i).
     if (lane == 0) {
       constexpr uint32_t idSP = idesc_f16(kRows, kInner, BF16, false);
       constexpr uint32_t idAcc = idesc_f16(kRows, D, BF16, true);
       auto stage = [&](int i) -> uint32_t { return sbase + L::kOffStage + (i % NS) * L::kStageBytes; };
-      // Descriptors are built once; a K step only moves the start address
-      // (a compile-time offset added to the low field).
-      const uint64_t dK0 = desc_kmajor(sbase + L::kOffK), dV0 = desc_kmajor(sbase + L::kOffV);
-      auto issue_sp = [&](int i) {
-        const int bf = i & 1;
-        const uint64_t dq = desc_kmajor(stage(i)), ddo = desc_kmajor(stage(i) + L::kQBytes);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t offkv = ((kk >> 2) * (kRows * 128) + (kk & 3) * 32) >> 4;
-          const uint32_t offq = ((kk >> 2) * (kInner * 128) + (kk & 3) * 32) >> 4;
-          mma_ss(tmem + L::kTmemS + 64 * bf, dK0 + offkv, dq + offq, idSP, kk > 0 ? 1u : 0u);
-          mma_ss(tmem + L::kTmemDP + 64 * bf, dV0 + offkv, ddo + offq, idSP, kk > 0 ? 1u : 0u);
-        }
-        mma_commit(bar(kSPFull + bf));
-      };
-      bool ok = n_iter == 0 || mbar_wait(bar(kKVFull), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
-      if (ok && n_iter > 0) {
-        ok = mbar_wait(bar(kQFull), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
-        if (ok) {
+      if (warp == 1) {
+        // Descriptors are built once; a K step only moves the start address
+        // (a compile-time offset added to the low field).
+        const uint64_t dK0 = desc_kmajor(sbase + L::kOffK), dV0 = desc_kmajor(sbase + L::kOffV);
+        bool ok = n_iter == 0 || mbar_wait(bar(kKVFull), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
+        for (int i = 0; i < n_iter && ok; ++i) {
+          const int bf = i & 1;
+          if (!(ok = mbar_wait(bar(kQFull + i % NS), (i / NS) & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
+          if (i >= 2 && !(ok = mbar_wait(bar(kDDDone + bf), ((i - 2) >> 1) & 1, ctl, BFA_ERR_DEVICE_TIMEOUT)))
+            break;
           tc_fence_after();
-          issue_sp(0);
-        }
-      }
-      for (int i = 0; i < n_iter && ok; ++i) {
-        const int bf = i & 1, k = i >> 1;
-        if (i + 1 < n_iter) {
-          // Q/dO come by TMA (ordered by the mbarrier). The S/dP buffer being
-          // overwritten was last read by the elementwise warps of step i - 1,
-          // ordered by the DSFull wait and fence of that step.
-          const int n1 = i + 1;
-          if (!(ok = mbar_wait(bar(kQFull + n1 % NS), (n1 / NS) & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
-          issue_sp(n1);
-        }
-        if (!(ok = mbar_wait(bar(kDSFull + bf), k & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
-        tc_fence_after();
-        const uint64_t mq = desc_mnmajor(stage(i), kInner * 128);
-        const uint64_t mdo = desc_mnmajor(stage(i) + L::kQBytes, kInner * 128);
+          const uint64_t dq = desc_kmajor(stage(i)), ddo = desc_kmajor(stage(i) + L::kQBytes);
 #pragma unroll
-        for (int kk = 0; kk < kInner / 16; ++kk) {
-          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-          mma_ts(tmem + L::kTmemDV, tmem + L::kTmemS + 64 * bf + 32 * (kk >> 1) + 8 * (kk & 1), mdo + ((kk * 2048) >> 4),
-                 idAcc, acc);
-          mma_ts(tmem + L::kTmemDK, tmem + L::kTmemDP + 64 * bf + 32 * (kk >> 1) + 8 * (kk & 1), mq + ((kk * 2048) >> 4),
-                 idAcc, acc);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t offkv = ((kk >> 2) * (kRows * 128) + (kk & 3) * 32) >> 4;
+            const uint32_t offq = ((kk >> 2) * (kInner * 128) + (kk & 3) * 32) >> 4;
+            mma_ss(tmem + L::kTmemS + 64 * bf, dK0 + offkv, dq + offq, idSP, kk > 0 ? 1u : 0u);
+            mma_ss(tmem + L::kTmemDP + 64 * bf, dV0 + offkv, ddo + offq, idSP, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(bar(kSPFull + bf));
         }
-        mma_commit(bar(kQEmpty + i % NS));
+        mma_commit(bar(kDrainSP));
+        drain_wait(bar(kDrainSP), 0, p.timeout_ns);
+      } else {
+        bool ok = true;
+        for (int i = 0; i < n_iter && ok; ++i) {
+          const int bf = i & 1, k = i >> 1;
+          if (!(ok = mbar_wait(bar(kDSFull + bf), k & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
+          tc_fence_after();
+          const uint64_t mq = desc_mnmajor(stage(i), kInner * 128);
+          const uint64_t mdo = desc_mnmajor(stage(i) + L::kQBytes, kInner * 128);
+#pragma unroll
+          for (int kk = 0; kk < kInner / 16; ++kk) {
+            const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+            mma_ts(tmem + L::kTmemDV, tmem + L::kTmemS + 64 * bf + 32 * (kk >> 1) + 8 * (kk & 1),
+                   mdo + ((kk * 2048) >> 4), idAcc, acc);
+            mma_ts(tmem + L::kTmemDK, tmem + L::kTmemDP + 64 * bf + 32 * (kk >> 1) + 8 * (kk & 1),
+                   mq + ((kk * 2048) >> 4), idAcc, acc);
+          }
+          mma_commit(bar(kQEmpty + i % NS));
+          mma_commit(bar(kDDDone + bf));
+        }
+        mma_commit(bar(kAccDone));
+        mma_commit(bar(kDrain));
+        drain_wait(bar(kDrain), 0, p.timeout_ns);
       }
-      mma_commit(bar(kAccDone));
-      mma_commit(bar(kDrain));
-      drain_wait(bar(kDrain), 0, p.timeout_ns);
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ elementwise
@@ -268,25 +271,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float cap_in = CAP ? p.scale / p.soft_cap : 0.f;
     const float cap_out = CAP ? p.soft_cap * kLog2e : 0.f;
     bool ok = true;
+    // Per-step metadata without a division or the general tile test per step
+    // (a step's setup is a serial chain on the elementwise warps' critical
+    // path): the q-head offset hs and query-tile index ts advance
+    // incrementally (a division only under a block-sparse mask, whose walk
+    // skips steps), and without documents tile_full's conditions are linear
+    // in the step's first query q0: the step is fully kept exactly when q0
+    // lies in [full_lo, full_hi].
+    int hs = 0, ts = -1;
+    const bool lin_full = p.doc_lo == nullptr;
+    int64_t full_lo = p.causal ? (int64_t)c0 + kRows - 1 + p.k_off - p.q_off : -((int64_t)1 << 40);
+    int64_t full_hi = (int64_t)p.Sq - kInner;
+    if (p.window > 0) full_hi = min(full_hi, (int64_t)p.window + c0 + p.k_off - p.q_off - (kInner - 1));
+    if (c0 + kRows > p.Sk) full_hi = full_lo - 1;
     int sv = -1;
     for (int i = 0; i < n_iter; ++i) {
       const int bf = i & 1, k = i >> 1, st = i % NS;
       sv = next_step(sv);
-      const int hq = step_hq(sv);
-      const int q0 = step_q0(sv);
-      uint32_t wbar = bar(kSPFull + bf), wpar = (uint32_t)(k & 1);
-      if ((p.debug_flags & BFA_DEBUG_INJECT_STALL) && i == 0) {
-        wbar = bar(kNever);
-        wpar = 0;
+      if (p.blk) {
+        hs = sv / n_qt;
+        ts = sv - hs * n_qt;
+      } else if (++ts == n_qt) {
+        ts = 0;
+        ++hs;
       }
-      if (!(ok = warp_wait(wbar, wpar, ctl))) break;
-      // The stage's lse2 / Δ arrived with its Q / dO (same barrier phase).
-      if (!(ok = warp_wait(bar(kQFull + st), (uint32_t)((i / NS) & 1), ctl))) break;
-      tc_fence_after();
+      const int hq = hkv * p.G + hs;
+      const int q0 = (qt0 + ts) * kInner;
+      // The step's mask and bias constants first: they overlap the wait.
       const uint32_t tSb = tmem + lane_base + L::kTmemS + 64 * bf;
       const uint32_t tDb = tmem + lane_base + L::kTmemDP + 64 * bf;
       const float* rowv = (const float*)(smem + L::kOffRow + st * 512);
-      const bool full = tile_full(p, q0, q0 + kInner, c0, c0 + kRows);
+      const bool full = lin_full ? ((int64_t)q0 >= full_lo && (int64_t)q0 <= full_hi)
+                                 : tile_full(p, q0, q0 + kInner, c0, c0 + kRows);
       const float slope = ALIBI ? p.alibi[hq] : 0.f;
       const float slope2 = slope * kLog2e;
       // ALiBi bias slope·(g0_i - j) (alibi_ref): with slope > 0, g0_i =
@@ -300,80 +316,105 @@ __global__ void __launch_bounds__(kThreads, 1)
                        : !shifted ? slope2 * (float)((int64_t)q0 + p.q_off - gj)
                        : p.window > 0 ? slope2 * (float)((int64_t)q0 + p.q_off - p.window - gj)
                                       : neg_inf();
-      int clo, chi;  // kept query columns [clo, chi) of this key row
-      queries_for_key(p, gj, kj < p.Sk, q0, kInner, &clo, &chi);
+      int clo = 0, chi = kInner;  // kept query columns [clo, chi) of this key row (masked steps)
+      if (!full) queries_for_key(p, gj, kj < p.Sk, q0, kInner, &clo, &chi);
+      uint32_t wbar = bar(kSPFull + bf), wpar = (uint32_t)(k & 1);
+      if ((p.debug_flags & BFA_DEBUG_INJECT_STALL) && i == 0) {
+        wbar = bar(kNever);
+        wpar = 0;
+      }
+      if (!(ok = warp_wait(wbar, wpar, ctl))) break;
+      // The stage's lse2 / Δ arrived with its Q / dO (same barrier phase).
+      if (!(ok = warp_wait(bar(kQFull + st), (uint32_t)((i / NS) & 1), ctl))) break;
+      tc_fence_after();
       // One body per case (mask or not), chosen once per step: no branches
       // inside the unrolled column loop.
       const int half = eg;
+      // Sᵀ first; dPᵀ loads while P is formed (pass 1), dS follows (pass 2).
       uint32_t sr[32], dr[32];
       tmem_ld32(tSb + 32 * half, sr);
-      tmem_ld32(tDb + 32 * half, dr);
       tmem_ld_wait();
+      tmem_ld32(tDb + 32 * half, dr);
       const bool small = CAP && cap_small<32>(sr, cap_in);
       auto step = [&](auto masked, auto small_tag) {
         constexpr bool MASKED = decltype(masked)::value;
         constexpr bool SMALL = decltype(small_tag)::value;
-        {
-          uint32_t ppk[16], dpk[16];
+        float pr[32];
+        float tt[CAP ? 32 : 1];
+        uint32_t ppk[16];
 #pragma unroll
-          for (int c = 0; c < 32; c += 4) {
-            const float4 l4 = *reinterpret_cast<const float4*>(rowv + 32 * half + c);
-            const float4 d4 = *reinterpret_cast<const float4*>(rowv + 64 + 32 * half + c);
-            const float lse_c[4] = {l4.x, l4.y, l4.z, l4.w};
-            const float dl_c[4] = {d4.x, d4.y, d4.z, d4.w};
-            float pr4[4], ds4[4];
-            if (!CAP && !ALIBI) {
-              // Plain logits: two keys per packed instruction (fma / add /
-              // mul .f32x2), which leaves issue slots to the MMA thread on
-              // the same sub-partition.
+        for (int c = 0; c < 32; c += 4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(rowv + 32 * half + c);
+          const float lse_c[4] = {l4.x, l4.y, l4.z, l4.w};
+          if (!CAP && !ALIBI) {
+            // Plain logits: two keys per packed instruction, which leaves
+            // issue slots to the MMA thread on the same sub-partition.
 #pragma unroll
-              for (int h = 0; h < 4; h += 2) {
-                const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[c + h]), __uint_as_float(sr[c + h + 1])),
-                                            make_float2(sl2, sl2), make_float2(-lse_c[h], -lse_c[h + 1]));
-                float pr0 = ex2(x.x), pr1 = ex2(x.y);
-                if (MASKED) {
-                  const int cc = 32 * half + c + h;
-                  pr0 = ((unsigned)(cc - clo) < (unsigned)(chi - clo)) ? pr0 : 0.f;
-                  pr1 = ((unsigned)(cc + 1 - clo) < (unsigned)(chi - clo)) ? pr1 : 0.f;
-                }
-                const float2 dd = __fadd2_rn(make_float2(__uint_as_float(dr[c + h]), __uint_as_float(dr[c + h + 1])),
-                                             make_float2(-dl_c[h], -dl_c[h + 1]));
-                const float2 ds = __fmul2_rn(__fmul2_rn(make_float2(pr0, pr1), dd), make_float2(p.scale, p.scale));
-                pr4[h] = pr0;
-                pr4[h + 1] = pr1;
-                ds4[h] = ds.x;
-                ds4[h + 1] = ds.y;
+            for (int h = 0; h < 4; h += 2) {
+              const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[c + h]), __uint_as_float(sr[c + h + 1])),
+                                          make_float2(sl2, sl2), make_float2(-lse_c[h], -lse_c[h + 1]));
+              float pr0 = ex2(x.x), pr1 = ex2(x.y);
+              if (MASKED) {
+                const int cc = 32 * half + c + h;
+                pr0 = ((unsigned)(cc - clo) < (unsigned)(chi - clo)) ? pr0 : 0.f;
+                pr1 = ((unsigned)(cc + 1 - clo) < (unsigned)(chi - clo)) ? pr1 : 0.f;
               }
-            } else {
+              pr[c + h] = pr0;
+              pr[c + h + 1] = pr1;
+            }
+          } else {
 #pragma unroll
             for (int h = 0; h < 4; ++h) {
               const int cc = 32 * half + c + h;
               const float raw = __uint_as_float(sr[c + h]);
-              float pr, t = 0.f;
+              float pv, t = 0.f;
               if (CAP || ALIBI) {
                 float x = logit2<CAP, SMALL>(raw, sl2, cap_in, cap_out, &t);
                 if (ALIBI) x += fmaxf(ba, fmaf(slope2, (float)cc, bq));
-                pr = ex2(x - lse_c[h]);
+                pv = ex2(x - lse_c[h]);
               } else {
-                pr = ex2(fmaf(raw, sl2, -lse_c[h]));
+                pv = ex2(fmaf(raw, sl2, -lse_c[h]));
               }
-              if (MASKED) pr = ((unsigned)(cc - clo) < (unsigned)(chi - clo)) ? pr : 0.f;
-              float ds = pr * (__uint_as_float(dr[c + h]) - dl_c[h]) * p.scale;
-              if (CAP) ds *= (1.f - t * t);
-              pr4[h] = pr;
+              if (MASKED) pv = ((unsigned)(cc - clo) < (unsigned)(chi - clo)) ? pv : 0.f;
+              pr[c + h] = pv;
+              if (CAP) tt[c + h] = t;
+            }
+          }
+          ppk[c / 2] = pack2<BF16>(pr[c], pr[c + 1]);
+          ppk[c / 2 + 1] = pack2<BF16>(pr[c + 2], pr[c + 3]);
+        }
+        // Pᵀ of half h -> packed columns [32h, 32h + 16) of the S buffer:
+        // inside this half's own fp32 columns, read above.
+        tmem_st16(tSb + 32 * half, ppk);
+        tmem_ld_wait();  // dPᵀ
+        uint32_t dpk[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 4) {
+          const float4 d4 = *reinterpret_cast<const float4*>(rowv + 64 + 32 * half + c);
+          const float dl_c[4] = {d4.x, d4.y, d4.z, d4.w};
+          float ds4[4];
+          if (!CAP && !ALIBI) {
+#pragma unroll
+            for (int h = 0; h < 4; h += 2) {
+              const float2 dd = __fadd2_rn(make_float2(__uint_as_float(dr[c + h]), __uint_as_float(dr[c + h + 1])),
+                                           make_float2(-dl_c[h], -dl_c[h + 1]));
+              const float2 ds = __fmul2_rn(__fmul2_rn(make_float2(pr[c + h], pr[c + h + 1]), dd),
+                                           make_float2(p.scale, p.scale));
+              ds4[h] = ds.x;
+              ds4[h + 1] = ds.y;
+            }
+          } else {
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              float ds = pr[c + h] * (__uint_as_float(dr[c + h]) - dl_c[h]) * p.scale;
+              if (CAP) ds *= (1.f - tt[c + h] * tt[c + h]);
               ds4[h] = ds;
             }
-            }
-            ppk[c / 2] = pack2<BF16>(pr4[0], pr4[1]);
-            ppk[c / 2 + 1] = pack2<BF16>(pr4[2], pr4[3]);
-            dpk[c / 2] = pack2<BF16>(ds4[0], ds4[1]);
-            dpk[c / 2 + 1] = pack2<BF16>(ds4[2], ds4[3]);
           }
-          // Pᵀ / dSᵀ of half h -> packed columns [32h, 32h + 16) of the
-          // buffer: inside this half's own fp32 columns, read above.
-          tmem_st16(tSb + 32 * half, ppk);
-          tmem_st16(tDb + 32 * half, dpk);
+          dpk[c / 2] = pack2<BF16>(ds4[0], ds4[1]);
+          dpk[c / 2 + 1] = pack2<BF16>(ds4[2], ds4[3]);
         }
+        tmem_st16(tDb + 32 * half, dpk);
       };
       if (small) {
         if (full) step(std::false_type{}, std::true_type{});
@@ -734,10 +775,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       p.delta[ridx] = dlt;
       p.lse2[ridx] = lse2;
     }
+    // Without documents tile_full's conditions are linear in the key tile's
+    // first key j0: the tile is fully kept exactly when j0 lies in
+    // [full_lo, full_hi] (no general tile test on the critical path).
+    const bool lin_full = p.doc_lo == nullptr;
+    int64_t full_lo = p.window > 0 ? (int64_t)q0 + kRows - 1 + p.q_off - p.k_off - p.window : 0;
+    int64_t full_hi = (int64_t)p.Sk - NK;
+    if (p.causal) full_hi = min(full_hi, (int64_t)q0 + p.q_off - p.k_off - (NK - 1));
+    if (q0 + kRows > p.Sq) full_hi = full_lo - 1;
     int jv = jt0 - 1;
     for (int i = 0; i < n_iter && ok; ++i) {
       jv = next_tile(jv);
       const int j0 = jv * NK;
+      const bool full = lin_full ? ((int64_t)j0 >= full_lo && (int64_t)j0 <= full_hi)
+                                 : tile_full(p, q0, q0 + kRows, j0, j0 + NK);
+      const float abase = ALIBI ? slope2 * (float)(g0 - (int64_t)j0 - p.k_off) : 0.f;
+      int clo = 0, chi = NK;  // kept key columns [clo, chi) of this query row (masked tiles)
+      if (!full) keys_for_query(p, gi, qi < p.Sq, j0, NK, &clo, &chi);
       uint32_t wbar = bar(kSPFull), wpar = (uint32_t)(i & 1);
       if ((p.debug_flags & BFA_DEBUG_INJECT_STALL) && i == 0) {
         wbar = bar(kNever);
@@ -755,10 +809,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kSRead));
-      const bool full = tile_full(p, q0, q0 + kRows, j0, j0 + NK);
-      const float abase = ALIBI ? slope2 * (float)(g0 - (int64_t)j0 - p.k_off) : 0.f;
-      int clo, chi;  // kept key columns [clo, chi) of this query row
-      keys_for_query(p, gi, qi < p.Sq, j0, NK, &clo, &chi);
       uint8_t* ds_row = smem + L::kOffDS + eg * (kRows * 128);  // this warpgroup's 64 keys
       const bool small = CAP && cap_small<64>(sr, cap_in);
       auto step = [&](auto masked, auto small_tag) {
@@ -891,7 +941,7 @@ int launch_bwd(const Params& p, int dtype, cudaStream_t st) {
     static std::once_flag once;
     static bool attr_ok = false;
     std::call_once(once, [&] { attr_ok = set_smem(kern, L::kSmemBytes); });
-    if (!attr_ok) return BFA_ERR_CUDA;
+    if (!attr_ok) return cuda_fail("dkdv_kernel shared-memory attribute", cudaSuccess);
     CUtensorMap m[6];
     if (!make_tmap_bhsd(&m[0], p.k, dtype, D, p.Sk, p.Hkv, p.B, p.sk_, kRows) ||
         !make_tmap_bhsd(&m[1], p.v, dtype, D, p.Sk, p.Hkv, p.B, p.sv_, kRows) ||
@@ -899,11 +949,11 @@ int launch_bwd(const Params& p, int dtype, cudaStream_t st) {
         !make_tmap_bhsd(&m[3], p.dout, dtype, D, p.Sq, p.Hq, p.B, p.sdo_, kInner) ||
         !make_tmap_bhsd(&m[4], p.dk, gdt, D, p.Sk, p.Hkv, p.B, p.sdk_, kRows) ||
         !make_tmap_bhsd(&m[5], p.dv, gdt, D, p.Sk, p.Hkv, p.B, p.sdv_, kRows))
-      return BFA_ERR_CUDA;
+      return BFA_ERR_CUDA;  // make_tmap_bhsd recorded the detail
     const unsigned grid = (unsigned)((p.Sk + kRows - 1) / kRows) * p.Hkv * p.B;
     kern<<<grid, kThreads, L::kSmemBytes, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], p);
     note_launch();
-    return cudaGetLastError() == cudaSuccess ? BFA_OK : BFA_ERR_CUDA;
+    return launch_status("dkdv_kernel launch");
   };
   auto run_dq = [&]() -> int {
     using L = DqLayout<D>;
@@ -911,24 +961,25 @@ int launch_bwd(const Params& p, int dtype, cudaStream_t st) {
     static std::once_flag once;
     static bool attr_ok = false;
     std::call_once(once, [&] { attr_ok = set_smem(kern, L::kSmemBytes); });
-    if (!attr_ok) return BFA_ERR_CUDA;
+    if (!attr_ok) return cuda_fail("dq_kernel shared-memory attribute", cudaSuccess);
     CUtensorMap m[6];
     if (!make_tmap_bhsd(&m[0], p.q, dtype, D, p.Sq, p.Hq, p.B, p.sq_, kRows) ||
         !make_tmap_bhsd(&m[1], p.dout, dtype, D, p.Sq, p.Hq, p.B, p.sdo_, kRows) ||
         !make_tmap_bhsd(&m[2], p.k, dtype, D, p.Sk, p.Hkv, p.B, p.sk_, L::kKeys) ||
         !make_tmap_bhsd(&m[3], p.v, dtype, D, p.Sk, p.Hkv, p.B, p.sv_, L::kKeys) ||
         !make_tmap_bhsd(&m[4], p.dq, gdt, D, p.Sq, p.Hq, p.B, p.sdq_, kRows))
-      return BFA_ERR_CUDA;
+      return BFA_ERR_CUDA;  // make_tmap_bhsd recorded the detail
     // O (fused Δ only; otherwise a copy of the Q map that is never read).
     if (p.fuse_delta) {
-      if (!make_tmap_bhsd(&m[5], p.o, dtype, D, p.Sq, p.Hq, p.B, p.so_, kRows)) return BFA_ERR_CUDA;
+      if (!make_tmap_bhsd(&m[5], p.o, dtype, D, p.Sq, p.Hq, p.B, p.so_, kRows))
+        return BFA_ERR_CUDA;  // make_tmap_bhsd recorded the detail
     } else {
       m[5] = m[0];
     }
     const unsigned grid = (unsigned)((p.Sq + kRows - 1) / kRows) * p.Hq * p.B;
     kern<<<grid, kThreads, L::kSmemBytes, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], p);
     note_launch();
-    return cudaGetLastError() == cudaSuccess ? BFA_OK : BFA_ERR_CUDA;
+    return launch_status("dq_kernel launch");
   };
   // With a fused Δ the dQ kernel writes the row statistics dK/dV reads, so
   // it runs first.

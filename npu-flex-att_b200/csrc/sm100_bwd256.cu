@@ -808,7 +808,7 @@ int launch_kv(const Params& p, int dtype, cudaStream_t st) {
   static std::once_flag once;
   static bool attr_ok = false;
   std::call_once(once, [&] { attr_ok = set_smem(kern, L::kSmemBytes); });
-  if (!attr_ok) return BFA_ERR_CUDA;
+  if (!attr_ok) return cuda_fail("dkdv256_kernel shared-memory attribute", cudaSuccess);
   CUtensorMap m[5];
   const bool dk = MODE == kModeDK;
   if (!make_tmap_bhsd(&m[0], p.k, dtype, kD, p.Sk, p.Hkv, p.B, p.sk_, kRows) ||
@@ -816,11 +816,11 @@ int launch_kv(const Params& p, int dtype, cudaStream_t st) {
       !make_tmap_bhsd(&m[2], p.q, dtype, kD, p.Sq, p.Hq, p.B, p.sq_, kInner) ||
       !make_tmap_bhsd(&m[3], p.dout, dtype, kD, p.Sq, p.Hq, p.B, p.sdo_, kInner) ||
       !make_tmap_bhsd(&m[4], dk ? p.dk : p.dv, gdt, kD, p.Sk, p.Hkv, p.B, dk ? p.sdk_ : p.sdv_, kRows))
-    return BFA_ERR_CUDA;
+    return BFA_ERR_CUDA;  // make_tmap_bhsd recorded the detail
   const unsigned grid = (unsigned)((p.Sk + kRows - 1) / kRows) * p.Hkv * p.B;
   kern<<<grid, kThreads, L::kSmemBytes, st>>>(m[0], m[1], m[2], m[3], m[4], p);
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? BFA_OK : BFA_ERR_CUDA;
+  return launch_status("dkdv256_kernel launch");
 }
 
 template <bool BF16, bool CAP, bool ALIBI>
@@ -838,18 +838,18 @@ int launch_bwd(const Params& p, int dtype, cudaStream_t st) {
     static std::once_flag once;
     static bool attr_ok = false;
     std::call_once(once, [&] { attr_ok = set_smem(kern, L::kSmemBytes); });
-    if (!attr_ok) return BFA_ERR_CUDA;
+    if (!attr_ok) return cuda_fail("dq256_kernel shared-memory attribute", cudaSuccess);
     CUtensorMap m[5];
     if (!make_tmap_bhsd(&m[0], p.q, dtype, kD, p.Sq, p.Hq, p.B, p.sq_, kRows) ||
         !make_tmap_bhsd(&m[1], p.dout, dtype, kD, p.Sq, p.Hq, p.B, p.sdo_, kRows) ||
         !make_tmap_bhsd(&m[2], p.k, dtype, kD, p.Sk, p.Hkv, p.B, p.sk_, L::kKeys) ||
         !make_tmap_bhsd(&m[3], p.v, dtype, kD, p.Sk, p.Hkv, p.B, p.sv_, L::kKeys) ||
         !make_tmap_bhsd(&m[4], p.dq, gdt, kD, p.Sq, p.Hq, p.B, p.sdq_, kRows))
-      return BFA_ERR_CUDA;
+      return BFA_ERR_CUDA;  // make_tmap_bhsd recorded the detail
     const unsigned grid = (unsigned)((p.Sq + kRows - 1) / kRows) * p.Hq * p.B;
     kern<<<grid, kThreads, L::kSmemBytes, st>>>(m[0], m[1], m[2], m[3], m[4], p);
     note_launch();
-    if (cudaGetLastError() != cudaSuccess) return BFA_ERR_CUDA;
+    if (int rc = launch_status("dq256_kernel launch")) return rc;
   }
   return BFA_OK;
 }

@@ -286,12 +286,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tr0 = q0 + t * kBM;
     float m = neg_inf(), l = 0.f;
     bool ok = true;
+    // Without documents tile_full's conditions are linear in the key tile's
+    // first key c0: the tile is fully kept exactly when c0 lies in
+    // [full_lo, full_hi] (no general tile test per step).
+    const bool lin_full = p.doc_lo == nullptr;
+    int64_t full_lo = p.window > 0 ? (int64_t)tr0 + kBM - 1 + p.q_off - p.k_off - p.window : 0;
+    int64_t full_hi = (int64_t)p.Sk - kBN;
+    if (p.causal) full_hi = min(full_hi, (int64_t)tr0 + p.q_off - p.k_off - (kBN - 1));
+    if (tr0 + kBM > p.Sq) full_hi = full_lo - 1;
 
     int jt = jlo - 1;
     for (int it = 0; it < n_iter; ++it) {
       jt = next_tile(jt);
       const int c0 = jt * kBN;
       const bool blk_on = !BLK || ((t == 0 || two_tiles) && block_on(p, b, hq, qb0 + t, jt));  // this query tile's block
+      // The whole 128-column S row comes into registers with four TMEM loads
+      // and one wait: one TMEM round trip per step instead of one per
+      // 32-column chunk and pass. Logits in base 2 (cap, ALiBi, mask) are
+      // formed in place; a plain, fully kept tile only needs max(S) (the
+      // scale is > 0) and folds the scale into the exponent with one FMA.
+      // Four independent max accumulators (three-input max) and two packed
+      // sum accumulators break the dependency chains. The step's mask
+      // constants come first: they overlap the wait for S.
+      const bool full = blk_on && (lin_full ? ((int64_t)c0 >= full_lo && (int64_t)c0 <= full_hi)
+                                            : tile_full(p, tr0, tr0 + kBM, c0, c0 + kBN));
+      const bool store_x = CAP || ALIBI || !full || !(sl2 > 0.f);  // x != S * sl2
+      const float abase = ALIBI ? slope2 * (float)(g0 - (int64_t)c0 - p.k_off) : 0.f;
+      int clo = 0, chi = kBN;  // kept key columns [clo, chi) of this row (all of them on a full tile)
+      if (!full) keys_for_query(p, gi, r_local < p.Sq && blk_on, c0, kBN, &clo, &chi);
       uint32_t wbar = bar(kSFull + t), wpar = (uint32_t)(it & 1);
       if ((p.debug_flags & BFA_DEBUG_INJECT_STALL) && t == 0 && it == 0) {
         wbar = bar(kNever);
@@ -299,23 +321,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!(ok = warp_wait(wbar, wpar, ctl))) break;
       tc_fence_after();
-
-      // The whole 128-column S row comes into registers with four TMEM loads
-      // and one wait: one TMEM round trip per step instead of one per
-      // 32-column chunk and pass. Logits in base 2 (cap, ALiBi, mask) are
-      // formed in place; a plain, fully kept tile only needs max(S) (the
-      // scale is > 0) and folds the scale into the exponent with one FMA.
-      // Four independent max accumulators (three-input max) and two packed
-      // sum accumulators break the dependency chains.
-      const bool full = blk_on && tile_full(p, tr0, tr0 + kBM, c0, c0 + kBN);
-      const bool store_x = CAP || ALIBI || !full || !(sl2 > 0.f);  // x != S * sl2
-      const float abase = ALIBI ? slope2 * (float)(g0 - (int64_t)c0 - p.k_off) : 0.f;
-      int clo, chi;  // kept key columns [clo, chi) of this row (all of them on a full tile)
-      keys_for_query(p, gi, r_local < p.Sq && blk_on, c0, kBN, &clo, &chi);
-      if (full) {
-        clo = 0;
-        chi = kBN;
-      }
       uint32_t r[kBN / 32][32];
 #pragma unroll
       for (int ch = 0; ch < kBN / 32; ++ch) tmem_ld32(tS + 32 * ch, r[ch]);
@@ -494,12 +499,12 @@ int launch_fwd(const Params& p, const Tmaps4& tm, cudaStream_t st) {
     attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)L::kSmemBytes);
   });
-  if (attr_err != cudaSuccess) return BFA_ERR_CUDA;
+  if (attr_err != cudaSuccess) return cuda_fail("fwd_kernel shared-memory attribute", attr_err);
   const int n_mblk = (p.Sq + 2 * kBM - 1) / (2 * kBM);
   const unsigned grid = (unsigned)n_mblk * (unsigned)p.B * (unsigned)p.Hq;
   kern<<<grid, kThreads, L::kSmemBytes, st>>>(tm.m[0], tm.m[1], tm.m[2], tm.m[3], p);
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? BFA_OK : BFA_ERR_CUDA;
+  return launch_status("fwd_kernel launch");
 }
 
 template <int D, bool BF16, bool BLK>

@@ -517,12 +517,12 @@ int launch(const Params& p, const Tmaps4& tm, cudaStream_t st) {
   std::call_once(once, [&] {
     attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
   });
-  if (attr_err != cudaSuccess) return BFA_ERR_CUDA;
+  if (attr_err != cudaSuccess) return cuda_fail("fwd256_kernel shared-memory attribute", attr_err);
   const int n_qt = (p.Sq + kBM - 1) / kBM;
   const unsigned grid = (unsigned)n_qt * (unsigned)p.B * (unsigned)p.Hq;
   kern<<<grid, kThreads, kSmemBytes, st>>>(tm.m[0], tm.m[1], tm.m[2], tm.m[3], p);
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? BFA_OK : BFA_ERR_CUDA;
+  return launch_status("fwd256_kernel launch");
 }
 
 template <bool BF16>

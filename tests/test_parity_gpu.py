@@ -243,6 +243,36 @@ def test_autograd_through_flex_attention():
     assert _err(qd.grad, dq) < 2e-2 and _err(kd.grad, dk) < 2e-2 and _err(vd.grad, dv) < 2e-2
 
 
+def test_calls_from_a_fresh_thread():
+    """A thread whose first CUDA work is this library's (as PyTorch's autograd
+    device threads can be, when every tensor they touch comes from the caching
+    allocator) still gets the device context the tensor-map encoder needs, and
+    the same results bit for bit."""
+    import threading
+    q, k, v, go = (t.to(DEV) for t in _inputs(9, 1, 4, 2, 256, 256, 128, torch.bfloat16))
+    o, l = nfa.npu_flash_attention_forward(q, k, v, causal=True, return_lse=True)
+    g = nfa.npu_flash_attention_backward(q, k, v, o, l, go, causal=True)
+    torch.cuda.synchronize()
+    out = {}
+
+    def work():
+        try:
+            o2, l2 = nfa.npu_flash_attention_forward(q, k, v, causal=True, return_lse=True)
+            out["g"] = nfa.npu_flash_attention_backward(q, k, v, o2, l2, go, causal=True)
+            out["o"] = o2
+            torch.cuda.synchronize()
+        except Exception as e:  # reported below, on the test's thread
+            out["err"] = e
+
+    th = threading.Thread(target=work)
+    th.start()
+    th.join()
+    assert "err" not in out, out.get("err")
+    assert torch.equal(out["o"], o)
+    for a, b in zip(out["g"], g):
+        assert torch.equal(a, b)
+
+
 def test_cross_dtype_agreement():
     """S01-S03: fp32, fp16 and bf16 runs of the same data agree within 0.1."""
     q, k, v, _ = _inputs(0, 1, 2, 2, 128, 128, 64, torch.float32)
