@@ -544,7 +544,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     kDSFree = kOpsReady + 1,  // MMA -> elementwise: dQ(i) has read the dS tile
     kAccDone = kDSFree + 1,
     kDrain = kAccDone + 1,
-    kNever = kDrain + 1,
+    kDrainSP = kDrain + 1,
+    kNever = kDrainSP + 1,
     kNumBars = kNever + 1
   };
 
@@ -634,64 +635,66 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = (n > NS ? n - NS : 0); i < n; ++i)
         drain_wait(bar(kKVFull + i % NS), (i / NS) & 1, p.timeout_ns);
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || warp == 3) {
+    // Two threads issue the MMAs: warp 1 S(i+1) and dP(i+1), warp 3 dQ(i). A
+    // thread whose MMA queue is full blocks at its next issue, so with one
+    // issuer dQ(i) reached the tensor pipe several hundred cycles after dS(i)
+    // was ready. The stage's K/V is released after dQ(i), which is issued
+    // after the elementwise step that waited for S(i) and dP(i).
     if (lane == 0) {
-      constexpr uint32_t idSP = idesc_f16(kRows, NK, BF16, false);
-      constexpr uint32_t idAcc = idesc_f16(kRows, D, BF16, true);
       auto stage = [&](int i) -> uint32_t { return sbase + L::stage_off(i % NS); };
-      auto issue_s = [&](int i) {
-        const uint64_t dk = desc_kmajor(stage(i));
+      if (warp == 1) {
+        constexpr uint32_t idSP = idesc_f16(kRows, NK, BF16, false);
+        auto issue_s = [&](int i) {
+          const uint64_t dk = desc_kmajor(stage(i));
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t offk = ((kk >> 2) * (NK * 128) + (kk & 3) * 32) >> 4;
-          mma_ts(tmem + L::kTmemS, tmem + L::kTmemQ + 8 * kk, dk + offk, idSP, kk > 0 ? 1u : 0u);
-        }
-      };
-      auto issue_dp = [&](int i) {
-        const uint64_t dv = desc_kmajor(stage(i) + L::kKVBytes);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t offk = ((kk >> 2) * (NK * 128) + (kk & 3) * 32) >> 4;
+            mma_ts(tmem + L::kTmemS, tmem + L::kTmemQ + 8 * kk, dk + offk, idSP, kk > 0 ? 1u : 0u);
+          }
+        };
+        auto issue_dp = [&](int i) {
+          const uint64_t dv = desc_kmajor(stage(i) + L::kKVBytes);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t offk = ((kk >> 2) * (NK * 128) + (kk & 3) * 32) >> 4;
-          mma_ts(tmem + L::kTmemDP, tmem + L::kTmemDO + 8 * kk, dv + offk, idSP, kk > 0 ? 1u : 0u);
-        }
-        mma_commit(bar(kSPFull));
-      };
-      bool ok = n_iter == 0 || mbar_wait(bar(kOpsReady), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
-      if (ok && n_iter > 0) {
-        ok = mbar_wait(bar(kKVFull), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
-        if (ok) {
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t offk = ((kk >> 2) * (NK * 128) + (kk & 3) * 32) >> 4;
+            mma_ts(tmem + L::kTmemDP, tmem + L::kTmemDO + 8 * kk, dv + offk, idSP, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(bar(kSPFull));
+        };
+        bool ok = n_iter == 0 || mbar_wait(bar(kOpsReady), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
+        for (int i = 0; i < n_iter && ok; ++i) {
+          if (!(ok = mbar_wait(bar(kKVFull + i % NS), (i / NS) & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
+          // S(i) / dP(i) overwrite the TMEM the elementwise warps read for step i - 1.
+          if (i > 0 && !(ok = mbar_wait(bar(kSRead), (i - 1) & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
           tc_fence_after();
-          issue_s(0);
-          issue_dp(0);
+          issue_s(i);
+          if (i > 0 && !(ok = mbar_wait(bar(kDPRead), (i - 1) & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
+          tc_fence_after();
+          issue_dp(i);
         }
+        mma_commit(bar(kDrainSP));
+        drain_wait(bar(kDrainSP), 0, p.timeout_ns);
+      } else {
+        constexpr uint32_t idAcc = idesc_f16(kRows, D, BF16, true);
+        const uint64_t dS0 = desc_kmajor(sbase + L::kOffDS);
+        bool ok = true;
+        for (int i = 0; i < n_iter && ok; ++i) {
+          if (!(ok = mbar_wait(bar(kDSFull), i & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
+          tc_fence_after();
+          const uint64_t mk = desc_mnmajor(stage(i), NK * 128);
+#pragma unroll
+          for (int kk = 0; kk < NK / 16; ++kk) {
+            const uint32_t offs = ((kk >> 2) * (kRows * 128) + (kk & 3) * 32) >> 4;
+            mma_ss(tmem + L::kTmemDQ, dS0 + offs, mk + ((kk * 2048) >> 4), idAcc, (i > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(bar(kKVEmpty + i % NS));
+          mma_commit(bar(kDSFree));
+        }
+        mma_commit(bar(kAccDone));
+        mma_commit(bar(kDrain));
+        drain_wait(bar(kDrain), 0, p.timeout_ns);
       }
-      const uint64_t dS0 = desc_kmajor(sbase + L::kOffDS);
-      for (int i = 0; i < n_iter && ok; ++i) {
-        const int n1 = i + 1;
-        if (n1 < n_iter) {
-          if (!(ok = mbar_wait(bar(kKVFull + n1 % NS), (n1 / NS) & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
-          if (!(ok = mbar_wait(bar(kSRead), i & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
-          tc_fence_after();
-          issue_s(n1);
-          if (!(ok = mbar_wait(bar(kDPRead), i & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
-          tc_fence_after();
-          issue_dp(n1);
-        }
-        if (!(ok = mbar_wait(bar(kDSFull), i & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
-        tc_fence_after();
-        const uint64_t mk = desc_mnmajor(stage(i), NK * 128);
-#pragma unroll
-        for (int kk = 0; kk < NK / 16; ++kk) {
-          const uint32_t offs = ((kk >> 2) * (kRows * 128) + (kk & 3) * 32) >> 4;
-          mma_ss(tmem + L::kTmemDQ, dS0 + offs, mk + ((kk * 2048) >> 4), idAcc,
-                 (i > 0 || kk > 0) ? 1u : 0u);
-        }
-        mma_commit(bar(kKVEmpty + i % NS));
-        mma_commit(bar(kDSFree));
-      }
-      mma_commit(bar(kAccDone));
-      mma_commit(bar(kDrain));
-      drain_wait(bar(kDrain), 0, p.timeout_ns);
     }
   } else if (warp >= 4) {
     // Both warpgroups work on every step: warpgroup h takes key columns
