@@ -104,6 +104,39 @@ __device__ __forceinline__ StepWalker<Next> make_walker(Next n, int start) {
   return StepWalker<Next>(n, start);
 }
 
+// Without documents, whether a tile is fully kept is linear in its moving
+// coordinate: a kernel that walks key tiles for fixed query rows (or query
+// tiles for fixed keys) finds the kept range once and tests each step with
+// two compares instead of the general tile test.
+struct KeptRange {
+  int64_t lo, hi;
+  __device__ __forceinline__ bool has(int64_t x) const { return x >= lo && x <= hi; }
+};
+
+// Key tiles [c, c + nk) against fixed query rows [r0, r0 + nr) (local
+// indices): every pair is kept for c in the range (causal: the tile's last
+// key is at or before the first row; window: the last row minus the first
+// key is at most W; the tile lies inside Sk; with rows_in, the rows inside Sq).
+__device__ __forceinline__ KeptRange kept_keys(const Params& p, int r0, int nr, int nk, bool rows_in) {
+  KeptRange k;
+  k.lo = p.window > 0 ? (int64_t)r0 + nr - 1 + p.q_off - p.k_off - p.window : 0;
+  k.hi = (int64_t)p.Sk - nk;
+  if (p.causal) k.hi = min(k.hi, (int64_t)r0 + p.q_off - p.k_off - (nk - 1));
+  if (rows_in && r0 + nr > p.Sq) k.hi = k.lo - 1;
+  return k;
+}
+
+// Query tiles [q, q + nq) against fixed keys [c0, c0 + nk): the same
+// conditions, with the rows inside Sq and the keys inside Sk.
+__device__ __forceinline__ KeptRange kept_queries(const Params& p, int c0, int nk, int nq) {
+  KeptRange k;
+  k.lo = p.causal ? (int64_t)c0 + nk - 1 + p.k_off - p.q_off : -((int64_t)1 << 40);
+  k.hi = (int64_t)p.Sq - nq;
+  if (p.window > 0) k.hi = min(k.hi, (int64_t)p.window + c0 + p.k_off - p.q_off - (nq - 1));
+  if (c0 + nk > p.Sk) k.hi = k.lo - 1;
+  return k;
+}
+
 // keep_pair plus the block-sparse mask of (b, hq); positions absolute.
 __device__ __forceinline__ bool keep_elem(const Params& p, int b, int hq, int64_t gi, int64_t gj) {
   return keep_pair(p, gi, gj) &&

@@ -275,15 +275,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // (a step's setup is a serial chain on the elementwise warps' critical
     // path): the q-head offset hs and query-tile index ts advance
     // incrementally (a division only under a block-sparse mask, whose walk
-    // skips steps), and without documents tile_full's conditions are linear
-    // in the step's first query q0: the step is fully kept exactly when q0
-    // lies in [full_lo, full_hi].
+    // skips steps), and without documents the step is fully kept exactly
+    // when its first query lies in `kept`.
     int hs = 0, ts = -1;
     const bool lin_full = p.doc_lo == nullptr;
-    int64_t full_lo = p.causal ? (int64_t)c0 + kRows - 1 + p.k_off - p.q_off : -((int64_t)1 << 40);
-    int64_t full_hi = (int64_t)p.Sq - kInner;
-    if (p.window > 0) full_hi = min(full_hi, (int64_t)p.window + c0 + p.k_off - p.q_off - (kInner - 1));
-    if (c0 + kRows > p.Sk) full_hi = full_lo - 1;
+    const KeptRange kept = kept_queries(p, c0, kRows, kInner);
     int sv = -1;
     for (int i = 0; i < n_iter; ++i) {
       const int bf = i & 1, k = i >> 1, st = i % NS;
@@ -301,8 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tSb = tmem + lane_base + L::kTmemS + 64 * bf;
       const uint32_t tDb = tmem + lane_base + L::kTmemDP + 64 * bf;
       const float* rowv = (const float*)(smem + L::kOffRow + st * 512);
-      const bool full = lin_full ? ((int64_t)q0 >= full_lo && (int64_t)q0 <= full_hi)
-                                 : tile_full(p, q0, q0 + kInner, c0, c0 + kRows);
+      const bool full = lin_full ? kept.has(q0) : tile_full(p, q0, q0 + kInner, c0, c0 + kRows);
       const float slope = ALIBI ? p.alibi[hq] : 0.f;
       const float slope2 = slope * kLog2e;
       // ALiBi bias slope·(g0_i - j) (alibi_ref): with slope > 0, g0_i =
@@ -778,20 +773,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       p.delta[ridx] = dlt;
       p.lse2[ridx] = lse2;
     }
-    // Without documents tile_full's conditions are linear in the key tile's
-    // first key j0: the tile is fully kept exactly when j0 lies in
-    // [full_lo, full_hi] (no general tile test on the critical path).
+    // Without documents a key tile is fully kept exactly when its first key
+    // lies in `kept` (no general tile test on the critical path).
     const bool lin_full = p.doc_lo == nullptr;
-    int64_t full_lo = p.window > 0 ? (int64_t)q0 + kRows - 1 + p.q_off - p.k_off - p.window : 0;
-    int64_t full_hi = (int64_t)p.Sk - NK;
-    if (p.causal) full_hi = min(full_hi, (int64_t)q0 + p.q_off - p.k_off - (NK - 1));
-    if (q0 + kRows > p.Sq) full_hi = full_lo - 1;
+    const KeptRange kept = kept_keys(p, q0, kRows, NK, true);
     int jv = jt0 - 1;
     for (int i = 0; i < n_iter && ok; ++i) {
       jv = next_tile(jv);
       const int j0 = jv * NK;
-      const bool full = lin_full ? ((int64_t)j0 >= full_lo && (int64_t)j0 <= full_hi)
-                                 : tile_full(p, q0, q0 + kRows, j0, j0 + NK);
+      const bool full = lin_full ? kept.has(j0) : tile_full(p, q0, q0 + kRows, j0, j0 + NK);
       const float abase = ALIBI ? slope2 * (float)(g0 - (int64_t)j0 - p.k_off) : 0.f;
       int clo = 0, chi = NK;  // kept key columns [clo, chi) of this query row (masked tiles)
       if (!full) keys_for_query(p, gi, qi < p.Sq, j0, NK, &clo, &chi);

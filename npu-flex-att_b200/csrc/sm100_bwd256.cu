@@ -330,6 +330,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float cap_in = CAP ? p.scale / p.soft_cap : 0.f;
     const float cap_out = CAP ? p.soft_cap * kLog2e : 0.f;
     bool ok = true;
+    // Without documents a step is fully kept exactly when its first query
+    // lies in `kept` (no general tile test per step).
+    const bool lin_full = p.doc_lo == nullptr;
+    const KeptRange kept = kept_queries(p, c0, kRows, kInner);
     int sv = -1;
     for (int i = 0; i < n_iter; ++i) {
       const int bf = i & 1, e = i % NR;
@@ -346,7 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tSb = tmem + lane_base + L::kTmemS + 64 * bf + 32 * eg;
       const uint32_t tDb = tmem + lane_base + L::kTmemDP + 64 * bf + 32 * eg;
       const float* rowv = (const float*)(smem + L::kOffRow + e * L::kRowBytes);
-      const bool full = tile_full(p, q0, q0 + kInner, c0, c0 + kRows);
+      const bool full = lin_full ? kept.has(q0) : tile_full(p, q0, q0 + kInner, c0, c0 + kRows);
       const float slope = ALIBI ? p.alibi[hq] : 0.f;
       const float slope2 = slope * kLog2e;
       // ALiBi bias slope·(g0_i - j) (alibi_ref): with slope > 0, g0_i =
@@ -360,8 +364,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                        : !shifted ? slope2 * (float)((int64_t)q0 + p.q_off - gj)
                        : p.window > 0 ? slope2 * (float)((int64_t)q0 + p.q_off - p.window - gj)
                                       : neg_inf();
-      int clo, chi;  // kept query columns [clo, chi) of this key row
-      queries_for_key(p, gj, kj < p.Sk, q0, kInner, &clo, &chi);
+      int clo = 0, chi = kInner;  // kept query columns [clo, chi) of this key row (masked steps)
+      if (!full) queries_for_key(p, gj, kj < p.Sk, q0, kInner, &clo, &chi);
       uint32_t sr[32], dr[32];
       tmem_ld32(tSb, sr);
       if (DK) tmem_ld32(tDb, dr);
@@ -687,6 +691,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     uint8_t* ds_base = smem + L::kOffDS;
+    // Without documents a key step is fully kept exactly when its first key
+    // lies in `kept` (no general tile test per step).
+    const bool lin_full = p.doc_lo == nullptr;
+    const KeptRange kept = kept_keys(p, q0, kRows, NK, true);
     int jv = jt0 - 1;
     for (int j = 0; j < n_iter && ok; ++j) {
       jv = next_tile(jv);
@@ -709,10 +717,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kDPRead));
-      const bool full = tile_full(p, q0, q0 + kRows, j0, j0 + NK);
+      const bool full = lin_full ? kept.has(j0) : tile_full(p, q0, q0 + kRows, j0, j0 + NK);
       const float abase = ALIBI ? slope2 * (float)(g0 - (int64_t)j0 - p.k_off) : 0.f;
-      int clo, chi;  // kept key columns [clo, chi) of this query row
-      keys_for_query(p, gi, qi < p.Sq, j0, NK, &clo, &chi);
+      int clo = 0, chi = NK;  // kept key columns [clo, chi) of this query row (masked steps)
+      if (!full) keys_for_query(p, gi, qi < p.Sq, j0, NK, &clo, &chi);
       uint32_t dpk[16];
       auto body = [&](auto masked, auto small_tag) {
         constexpr bool MASKED = decltype(masked)::value;

@@ -286,14 +286,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tr0 = q0 + t * kBM;
     float m = neg_inf(), l = 0.f;
     bool ok = true;
-    // Without documents tile_full's conditions are linear in the key tile's
-    // first key c0: the tile is fully kept exactly when c0 lies in
-    // [full_lo, full_hi] (no general tile test per step).
+    // Without documents a key tile is fully kept exactly when its first key
+    // lies in `kept` (no general tile test per step). Rows past Sq may share
+    // a full tile: their results are not stored.
     const bool lin_full = p.doc_lo == nullptr;
-    int64_t full_lo = p.window > 0 ? (int64_t)tr0 + kBM - 1 + p.q_off - p.k_off - p.window : 0;
-    int64_t full_hi = (int64_t)p.Sk - kBN;
-    if (p.causal) full_hi = min(full_hi, (int64_t)tr0 + p.q_off - p.k_off - (kBN - 1));
-    if (tr0 + kBM > p.Sq) full_hi = full_lo - 1;
+    const KeptRange kept = kept_keys(p, tr0, kBM, kBN, false);
 
     int jt = jlo - 1;
     for (int it = 0; it < n_iter; ++it) {
@@ -308,8 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Four independent max accumulators (three-input max) and two packed
       // sum accumulators break the dependency chains. The step's mask
       // constants come first: they overlap the wait for S.
-      const bool full = blk_on && (lin_full ? ((int64_t)c0 >= full_lo && (int64_t)c0 <= full_hi)
-                                            : tile_full(p, tr0, tr0 + kBM, c0, c0 + kBN));
+      const bool full = blk_on && (lin_full ? kept.has(c0) : tile_full(p, tr0, tr0 + kBM, c0, c0 + kBN));
       const bool store_x = CAP || ALIBI || !full || !(sl2 > 0.f);  // x != S * sl2
       const float abase = ALIBI ? slope2 * (float)(g0 - (int64_t)c0 - p.k_off) : 0.f;
       int clo = 0, chi = kBN;  // kept key columns [clo, chi) of this row (all of them on a full tile)

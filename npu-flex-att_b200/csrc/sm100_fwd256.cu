@@ -288,6 +288,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 c4 = cap_out * kT4, c5 = cap_out * kT5;
     float m = neg_inf(), l = 0.f;
     bool ok = true;
+    // Without documents a key tile is fully kept exactly when its first key
+    // lies in `kept` (no general tile test per step). Rows past Sq may share
+    // a full tile: their results are not stored.
+    const bool lin_full = p.doc_lo == nullptr;
+    const KeptRange kept = kept_keys(p, q0, kBM, kBN, false);
 
     int jt = jlo - 1;
     for (int it = 0; it < n_iter; ++it) {
@@ -303,15 +308,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!(ok = warp_wait(wbar, wpar, ctl))) break;
       tc_fence_after();
 
-      const bool full = tile_full(p, q0, q0 + kBM, c0k, c0k + kBN);
+      const bool full = lin_full ? kept.has(c0k) : tile_full(p, q0, q0 + kBM, c0k, c0k + kBN);
       const bool store_x = CAP || ALIBI || !full || !(sl2 > 0.f);  // x != S * sl2
       const float abase = ALIBI ? slope2 * (float)(g0 - (int64_t)c0k - p.k_off) : 0.f;
-      int clo, chi;  // kept key columns [clo, chi) of this row
-      keys_for_query(p, gi, r_local < p.Sq, c0k, kBN, &clo, &chi);
-      if (full) {
-        clo = 0;
-        chi = kBN;
-      }
+      int clo = 0, chi = kBN;  // kept key columns [clo, chi) of this row (all of them on a full tile)
+      if (!full) keys_for_query(p, gi, r_local < p.Sq, c0k, kBN, &clo, &chi);
       uint32_t r[2][32];  // this warpgroup's keys [64h, 64h + 64)
       tmem_ld32(tS + 64 * eg, r[0]);
       tmem_ld32(tS + 64 * eg + 32, r[1]);
