@@ -10,7 +10,7 @@ kernel is timed on its own). FLOPs count only unmasked (i, j) pairs,
 element-exact: 4·D per pair forward, 10·D backward.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload c3|c2|c4|c4t|c5|c5u|decode]
+                  [--workload c3|c2|c4|c4t|c5|c5u|decode|fp32]
 
 N > 1 is launched with torchrun (one process per GPU); each rank runs its own
 batch shard (weak scaling, no collective on the data path); the step time is
@@ -634,6 +634,70 @@ def run_c2(args):
         "note": "latency-bound configuration; auxiliary to the c3 headline line"}), flush=True)
 
 
+FP32_CASES = [  # (B, Hq, Hkv, S, D): c1 itself, then larger fp32 problems
+    (1, 2, 2, 128, 64),
+    (1, 8, 2, 2048, 64),
+    (1, 8, 2, 2048, 128),
+]
+
+
+def run_fp32(args):
+    """fp32 inputs (config 1 and larger causal fp32 problems). fp32 runs on the
+    CUDA-core kernels (simt_attention.cu): the tcgen05 kernels take 16-bit
+    operands only. Timed per call like c2: forward and backward separately,
+    CUDA events, L2 flushed before every call, median over the reps."""
+    import bfa_lib
+    import npu_flash_attention as nfa
+    _, _, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    lib = bfa_lib.load()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    reps = max(args.steps, 10)
+    cases, launches = [], 0
+    for (B, Hq, Hkv, S, D) in FP32_CASES:
+        g = torch.Generator(device=dev).manual_seed(S + D)
+        q, do = (torch.randn(B, Hq, S, D, generator=g, device=dev) for _ in range(2))
+        k, v = (torch.randn(B, Hkv, S, D, generator=g, device=dev) for _ in range(2))
+        f_ms, b_ms = [], []
+        for i in range(args.warmup + reps):
+            flush.fill_(i & 255)
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            n0 = lib.bfa_launch_count()
+            e[0].record()
+            o, lse = nfa.npu_flash_attention_forward(q, k, v, causal=True, return_lse=True)
+            e[1].record()
+            flush.fill_((i + 1) & 255)
+            e[2].record()
+            nfa.npu_flash_attention_backward(q, k, v, o, lse, do, causal=True)
+            e[3].record()
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                f_ms.append(e[0].elapsed_time(e[1]))
+                b_ms.append(e[2].elapsed_time(e[3]))
+                launches += lib.bfa_launch_count() - n0
+        nfa.check_device_status(dev)
+        fm, bm = statistics.median(f_ms), statistics.median(b_ms)
+        pairs = pairs_per_head(dict(S=S, causal=True)) * B * Hq
+        cases.append({"B": B, "Hq": Hq, "Hkv": Hkv, "S": S, "D": D, "fwd_ms": round(fm, 4),
+                      "bwd_ms": round(bm, 4),
+                      "fwd_bwd_tflops": round(14.0 * D * pairs / ((fm + bm) * 1e-3) / 1e12, 3)})
+    head = cases[-1]
+    print(json.dumps({
+        "metric": METRIC, "value": head["fwd_bwd_tflops"], "unit": "TFLOPS", "n_gpus": 1,
+        "value_is": "fwd+bwd TFLOPS of the largest fp32 case (sum of its median fwd and bwd latencies)",
+        "steps": reps, "warmup": args.warmup, "ms_per_step": round(head["fwd_ms"] + head["bwd_ms"], 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1), generated on device)",
+        "config": {"workload": "fp32 causal: config 1 (B=1 H=2 S=128 D=64) and B=1 Hq=8 Hkv=2 S=2048 "
+                               "D=64/128 on the CUDA-core kernels",
+                   "global_batch": 1, "seq_len": head["S"], "parallelism": "1 GPU",
+                   "l2": "flushed (256 MB write) before every timed call"},
+        "gpu_launches": int(launches), "cases": cases,
+        "roofline": None, "cpu_baseline": None, "e2e": None,
+        "note": "auxiliary line: the fp32 path; the c3 line is the headline"}), flush=True)
+
+
 DEC = dict(B=8, Hq=32, Hkv=8, Sq=1, Sk=32768, D=128)
 DEC_WORKLOAD = ("decode: bf16 B=8 Hq=32 Hkv=8 D=128, 1 query per head, 32768 keys, causal with "
                 "the query at the end of the keys (split-KV path)")
@@ -714,10 +778,11 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["c3", "c2", "c4", "c4t", "c5", "c5u", "decode"], default="c3",
+    ap.add_argument("--workload", choices=["c3", "c2", "c4", "c4t", "c5", "c5u", "decode", "fp32"], default="c3",
                     help="c3 (default, the headline), c2 (fp16 latencies), c4 / c4t (D=256 window + "
                          "soft-cap at S=8192 / 8190), c5 (context-parallel ring), c5u (context-"
-                         "parallel Ulysses) or decode (split-KV decoding forward)")
+                         "parallel Ulysses), decode (split-KV decoding forward) or fp32 (the fp32 "
+                         "path: config 1 and larger fp32 problems)")
     ap.add_argument("--ref-step-s", type=float, default=2.0,
                     help="CPU seconds per step of the reference arm (a bounded sample of slices)")
     ap.add_argument("--no-cp", action="store_true", help="skip the context-parallel key of the c3 line")
@@ -735,6 +800,8 @@ def main():
         run_c2(args)
     elif args.workload == "decode":
         run_decode(args)
+    elif args.workload == "fp32":
+        run_fp32(args)
     else:
         run_ours(args)
 
