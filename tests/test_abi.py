@@ -133,3 +133,8 @@ def test_ctypes_structures_match_header_layout(tmp_path):
         assert got[(cname, "size")] == ctypes.sizeof(cls), cname
         for field, _ in cls._fields_:
             assert got[(cname, field)] == getattr(cls, field).offset, (cname, field)
+
+
+def test_last_error_is_a_string_before_any_failure():
+    lib = bfa_lib.load()
+    assert isinstance(lib.bfa_last_error(), bytes)
