@@ -94,8 +94,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     kKVFull = 1,
     kKVEmpty = 1 + NS,
     kSFull = 1 + 2 * NS,
-    kPFull = kSFull + 2,
-    kODone = kPFull + 2,
+    kPFull = kSFull + 2,   // all of P_t(j) (and a rescaled O_t) in TMEM
+    kPHalf = kPFull + 2,   // P_t(j) of keys [0, 64) in TMEM (and a rescaled O_t)
+    kODone = kPHalf + 2,
     kDrain = kODone + 2,
     kNever = kDrain + 1,
     kNumBars = kNever + 1
@@ -144,7 +145,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; ++i)
-      mbar_init(bar(i), (i >= kPFull && i < kPFull + 2) ? 4u : 1u);
+      mbar_init(bar(i), (i >= kPFull && i < kPHalf + 2) ? 4u : 1u);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -219,14 +220,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit(bar(kSFull + t));
       };
-      auto issue_pv = [&](int t, int idx, bool acc) {
+      // PV_t(j) in two halves of 64 keys: the first is issued once the
+      // softmax has stored P for those keys, and runs while it forms the rest.
+      auto issue_pv = [&](int t, int idx, bool acc, int half) {
         const uint64_t dv = desc_mnmajor(kv_addr(idx), kBN * 128);
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
+        for (int k4 = 0; k4 < kBN / 32; ++k4) {
+          const int kk = half * (kBN / 32) + k4;
           mma_ts(tmem + L::kTmemO + t * D, tmem + L::kTmemS + t * kBN + kk * 8,
                  dv + ((kk * 16 * 128) >> 4), idO, (acc || kk > 0) ? 1u : 0u);
         }
-        mma_commit(bar(kODone + t));
+        if (half == 1) mma_commit(bar(kODone + t));
+      };
+      auto wait_pv = [&](int t, int it) {  // both halves of PV_t(it), each once its P is stored
+        if (!mbar_wait(bar(kPHalf + t), it & 1, ctl, BFA_ERR_DEVICE_TIMEOUT)) return false;
+        tc_fence_after();
+        issue_pv(t, 2 * it + 1, it > 0, 0);
+        if (!mbar_wait(bar(kPFull + t), it & 1, ctl, BFA_ERR_DEVICE_TIMEOUT)) return false;
+        tc_fence_after();
+        issue_pv(t, 2 * it + 1, it > 0, 1);
+        return true;
       };
       auto wait_load = [&](int idx) {
         return mbar_wait(bar(kKVFull + idx % NS), (idx / NS) & 1, ctl, BFA_ERR_DEVICE_TIMEOUT);
@@ -244,18 +257,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int iv = 2 * it + 1, ik = 2 * it + 2;
           const bool more = it + 1 < n_iter;
           if (!(ok = wait_load(iv))) break;
-          if (!(ok = mbar_wait(bar(kPFull + 0), it & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
-          tc_fence_after();
-          issue_pv(0, iv, it > 0);
+          if (!(ok = wait_pv(0, it))) break;
           if (more) {
             // K comes by TMA (ordered by the mbarrier); the softmax reads of
             // S_0 were ordered by the PFull wait and fence above.
             if (!(ok = wait_load(ik))) break;
             issue_s(0, ik);
           }
-          if (!(ok = mbar_wait(bar(kPFull + 1), it & 1, ctl, BFA_ERR_DEVICE_TIMEOUT))) break;
-          tc_fence_after();
-          issue_pv(1, iv, it > 0);
+          if (!(ok = wait_pv(1, it))) break;
           mma_commit(bar(kKVEmpty + iv % NS));
           if (more) {
             issue_s(1, ik);
@@ -390,6 +399,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr bool SPLIT = decltype(split)::value && kPolyEvery > 0;
 #pragma unroll
         for (int ch = 0; ch < kBN / 32; ++ch) {
+          if (ch == 2) {  // P of keys [0, 64) is stored: the first PV half may start
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kPHalf + t));
+          }
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
@@ -402,27 +417,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st16(tS + 16 * ch, pk);
         }
       };
-      if (full) exps(std::true_type{});
-      else exps(std::false_type{});
-      const float rs = (s2[0].x + s2[0].y) + (s2[1].x + s2[1].y);
-      l = l * alpha + rs;
-      m = m_new;
+      // O_t is rescaled (rarely) before the first PV half may read it.
       if (it > 0) {
         // PV_t(it-1) is complete (its commit precedes S_t(it)'s), so O_t is stable.
         if (!(ok = warp_wait(bar(kODone + t), (uint32_t)((it - 1) & 1), ctl))) break;
         tc_fence_after();
         if (rescale) {
+          // 16 columns at a time: the S row is still live in registers.
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tO + 32 * c, r);
+          for (int c = 0; c < D / 16; ++c) {
+            uint32_t o16[16];
+            tmem_ld16(tO + 16 * c, o16);
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tmem_st32(tO + 32 * c, r);
+            for (int i = 0; i < 16; ++i) o16[i] = __float_as_uint(__uint_as_float(o16[i]) * alpha);
+            tmem_st16(tO + 16 * c, o16);
           }
         }
       }
+      if (full) exps(std::true_type{});
+      else exps(std::false_type{});
+      const float rs = (s2[0].x + s2[0].y) + (s2[1].x + s2[1].y);
+      l = l * alpha + rs;
+      m = m_new;
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
