@@ -13,7 +13,8 @@
 //       copies on the host at :735-737) and the sum is deterministic.
 //
 // Tiles are 32 query rows x 32 key rows, 128 threads: thread t owns tile row
-// t/4 and, within it, every 4th key column and every 4th head-dim column.
+// t/4 and, within it, every 4th key column and every 4th float4 of the head
+// dim (starting at float4 t%4).
 #include <cuda_runtime.h>
 
 #include "bfa_common.cuh"
@@ -32,7 +33,7 @@ __device__ __forceinline__ const T* head_ptr(const void* base, const int64_t* st
 }
 
 // Stage rows [row0, row0 + nvalid) x [0, D) of a strided [S, D] slice into
-// shared memory as fp32 with row pitch DP+1; missing rows/cols become 0.
+// shared memory as fp32 with row pitch DP+4; missing rows/cols become 0.
 template <typename T, int DP>
 __device__ __forceinline__ void stage_rows(float* dst, const T* src, int64_t srow, int64_t scol,
                                            int row0, int nvalid, int D, int nrows) {
@@ -40,25 +41,42 @@ __device__ __forceinline__ void stage_rows(float* dst, const T* src, int64_t sro
     const int r = idx / DP, c = idx - r * DP;
     float val = 0.f;
     if (r < nvalid && c < D) val = to_f32<T>(src[(int64_t)(row0 + r) * srow + (int64_t)c * scol]);
-    dst[r * (DP + 1) + c] = val;
+    dst[r * (DP + 4) + c] = val;
   }
 }
 
+// Rows of the staged tiles have pitch DP + 4 floats: 16-byte aligned, so a
+// dot product reads both rows with 16-byte shared loads (a quarter of the
+// load instructions), and rows r, r+1, ... start 4 banks apart, so the
+// 8 rows a warp reads at once fill the 32 banks without conflicts.
+// Column of accumulator e of the thread with column group c: the thread
+// owns every 4th float4 of a row, starting at float4 c (the four threads of a
+// row read four consecutive float4s: no bank conflicts).
+__device__ __forceinline__ int acc_col(int e, int c) { return 16 * (e >> 2) + 4 * c + (e & 3); }
+
 template <int DP>
 __device__ __forceinline__ float dot_rows(const float* a, const float* b) {
-  float acc = 0.f;
-#pragma unroll 16
-  for (int d = 0; d < DP; ++d) acc = fmaf(a[d], b[d], acc);
-  return acc;
+  const float4* a4 = reinterpret_cast<const float4*>(a);
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+  float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 8
+  for (int d = 0; d < DP / 4; ++d) {
+    const float4 x = a4[d], y = b4[d];
+    acc0 = fmaf(x.x, y.x, acc0);
+    acc1 = fmaf(x.y, y.y, acc1);
+    acc0 = fmaf(x.z, y.z, acc0);
+    acc1 = fmaf(x.w, y.w, acc1);
+  }
+  return acc0 + acc1;
 }
 
 template <typename T, int DP>
 __global__ void __launch_bounds__(NT) simt_fwd_kernel(Params p) {
   extern __shared__ float smem[];
   float* sQ = smem;
-  float* sK = sQ + TM * (DP + 1);
-  float* sV = sK + TN * (DP + 1);
-  float* sP = sV + TN * (DP + 1);  // [TM][TN+1]
+  float* sK = sQ + TM * (DP + 4);
+  float* sV = sK + TN * (DP + 4);
+  float* sP = sV + TN * (DP + 4);  // [TM][TN+1]
 
   const int r0 = blockIdx.x * TM, hq = blockIdx.y, b = blockIdx.z;
   const int hkv = hq / p.G;
@@ -90,7 +108,7 @@ __global__ void __launch_bounds__(NT) simt_fwd_kernel(Params p) {
     for (int u = 0; u < TN / 4; ++u) {
       const int jj = c + 4 * u;
       const int64_t gj = (int64_t)k0 + jj + p.k_off;
-      const float dot = dot_rows<DP>(sQ + r * (DP + 1), sK + jj * (DP + 1));
+      const float dot = dot_rows<DP>(sQ + r * (DP + 4), sK + jj * (DP + 4));
       const float val = transform_logit(dot, p.scale, p.soft_cap, slope, gi, gj, nullptr);
       const bool ok = (jj < kn) && (r < rows) && keep_elem(p, b, hq, gi, gj);
       s[u] = ok ? val : neg_inf();
@@ -116,9 +134,15 @@ __global__ void __launch_bounds__(NT) simt_fwd_kernel(Params p) {
     for (int e = 0; e < DP / 4; ++e) acc[e] *= alpha;
     for (int jj = 0; jj < TN; ++jj) {
       const float pv = sP[r * (TN + 1) + jj];
-      const float* vrow = sV + jj * (DP + 1) + c;
+      const float4* vrow = reinterpret_cast<const float4*>(sV + jj * (DP + 4)) + c;
 #pragma unroll
-      for (int e = 0; e < DP / 4; ++e) acc[e] = fmaf(pv, vrow[4 * e], acc[e]);
+      for (int g = 0; g < DP / 16; ++g) {
+        const float4 v4 = vrow[4 * g];
+        acc[4 * g] = fmaf(pv, v4.x, acc[4 * g]);
+        acc[4 * g + 1] = fmaf(pv, v4.y, acc[4 * g + 1]);
+        acc[4 * g + 2] = fmaf(pv, v4.z, acc[4 * g + 2]);
+        acc[4 * g + 3] = fmaf(pv, v4.w, acc[4 * g + 3]);
+      }
     }
   }
 
@@ -127,7 +151,7 @@ __global__ void __launch_bounds__(NT) simt_fwd_kernel(Params p) {
     T* O = (T*)p.o + (int64_t)b * p.so_[0] + (int64_t)hq * p.so_[1] + (int64_t)(r0 + r) * p.so_[2];
 #pragma unroll
     for (int e = 0; e < DP / 4; ++e) {
-      const int d = c + 4 * e;
+      const int d = acc_col(e, c);
       if (d < p.D) O[(int64_t)d * p.so_[3]] = from_f32<T>(acc[e] * inv);
     }
     if (c == 0) {
@@ -140,10 +164,10 @@ template <typename T, int DP>
 __global__ void __launch_bounds__(NT) simt_bwd_dq_kernel(Params p) {
   extern __shared__ float smem[];
   float* sQ = smem;
-  float* sDO = sQ + TM * (DP + 1);
-  float* sK = sDO + TM * (DP + 1);
-  float* sV = sK + TN * (DP + 1);
-  float* sDS = sV + TN * (DP + 1);  // [TM][TN+1]
+  float* sDO = sQ + TM * (DP + 4);
+  float* sK = sDO + TM * (DP + 4);
+  float* sV = sK + TN * (DP + 4);
+  float* sDS = sV + TN * (DP + 4);  // [TM][TN+1]
 
   const int r0 = blockIdx.x * TM, hq = blockIdx.y, b = blockIdx.z;
   const int hkv = hq / p.G;
@@ -179,10 +203,10 @@ __global__ void __launch_bounds__(NT) simt_bwd_dq_kernel(Params p) {
       float ds = 0.f;
       if (row_live && jj < kn && keep_elem(p, b, hq, gi, gj)) {
         float t;
-        const float dot = dot_rows<DP>(sQ + r * (DP + 1), sK + jj * (DP + 1));
+        const float dot = dot_rows<DP>(sQ + r * (DP + 4), sK + jj * (DP + 4));
         const float val = transform_logit(dot, p.scale, p.soft_cap, slope, gi, gj, &t);
         const float pr = expf(val - lse);
-        const float dp = dot_rows<DP>(sDO + r * (DP + 1), sV + jj * (DP + 1));
+        const float dp = dot_rows<DP>(sDO + r * (DP + 4), sV + jj * (DP + 4));
         ds = pr * (dp - dlt);
         if (p.soft_cap > 0.f) ds *= (1.f - t * t);
         ds *= p.scale;
@@ -192,16 +216,22 @@ __global__ void __launch_bounds__(NT) simt_bwd_dq_kernel(Params p) {
     __syncwarp();
     for (int jj = 0; jj < TN; ++jj) {
       const float dsv = sDS[r * (TN + 1) + jj];
-      const float* krow = sK + jj * (DP + 1) + c;
+      const float4* krow = reinterpret_cast<const float4*>(sK + jj * (DP + 4)) + c;
 #pragma unroll
-      for (int e = 0; e < DP / 4; ++e) acc[e] = fmaf(dsv, krow[4 * e], acc[e]);
+      for (int g = 0; g < DP / 16; ++g) {
+        const float4 k4 = krow[4 * g];
+        acc[4 * g] = fmaf(dsv, k4.x, acc[4 * g]);
+        acc[4 * g + 1] = fmaf(dsv, k4.y, acc[4 * g + 1]);
+        acc[4 * g + 2] = fmaf(dsv, k4.z, acc[4 * g + 2]);
+        acc[4 * g + 3] = fmaf(dsv, k4.w, acc[4 * g + 3]);
+      }
     }
   }
   if (r < rows) {
     const int64_t base = (int64_t)b * p.sdq_[0] + (int64_t)hq * p.sdq_[1] + (int64_t)(r0 + r) * p.sdq_[2];
 #pragma unroll
     for (int e = 0; e < DP / 4; ++e) {
-      const int d = c + 4 * e;
+      const int d = acc_col(e, c);
       if (d >= p.D) continue;
       const int64_t at = base + (int64_t)d * p.sdq_[3];
       if (p.grad_acc) ((float*)p.dq)[at] += acc[e];
@@ -214,10 +244,10 @@ template <typename T, int DP>
 __global__ void __launch_bounds__(NT) simt_bwd_dkdv_kernel(Params p) {
   extern __shared__ float smem[];
   float* sK = smem;
-  float* sV = sK + TN * (DP + 1);
-  float* sQ = sV + TN * (DP + 1);
-  float* sDO = sQ + TM * (DP + 1);
-  float* sP = sDO + TM * (DP + 1);   // [TN][TM+1]
+  float* sV = sK + TN * (DP + 4);
+  float* sQ = sV + TN * (DP + 4);
+  float* sDO = sQ + TM * (DP + 4);
+  float* sP = sDO + TM * (DP + 4);   // [TN][TM+1]
   float* sDS = sP + TN * (TM + 1);   // [TN][TM+1]
   float* sL = sDS + TN * (TM + 1);   // [TM]
   float* sDl = sL + TM;              // [TM]
@@ -259,10 +289,10 @@ __global__ void __launch_bounds__(NT) simt_bwd_dkdv_kernel(Params p) {
         const float lse = sL[ii];
         if (r < cols && ii < qn && lse != neg_inf() && keep_elem(p, b, hq, gi, gj)) {
           float t;
-          const float dot = dot_rows<DP>(sQ + ii * (DP + 1), sK + r * (DP + 1));
+          const float dot = dot_rows<DP>(sQ + ii * (DP + 4), sK + r * (DP + 4));
           const float val = transform_logit(dot, p.scale, p.soft_cap, slope, gi, gj, &t);
           pr = expf(val - lse);
-          const float dp = dot_rows<DP>(sDO + ii * (DP + 1), sV + r * (DP + 1));
+          const float dp = dot_rows<DP>(sDO + ii * (DP + 4), sV + r * (DP + 4));
           ds = pr * (dp - sDl[ii]);
           if (p.soft_cap > 0.f) ds *= (1.f - t * t);
           ds *= p.scale;
@@ -274,12 +304,19 @@ __global__ void __launch_bounds__(NT) simt_bwd_dkdv_kernel(Params p) {
       for (int ii = 0; ii < TM; ++ii) {
         const float pv = sP[r * (TM + 1) + ii];
         const float dsv = sDS[r * (TM + 1) + ii];
-        const float* dorow = sDO + ii * (DP + 1) + c;
-        const float* qrow = sQ + ii * (DP + 1) + c;
+        const float4* dorow = reinterpret_cast<const float4*>(sDO + ii * (DP + 4)) + c;
+        const float4* qrow = reinterpret_cast<const float4*>(sQ + ii * (DP + 4)) + c;
 #pragma unroll
-        for (int e = 0; e < DP / 4; ++e) {
-          adv[e] = fmaf(pv, dorow[4 * e], adv[e]);
-          adk[e] = fmaf(dsv, qrow[4 * e], adk[e]);
+        for (int g = 0; g < DP / 16; ++g) {
+          const float4 o4 = dorow[4 * g], q4 = qrow[4 * g];
+          adv[4 * g] = fmaf(pv, o4.x, adv[4 * g]);
+          adv[4 * g + 1] = fmaf(pv, o4.y, adv[4 * g + 1]);
+          adv[4 * g + 2] = fmaf(pv, o4.z, adv[4 * g + 2]);
+          adv[4 * g + 3] = fmaf(pv, o4.w, adv[4 * g + 3]);
+          adk[4 * g] = fmaf(dsv, q4.x, adk[4 * g]);
+          adk[4 * g + 1] = fmaf(dsv, q4.y, adk[4 * g + 1]);
+          adk[4 * g + 2] = fmaf(dsv, q4.z, adk[4 * g + 2]);
+          adk[4 * g + 3] = fmaf(dsv, q4.w, adk[4 * g + 3]);
         }
       }
     }
@@ -289,7 +326,7 @@ __global__ void __launch_bounds__(NT) simt_bwd_dkdv_kernel(Params p) {
     const int64_t bv = (int64_t)b * p.sdv_[0] + (int64_t)hkv * p.sdv_[1] + (int64_t)(c0 + r) * p.sdv_[2];
 #pragma unroll
     for (int e = 0; e < DP / 4; ++e) {
-      const int d = c + 4 * e;
+      const int d = acc_col(e, c);
       if (d >= p.D) continue;
       const int64_t ak = bk + (int64_t)d * p.sdk_[3], av = bv + (int64_t)d * p.sdv_[3];
       if (p.grad_acc) {
@@ -388,7 +425,7 @@ static bool rows_vec_ok(const void* ptr, const int64_t* st, int D) {
 
 template <typename T, int DP>
 int launch_fwd_t(const Params& p, cudaStream_t st) {
-  const size_t smem = (size_t)(TM + 2 * TN) * (DP + 1) * 4 + (size_t)TM * (TN + 1) * 4;
+  const size_t smem = (size_t)(TM + 2 * TN) * (DP + 4) * 4 + (size_t)TM * (TN + 1) * 4;
   auto kern = simt_fwd_kernel<T, DP>;
   if (cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))
     return cuda_fail("simt_fwd_kernel shared-memory attribute", e);
@@ -402,7 +439,7 @@ int launch_fwd_t(const Params& p, cudaStream_t st) {
 template <typename T, int DP>
 int launch_bwd_t(const Params& p, cudaStream_t st) {
   if (p.phases & BFA_BWD_PHASE_DQ) {
-    const size_t smem = (size_t)(2 * TM + 2 * TN) * (DP + 1) * 4 + (size_t)TM * (TN + 1) * 4;
+    const size_t smem = (size_t)(2 * TM + 2 * TN) * (DP + 4) * 4 + (size_t)TM * (TN + 1) * 4;
     auto kern = simt_bwd_dq_kernel<T, DP>;
     if (cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))
       return cuda_fail("simt backward shared-memory attribute", e);
@@ -414,7 +451,7 @@ int launch_bwd_t(const Params& p, cudaStream_t st) {
     }
   }
   if (p.phases & BFA_BWD_PHASE_DKDV) {
-    const size_t smem = (size_t)(2 * TM + 2 * TN) * (DP + 1) * 4 + (size_t)2 * TN * (TM + 1) * 4 + 2 * TM * 4;
+    const size_t smem = (size_t)(2 * TM + 2 * TN) * (DP + 4) * 4 + (size_t)2 * TN * (TM + 1) * 4 + 2 * TM * 4;
     auto kern = simt_bwd_dkdv_kernel<T, DP>;
     if (cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))
       return cuda_fail("simt backward shared-memory attribute", e);
