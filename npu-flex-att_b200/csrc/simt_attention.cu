@@ -15,6 +15,8 @@
 // Tiles are 32 query rows x 32 key rows, 128 threads: thread t owns tile row
 // t/4 and, within it, every 4th key column and every 4th float4 of the head
 // dim (starting at float4 t%4).
+#include <algorithm>
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
 #include "bfa_common.cuh"
@@ -240,8 +242,14 @@ __global__ void __launch_bounds__(NT) simt_bwd_dq_kernel(Params p) {
   }
 }
 
+// One cluster of `nsplit` CTAs per (b, kv-head, kv tile): CTA `split` takes
+// every nsplit-th (q-head, query tile) work item, and the cluster's partial
+// dK / dV are added in rank order through distributed shared memory, so the
+// result does not depend on timing (deterministic) while nsplit times more
+// CTAs share the work.
 template <typename T, int DP>
 __global__ void __launch_bounds__(NT) simt_bwd_dkdv_kernel(Params p) {
+  namespace cg = cooperative_groups;
   extern __shared__ float smem[];
   float* sK = smem;
   float* sV = sK + TN * (DP + 4);
@@ -252,7 +260,9 @@ __global__ void __launch_bounds__(NT) simt_bwd_dkdv_kernel(Params p) {
   float* sL = sDS + TN * (TM + 1);   // [TM]
   float* sDl = sL + TM;              // [TM]
 
-  const int c0 = blockIdx.x * TN, hkv = blockIdx.y, b = blockIdx.z;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int nsplit = (int)cluster.dim_blocks().x, split = (int)cluster.block_rank();
+  const int c0 = (blockIdx.x / nsplit) * TN, hkv = blockIdx.y, b = blockIdx.z;
   const int cols = min(TN, p.Sk - c0);
   stage_rows<T, DP>(sK, head_ptr<T>(p.k, p.sk_, b, hkv), p.sk_[2], p.sk_[3], c0, cols, p.D, TN);
   stage_rows<T, DP>(sV, head_ptr<T>(p.v, p.sv_, b, hkv), p.sv_[2], p.sv_[3], c0, cols, p.D, TN);
@@ -265,12 +275,14 @@ __global__ void __launch_bounds__(NT) simt_bwd_dkdv_kernel(Params p) {
 
   int qlo, qhi;
   query_range(p, c0, c0 + cols, &qlo, &qhi);
+  int work = 0;  // work item index over (q-head, query tile)
   for (int g = 0; g < p.G; ++g) {
     const int hq = hkv * p.G + g;
     const float slope = p.alibi ? p.alibi[hq] : 0.f;
     const T* Q = head_ptr<T>(p.q, p.sq_, b, hq);
     const T* DO = head_ptr<T>(p.dout, p.sdo_, b, hq);
     for (int q0 = (qlo / TM) * TM; q0 < qhi; q0 += TM) {
+      if ((work++ % nsplit) != split) continue;  // another CTA of the cluster's
       const int qn = min(TM, p.Sq - q0);
       __syncthreads();
       stage_rows<T, DP>(sQ, Q, p.sq_[2], p.sq_[3], q0, qn, p.D, TM);
@@ -320,6 +332,32 @@ __global__ void __launch_bounds__(NT) simt_bwd_dkdv_kernel(Params p) {
         }
       }
     }
+  }
+  if (nsplit > 1) {
+    // Partials into this CTA's Q / dO tiles, then rank 0 adds the others'
+    // in rank order and writes the result.
+    float* pk = sQ;
+    float* pv = sDO;
+    __syncthreads();
+#pragma unroll
+    for (int e = 0; e < DP / 4; ++e) {
+      pk[r * (DP + 4) + acc_col(e, c)] = adk[e];
+      pv[r * (DP + 4) + acc_col(e, c)] = adv[e];
+    }
+    cluster.sync();
+    if (split == 0) {
+      for (int rk = 1; rk < nsplit; ++rk) {
+        const float* rpk = cluster.map_shared_rank(pk, rk);
+        const float* rpv = cluster.map_shared_rank(pv, rk);
+#pragma unroll
+        for (int e = 0; e < DP / 4; ++e) {
+          adk[e] += rpk[r * (DP + 4) + acc_col(e, c)];
+          adv[e] += rpv[r * (DP + 4) + acc_col(e, c)];
+        }
+      }
+    }
+    cluster.sync();  // the other ranks' shared memory stays alive until read
+    if (split != 0) return;
   }
   if (r < cols) {
     const int64_t bk = (int64_t)b * p.sdk_[0] + (int64_t)hkv * p.sdk_[1] + (int64_t)(c0 + r) * p.sdk_[2];
@@ -455,9 +493,31 @@ int launch_bwd_t(const Params& p, cudaStream_t st) {
     auto kern = simt_bwd_dkdv_kernel<T, DP>;
     if (cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))
       return cuda_fail("simt backward shared-memory attribute", e);
-    dim3 grid((p.Sk + TN - 1) / TN, p.Hkv, p.B);
-    if (grid.x && grid.y && grid.z) {
-      kern<<<grid, NT, smem, st>>>(p);
+    const int n_kt = (p.Sk + TN - 1) / TN;
+    // Split each kv tile's work over a cluster of up to 8 CTAs until about
+    // two waves of CTAs cover the SMs (bounded by the work items a tile has).
+    const long long units = (long long)n_kt * p.Hkv * p.B;
+    int nsplit = 1;
+    if (units > 0) {
+      const long long want = (2LL * sm_count() + units - 1) / units;
+      const int items = p.G * ((p.Sq + TM - 1) / TM);
+      nsplit = (int)std::min<long long>({8LL, want, (long long)std::max(items, 1)});
+      nsplit = std::max(nsplit, 1);
+    }
+    if (units > 0) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)(n_kt * nsplit), p.Hkv, p.B);
+      cfg.blockDim = dim3(NT);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = st;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = (unsigned)nsplit;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p)) return cuda_fail("simt dK/dV cluster launch", e);
       note_launch();
       if (int rc = launch_status("simt backward kernel launch")) return rc;
     }
