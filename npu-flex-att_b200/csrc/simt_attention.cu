@@ -47,10 +47,31 @@ __device__ __forceinline__ void stage_rows(float* dst, const T* src, int64_t sro
   }
 }
 
-// Rows of the staged tiles have pitch DP + 4 floats: 16-byte aligned, so a
-// dot product reads both rows with 16-byte shared loads (a quarter of the
-// load instructions), and rows r, r+1, ... start 4 banks apart, so the
-// 8 rows a warp reads at once fill the 32 banks without conflicts.
+// Rows of the staged tiles have pitch DP + 4 floats: 16-byte aligned, so dot
+// products and accumulations read them with 16-byte shared loads, and rows
+// r, r+1, ... start 4 banks apart, so the 8 rows a warp reads at once fill
+// the 32 banks without conflicts.
+// The 8 dot products of row `a` with rows b0 + 4u·pitch, u = 0..7 (a thread's
+// 8 columns of a 32-wide tile): each float4 of `a` is read once for all 8.
+template <int DP>
+__device__ __forceinline__ void dots8(const float* a, const float* b0, float (&out)[8]) {
+  const float4* a4 = reinterpret_cast<const float4*>(a);
+#pragma unroll
+  for (int u = 0; u < 8; ++u) out[u] = 0.f;
+#pragma unroll 4
+  for (int d = 0; d < DP / 4; ++d) {
+    const float4 x = a4[d];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const float4 y = reinterpret_cast<const float4*>(b0 + 4 * u * (DP + 4))[d];
+      out[u] = fmaf(x.x, y.x, out[u]);
+      out[u] = fmaf(x.y, y.y, out[u]);
+      out[u] = fmaf(x.z, y.z, out[u]);
+      out[u] = fmaf(x.w, y.w, out[u]);
+    }
+  }
+}
+
 // Column of accumulator e of the thread with column group c: the thread
 // owns every 4th float4 of a row, starting at float4 c (the four threads of a
 // row read four consecutive float4s: no bank conflicts).
@@ -106,11 +127,13 @@ __global__ void __launch_bounds__(NT) simt_fwd_kernel(Params p) {
     __syncthreads();
     float s[TN / 4];
     float mx = neg_inf();
+    float dot8[8];
+    dots8<DP>(sQ + r * (DP + 4), sK + c * (DP + 4), dot8);
 #pragma unroll
     for (int u = 0; u < TN / 4; ++u) {
       const int jj = c + 4 * u;
       const int64_t gj = (int64_t)k0 + jj + p.k_off;
-      const float dot = dot_rows<DP>(sQ + r * (DP + 4), sK + jj * (DP + 4));
+      const float dot = dot8[u];
       const float val = transform_logit(dot, p.scale, p.soft_cap, slope, gi, gj, nullptr);
       const bool ok = (jj < kn) && (r < rows) && keep_elem(p, b, hq, gi, gj);
       s[u] = ok ? val : neg_inf();
@@ -198,6 +221,9 @@ __global__ void __launch_bounds__(NT) simt_bwd_dq_kernel(Params p) {
     stage_rows<T, DP>(sK, K, p.sk_[2], p.sk_[3], k0, kn, p.D, TN);
     stage_rows<T, DP>(sV, V, p.sv_[2], p.sv_[3], k0, kn, p.D, TN);
     __syncthreads();
+    float sdot[8], pdot[8];
+    dots8<DP>(sQ + r * (DP + 4), sK + c * (DP + 4), sdot);
+    dots8<DP>(sDO + r * (DP + 4), sV + c * (DP + 4), pdot);
 #pragma unroll
     for (int u = 0; u < TN / 4; ++u) {
       const int jj = c + 4 * u;
@@ -205,10 +231,10 @@ __global__ void __launch_bounds__(NT) simt_bwd_dq_kernel(Params p) {
       float ds = 0.f;
       if (row_live && jj < kn && keep_elem(p, b, hq, gi, gj)) {
         float t;
-        const float dot = dot_rows<DP>(sQ + r * (DP + 4), sK + jj * (DP + 4));
+        const float dot = sdot[u];
         const float val = transform_logit(dot, p.scale, p.soft_cap, slope, gi, gj, &t);
         const float pr = expf(val - lse);
-        const float dp = dot_rows<DP>(sDO + r * (DP + 4), sV + jj * (DP + 4));
+        const float dp = pdot[u];
         ds = pr * (dp - dlt);
         if (p.soft_cap > 0.f) ds *= (1.f - t * t);
         ds *= p.scale;
@@ -293,6 +319,9 @@ __global__ void __launch_bounds__(NT) simt_bwd_dkdv_kernel(Params p) {
         sDl[tid] = (tid < qn) ? p.delta[((int64_t)b * p.Hq + hq) * p.Sq_pad + q0 + tid] : 0.f;
       }
       __syncthreads();
+      float sdot[8], pdot[8];
+      dots8<DP>(sK + r * (DP + 4), sQ + c * (DP + 4), sdot);
+      dots8<DP>(sV + r * (DP + 4), sDO + c * (DP + 4), pdot);
 #pragma unroll
       for (int u = 0; u < TM / 4; ++u) {
         const int ii = c + 4 * u;
@@ -301,10 +330,10 @@ __global__ void __launch_bounds__(NT) simt_bwd_dkdv_kernel(Params p) {
         const float lse = sL[ii];
         if (r < cols && ii < qn && lse != neg_inf() && keep_elem(p, b, hq, gi, gj)) {
           float t;
-          const float dot = dot_rows<DP>(sQ + ii * (DP + 4), sK + r * (DP + 4));
+          const float dot = sdot[u];
           const float val = transform_logit(dot, p.scale, p.soft_cap, slope, gi, gj, &t);
           pr = expf(val - lse);
-          const float dp = dot_rows<DP>(sDO + ii * (DP + 4), sV + r * (DP + 4));
+          const float dp = pdot[u];
           ds = pr * (dp - sDl[ii]);
           if (p.soft_cap > 0.f) ds *= (1.f - t * t);
           ds *= p.scale;
