@@ -518,6 +518,11 @@ struct DqLayout {
   static_assert(kOffDO == kOffQ + kQBytes && 2 * kQBytes >= kRows * D * 4, "fp32 dQ staging");
 };
 
+#ifndef BFA_DQ_UNIT_GROUP
+#define BFA_DQ_UNIT_GROUP 4
+#endif
+constexpr int kDqUnitGroup = BFA_DQ_UNIT_GROUP;
+
 template <int D, bool BF16, bool CAP, bool ALIBI>
 __global__ void __launch_bounds__(kThreads, 1)
     dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
@@ -555,9 +560,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qt = (p.Sq + kRows - 1) / kRows;
-  const int bh = blockIdx.x % (p.B * p.Hq);
-  const int qt = n_qt - 1 - (int)(blockIdx.x / (p.B * p.Hq));  // heaviest causal tiles first
-  const int hq = bh % p.Hq, b = bh / p.Hq;
+  // Block order: (batch, kv-head) units in groups of kDqUnitGroup; within a
+  // group the query tile is the slow index, heaviest causal tiles first, so
+  // the CTAs in flight share a few units' K / V in L2.
+  const int BHkv = p.B * p.Hkv;
+  const int grp = (int)(blockIdx.x / ((unsigned)kDqUnitGroup * p.G * n_qt));
+  const int gsize = min(kDqUnitGroup, BHkv - grp * kDqUnitGroup) * p.G;  // q-heads in the group
+  const int rem = (int)(blockIdx.x - (unsigned)grp * kDqUnitGroup * p.G * n_qt);
+  const int qt = n_qt - 1 - rem / gsize;
+  const int bhq = grp * kDqUnitGroup * p.G + rem % gsize;  // (b, hq) with hq fastest
+  const int hq = bhq % p.Hq, b = bhq / p.Hq;
   const int hkv = hq / p.G;
   const int q0 = qt * kRows;
   int klo, khi;
