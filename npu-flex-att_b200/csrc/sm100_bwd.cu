@@ -18,11 +18,13 @@
 //   dV += Pᵀ dOᵢ and dK += dSᵀ Qᵢ (N = D, B operand MN-major).
 // dq_kernel: one CTA per (batch, q-head, 128-row query tile); loops over
 //   128-key tiles: S = Q Kⱼᵀ, dP = dO Vⱼᵀ (Q, dO held in TMEM), dQ += dS Kⱼ.
-// Warp roles in both: warp 0 TMA producer (+ LSE/Δ staging), warp 1 MMA
-// issuer, warp 2 TMEM allocator, warps 4-11 elementwise: two warpgroups, one
-// row per thread, each taking half of every step's 64 columns. S/dP are
-// double-buffered in TMEM so the MMAs of step i+1 overlap the elementwise
-// work of step i.
+// Warp roles in both: warp 0 TMA producer (+ LSE/Δ staging), warps 1 and 3
+// MMA issuers (warp 1 the S/dP products, warp 3 the accumulating dV/dK or dQ
+// products), warp 2 TMEM allocator, warps 4-11 elementwise: two warpgroups,
+// one row per thread, each taking half of every step's columns. The dQ
+// kernel forms Δ in its prologue when the call has both the Δ and dQ
+// phases. S/dP are double-buffered (dK/dV) or released early (dQ) in TMEM so
+// the MMAs of step i+1 overlap the elementwise work of step i.
 // Accumulate mode (Params::grad_acc): dq/dk/dv are fp32 and the epilogues
 // TMA reduce-add their fp32 tiles into them instead of storing 16-bit tiles.
 #include <cuda.h>

@@ -12,7 +12,7 @@ namespace bwd {
 
 using namespace sm100;
 
-constexpr int kThreads = 384;  // warps 0-3: TMA / MMA / TMEM alloc / idle; 4-11: two elementwise warpgroups
+constexpr int kThreads = 384;  // warps 0-3: TMA / MMA / TMEM alloc / MMA (D <= 128; idle at D = 256); 4-11: elementwise
 constexpr int kRows = 128;  // TMEM lanes / rows owned by the elementwise warps
 constexpr int kInner = 64;  // columns of one S/dP step
 
