@@ -18,7 +18,8 @@
 //               via smem + TMA store and the LSE.
 // The MMA order S_0(j), S_1(j), then per step PV_0(j), S_0(j+1), PV_1(j),
 // S_1(j+1) lets one tile's softmax run while the tensor core works on the
-// other tile. K/V are read with the GQA head map hkv = hq / G
+// other tile; each PV_t(j) goes out in two halves of 64 keys, the first once
+// the softmax has stored P for those keys. K/V are read with the GQA head map hkv = hq / G
 // (npu_flash_attention.py:42); no K/V expansion happens anywhere.
 #include <cuda.h>
 #include <cuda_runtime.h>
