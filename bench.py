@@ -5,7 +5,8 @@ Llama-3-8B-style GQA layer, B=4 per GPU, Hq=32, Hkv=8, D=128, S=4096, causal,
 scale 1/sqrt(128); q, k, v, grad_out ~ N(0,1) seeded, synthetic.
 
 One step = one forward + one backward of that layer through the library's
-C ABI (bfa_fwd, then Δ, dK/dV, dQ as three calls on one workspace so each
+C ABI (bfa_fwd, then the backward as two calls on one workspace: Δ and dQ --
+the dQ kernel forms Δ itself at head dims 64/128 -- and dK/dV, so each
 kernel is timed on its own). FLOPs count only unmasked (i, j) pairs,
 element-exact: 4·D per pair forward, 10·D backward.
 
