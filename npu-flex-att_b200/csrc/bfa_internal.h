@@ -20,9 +20,9 @@ int sm100_fwd256(const Params& p, int dtype, cudaStream_t st);  // head_dim 256 
 bool sm100_bwd_eligible(const Params& p, int dtype);
 int sm100_bwd(const Params& p, int dtype, cudaStream_t st);
 int sm100_bwd256(const Params& p, int dtype, cudaStream_t st);  // head_dim 256 (sm100_bwd256.cu)
-// Whether sm100_bwd's dQ kernel can form Δ itself (Params::fuse_delta): head
-// dims 64/128 with 16-byte aligned, unit-stride O rows. BFA_BWD_FUSE_DELTA=0
-// turns it off.
+// Whether sm100_bwd's dQ kernel can form Δ itself (Params::fuse_delta): the
+// tcgen05 path (head dims 64, 128, 256) with a TMA-compatible O.
+// BFA_BWD_FUSE_DELTA=0 turns it off.
 bool sm100_bwd_fuses_delta(const Params& p, int dtype);
 // Split-KV decoding forward (decode.cu): the G q-heads of a KV head have at
 // most 64 query rows. Its partial results live in a caller workspace of

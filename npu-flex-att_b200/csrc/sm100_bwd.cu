@@ -1029,7 +1029,7 @@ bool sm100_bwd_fuses_delta(const Params& p, int dtype) {
     const char* e = std::getenv("BFA_BWD_FUSE_DELTA");
     return !(e && e[0] == '0');
   }();
-  if (!enabled || (p.D != 64 && p.D != 128) || !p.lse || !p.lse2 || !sm100_bwd_eligible(p, dtype))
+  if (!enabled || !p.lse || !p.lse2 || !sm100_bwd_eligible(p, dtype))
     return false;
   return tma_layout_ok(p.o, p.so_, 2);  // the dQ kernel TMA-loads the O tile
 }

@@ -468,7 +468,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // computed. Ring units (64 keys x 256 dims), in MMA order:
 //   K_0, V_0, K_1, V_1, K'_0, K_2, V_2, K'_1, ...
 // (K'_j: K_j again, for dQ(j)). Q arrives in ring slots 2-3 and is copied
-// into TMEM before those slots are used.
+// into TMEM before those slots are used. With a fused Δ, the O tile arrives
+// in slots 0-1 and the ring starts once Δ is formed.
 struct Dq256Layout {
   static constexpr int kKeys = 64;
   static constexpr int NS = 4;
@@ -477,7 +478,8 @@ struct Dq256Layout {
   static constexpr uint32_t kOffRing = kOffDS + 16384;       // NS x 32 KB
   static constexpr uint32_t kOffQ = kOffRing + 2 * kUnit;    // Q staging = ring slots 2-3
   static constexpr uint32_t kOffBar = kOffRing + NS * kUnit;
-  static constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
+  static constexpr uint32_t kOffDlt = kOffBar + 512;         // fused Δ: [2 warpgroups][128 rows] partials
+  static constexpr uint32_t kSmemBytes = kOffDlt + 1024 + 1024;
   static constexpr uint32_t kTmemS = 0, kTmemDP = 64, kTmemDQ = 128, kTmemQ = 384;
   static_assert(kSmemBytes <= 232448, "smem budget");
 };
@@ -497,7 +499,8 @@ template <bool BF16, bool CAP, bool ALIBI>
 __global__ void __launch_bounds__(kThreads, 1)
     dq256_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
                  const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                 const __grid_constant__ CUtensorMap tmDQ, const Params p) {
+                 const __grid_constant__ CUtensorMap tmDQ, const __grid_constant__ CUtensorMap tmO,
+                 const Params p) {
   using L = Dq256Layout;
   constexpr int NS = L::NS;
   constexpr int NK = L::kKeys;
@@ -571,11 +574,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // A query tile that sees no key loads nothing: its epilogue stages
       // zeros, which must not meet a TMA write in flight.
+      const bool fuse = p.fuse_delta != 0;
       if (n_iter > 0) {
-        mbar_arrive_expect_tx(bar(kQFull), 2 * 65536);
+        mbar_arrive_expect_tx(bar(kQFull), (fuse ? 3 : 2) * 65536);
         for (int s = 0; s < 4; ++s) {
           tma_load_4d(sbase + L::kOffQ + s * kSub128, &tmQ, bar(kQFull), s * 64, q0, hq, b);
           tma_load_4d(sbase + L::kOffDO + s * kSub128, &tmDO, bar(kQFull), s * 64, q0, hq, b);
+          // Fused Δ: the O tile into ring slots 0-1, free until Δ is formed.
+          if (fuse) tma_load_4d(sbase + L::kOffRing + s * kSub128, &tmO, bar(kQFull), s * 64, q0, hq, b);
         }
       }
       int n = 0;
@@ -585,7 +591,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int slot = n % NS;
         bool ok = true;
         if (n >= NS) ok = mbar_wait(bar(kEmpty + slot), ((n / NS) & 1) ^ 1, ctl, BFA_ERR_DEVICE_TIMEOUT);
-        else if (slot >= 2) ok = mbar_wait(bar(kOpsReady), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);  // Q staging free
+        else if (slot >= 2 || fuse)  // Q staging (and, fused, the O tile) consumed
+          ok = mbar_wait(bar(kOpsReady), 0, ctl, BFA_ERR_DEVICE_TIMEOUT);
         if (!ok) return false;
         mbar_arrive_expect_tx(bar(kFull + slot), kUnit);
         const int key0 = (op == 0 ? w0.step(j) : op == 1 ? w1.step(j) : w2.step(j)) * NK;
@@ -666,14 +673,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float slope2 = slope * kLog2e;
     const int64_t g0 = ALIBI ? alibi_ref(p, slope, gi, qi < p.Sq) : gi;  // ALiBi bias slope·(g0 - j)
     const int64_t ridx = ((int64_t)b * p.Hq + hq) * p.Sq_pad + qi;
-    const float lse2 = p.lse2[ridx];
-    const float dlt = p.delta[ridx];
+    const bool fuse = p.fuse_delta != 0;
+    float lse2, dlt = 0.f;
+    if (!fuse) {
+      lse2 = p.lse2[ridx];
+      dlt = p.delta[ridx];
+    } else {
+      // lse2 as the Δ pass forms it: +inf past Sq and for rows that see no key.
+      lse2 = __int_as_float(0x7f800000);
+      if (qi < p.Sq) {
+        const float lse = p.lse[((int64_t)b * p.Hq + hq) * p.Sq + qi];
+        if (lse != neg_inf()) lse2 = row_lse2(p, lse, hq, qi);
+      }
+    }
+    float* dpart = reinterpret_cast<float*>(smem + L::kOffDlt);  // [warpgroup][row]
     bool ok = true;
     // Q into TMEM: warpgroup h moves dims [128h, 128h + 128) of this thread's
     // row (two 64-dim sub-tiles) into columns [64h, 64h + 64) of the Q area.
+    // Fused Δ: each warpgroup also sums O·dO over the same dims (O in ring
+    // slots 0-1, dO resident); the halves meet through shared memory. A tile
+    // that sees no key has Δ = 0 (its P is 0). TMA fills rows past Sq with 0.
     if (n_iter > 0) {
       ok = warp_wait(bar(kQFull), 0, ctl);
       if (ok) {
+        float2 acc2 = make_float2(0.f, 0.f);
 #pragma unroll 1
         for (int s = 2 * eg; s < 2 * eg + 2; ++s) {
           uint32_t r[32];
@@ -683,12 +706,30 @@ __global__ void __launch_bounds__(kThreads, 1)
             r[4 * c] = w.x; r[4 * c + 1] = w.y; r[4 * c + 2] = w.z; r[4 * c + 3] = w.w;
           }
           tmem_st32(tmem + lane_base + L::kTmemQ + 32 * s, r);
+          if (fuse) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const uint4 o4 = *reinterpret_cast<const uint4*>(smem + L::kOffRing + s * kSub128 + sw128_offset(row, c));
+              const uint4 d4 = *reinterpret_cast<const uint4*>(smem + L::kOffDO + s * kSub128 + sw128_offset(row, c));
+              const uint32_t ow[4] = {o4.x, o4.y, o4.z, o4.w}, dw[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) acc2 = __ffma2_rn(unpack2<BF16>(ow[e]), unpack2<BF16>(dw[e]), acc2);
+            }
+          }
         }
+        if (fuse) dpart[eg * kRows + row] = acc2.x + acc2.y;
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(kOpsReady));
+        // Both warpgroups' halves (the arrivals release the shared stores),
+        // added in the same order in both.
+        if (fuse && (ok = warp_wait(bar(kOpsReady), 0, ctl))) dlt = dpart[row] + dpart[kRows + row];
       }
+    }
+    if (fuse && eg == 0 && qi < p.Sq_pad) {
+      p.delta[ridx] = dlt;
+      p.lse2[ridx] = lse2;
     }
     uint8_t* ds_base = smem + L::kOffDS;
     // Without documents a key step is fully kept exactly when its first key
@@ -834,32 +875,47 @@ int launch_kv(const Params& p, int dtype, cudaStream_t st) {
 template <bool BF16, bool CAP, bool ALIBI>
 int launch_bwd(const Params& p, int dtype, cudaStream_t st) {
   const int gdt = p.grad_acc ? BFA_DTYPE_F32 : dtype;
-  if (p.phases & BFA_BWD_PHASE_DKDV) {
-    int rc = launch_kv<kModeDV, BF16, CAP, ALIBI>(p, dtype, st);
-    if (rc) return rc;
-    rc = launch_kv<kModeDK, BF16, CAP, ALIBI>(p, dtype, st);
-    if (rc) return rc;
-  }
-  if (p.phases & BFA_BWD_PHASE_DQ) {
+  auto run_dkdv = [&]() -> int {
+    const int rc = launch_kv<kModeDV, BF16, CAP, ALIBI>(p, dtype, st);
+    return rc ? rc : launch_kv<kModeDK, BF16, CAP, ALIBI>(p, dtype, st);
+  };
+  auto run_dq = [&]() -> int {
     using L = Dq256Layout;
     auto kern = dq256_kernel<BF16, CAP, ALIBI>;
     static std::once_flag once;
     static bool attr_ok = false;
     std::call_once(once, [&] { attr_ok = set_smem(kern, L::kSmemBytes); });
     if (!attr_ok) return cuda_fail("dq256_kernel shared-memory attribute", cudaSuccess);
-    CUtensorMap m[5];
+    CUtensorMap m[6];
     if (!make_tmap_bhsd(&m[0], p.q, dtype, kD, p.Sq, p.Hq, p.B, p.sq_, kRows) ||
         !make_tmap_bhsd(&m[1], p.dout, dtype, kD, p.Sq, p.Hq, p.B, p.sdo_, kRows) ||
         !make_tmap_bhsd(&m[2], p.k, dtype, kD, p.Sk, p.Hkv, p.B, p.sk_, L::kKeys) ||
         !make_tmap_bhsd(&m[3], p.v, dtype, kD, p.Sk, p.Hkv, p.B, p.sv_, L::kKeys) ||
         !make_tmap_bhsd(&m[4], p.dq, gdt, kD, p.Sq, p.Hq, p.B, p.sdq_, kRows))
       return BFA_ERR_CUDA;  // make_tmap_bhsd recorded the detail
+    // O (fused Δ only; otherwise a copy of the Q map that is never read).
+    if (p.fuse_delta) {
+      if (!make_tmap_bhsd(&m[5], p.o, dtype, kD, p.Sq, p.Hq, p.B, p.so_, kRows))
+        return BFA_ERR_CUDA;  // make_tmap_bhsd recorded the detail
+    } else {
+      m[5] = m[0];
+    }
     const unsigned grid = (unsigned)((p.Sq + kRows - 1) / kRows) * p.Hq * p.B;
-    kern<<<grid, kThreads, L::kSmemBytes, st>>>(m[0], m[1], m[2], m[3], m[4], p);
+    kern<<<grid, kThreads, L::kSmemBytes, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], p);
     note_launch();
-    if (int rc = launch_status("dq256_kernel launch")) return rc;
+    return launch_status("dq256_kernel launch");
+  };
+  // With a fused Δ the dQ kernel writes the row statistics dK/dV reads, so
+  // it runs first.
+  int rc = BFA_OK;
+  if (p.fuse_delta) {
+    rc = run_dq();
+    if (rc == BFA_OK && (p.phases & BFA_BWD_PHASE_DKDV)) rc = run_dkdv();
+    return rc;
   }
-  return BFA_OK;
+  if (p.phases & BFA_BWD_PHASE_DKDV) rc = run_dkdv();
+  if (rc == BFA_OK && (p.phases & BFA_BWD_PHASE_DQ)) rc = run_dq();
+  return rc;
 }
 
 template <bool BF16>

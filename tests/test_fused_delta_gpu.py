@@ -1,4 +1,4 @@
-"""The dQ kernel's fused Δ prologue (head dims 64/128): a backward call with
+"""The dQ kernels' fused Δ prologue (head dims 64, 128, 256): a backward call with
 both the Δ and dQ phases has the dQ kernel form Δ = rowsum(O∘dO) and the
 row statistic lse2 itself, and write them for the dK/dV kernel that runs
 after it. Here the workspace rows it writes are compared with the separate Δ
@@ -31,6 +31,8 @@ CASES = [
     (torch.bfloat16, 128, 2, 2, 640, 256, dict(causal=True, alibi=True)),
     (torch.bfloat16, 128, 2, 1, 384, 200, dict(causal=True, k_pos_offset=200)),  # rows 0..199 see no key
     (torch.bfloat16, 64, 2, 2, 129, 129, dict(causal=True, soft_cap=20.0, sliding_window=50)),
+    (torch.bfloat16, 256, 4, 2, 520, 520, dict(causal=True, soft_cap=30.0)),
+    (torch.float16, 256, 2, 1, 300, 200, dict(causal=True, k_pos_offset=100)),
 ]
 
 
