@@ -6,7 +6,7 @@ scale 1/sqrt(128); q, k, v, grad_out ~ N(0,1) seeded, synthetic.
 
 One step = one forward + one backward of that layer through the library's
 C ABI (bfa_fwd, then the backward as two calls on one workspace: Δ and dQ --
-the dQ kernel forms Δ itself at head dims 64/128 -- and dK/dV, so each
+the dQ kernel forms Δ itself on the tcgen05 path -- and dK/dV, so each
 kernel is timed on its own). FLOPs count only unmasked (i, j) pairs,
 element-exact: 4·D per pair forward, 10·D backward.
 
@@ -280,7 +280,7 @@ def run_ours(args):
         out, l_ = nfa.npu_flash_attention_forward(q, k, v, return_lse=True, **kw)
         if ev:
             ev[1].record()
-        # Δ and dQ in one call: for head dims 64/128 the dQ kernel forms Δ
+        # Δ and dQ in one call: on the tcgen05 path the dQ kernel forms Δ
         # itself and runs first; dK/dV then reads Δ from the workspace.
         nfa.npu_flash_attention_backward(q, k, v, out, l_, do,
                                          _phases=bfa_lib.PHASE_DELTA | bfa_lib.PHASE_DQ,
@@ -333,7 +333,7 @@ def run_ours(args):
     peak_tf, _, peak_kind = peaks()
     pairs = pairs_per_head(cfg) * B * Hq
     # "dq_delta": the dQ kernel with Δ formed in its prologue (head dims
-    # 64/128), or the Δ pass then dQ (head dim 256); its FLOPs are dQ's.
+    # 64/128/256), or the Δ pass then dQ (other paths); its FLOPs are dQ's.
     kern_flops = {"fwd": 4.0 * D * pairs, "dq_delta": 6.0 * D * pairs, "dkdv": 8.0 * D * pairs}
     names = ["fwd", "dq_delta", "dkdv"]
     dom = max(range(3), key=lambda j: phase_ms[j])
