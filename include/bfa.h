@@ -140,7 +140,9 @@ typedef struct bfa_bwd_args {
   int64_t wait_timeout_ns; /* bound on any device-side wait; 0 = 1 second */
   uint32_t debug_flags;    /* 0 in production; BFA_DEBUG_* for tests */
   uint32_t phases;         /* 0 = all; else a mask of BFA_BWD_PHASE_* (same workspace
-                              across the calls, Δ first) -- lets a caller time each kernel */
+                              across the calls, Δ first) -- lets a caller time each kernel.
+                              A call with both DELTA and DQ on the tcgen05 path forms Δ
+                              inside the dQ kernel and runs dQ before dK/dV */
   uint32_t accumulate;     /* 0: dq/dk/dv have the input dtype and are overwritten.
                               1: dq/dk/dv are fp32 accumulators and the gradients are
                               added to them (blockwise / context-parallel backward: no
