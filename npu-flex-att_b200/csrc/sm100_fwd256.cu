@@ -328,9 +328,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int e = 0; e < 32; e += 2)
               m4[(e >> 1) & 3] = fmax3(m4[(e >> 1) & 3], __uint_as_float(r[ch][e]), __uint_as_float(r[ch][e + 1]));
         } else {
-          // Logits in base 2, formed in place: cap, ALiBi, mask.
-          auto form = [&](auto poly_tag) {
+          // Logits in base 2, formed in place: cap, ALiBi, mask. The cap's
+          // tanh: the odd Taylor series on the FMA pipe when every |s/cap| of
+          // the warp's step is <= 1/2 (to u^11), or <= 1/8 (to u^7, below
+          // 2e-9 relative there), else the closed form on MUFU; the mask
+          // select only on tiles that are not fully kept.
+          auto form = [&](auto poly_tag, auto tiny_tag, auto masked_tag) {
             constexpr bool POLY = decltype(poly_tag)::value;
+            constexpr bool TINY = decltype(tiny_tag)::value;
+            constexpr bool MASKED = decltype(masked_tag)::value;
 #pragma unroll
             for (int ch = 0; ch < 2; ++ch) {
 #pragma unroll
@@ -340,7 +346,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float2 raw2 = make_float2(__uint_as_float(r[ch][e]), __uint_as_float(r[ch][e + 1]));
                 if (CAP) {
                   const float2 u = __fmul2_rn(raw2, make_float2(cap_in, cap_in));
-                  if (POLY) {
+                  if (POLY && TINY) {
+                    const float2 z = __fmul2_rn(u, u);
+                    float2 q = __ffma2_rn(z, make_float2(c3, c3), make_float2(c2, c2));
+                    q = __ffma2_rn(z, q, make_float2(c1, c1));
+                    q = __ffma2_rn(z, q, make_float2(c0, c0));
+                    x2 = __fmul2_rn(u, q);
+                  } else if (POLY) {
                     const float2 z = __fmul2_rn(u, u);
                     float2 q = __ffma2_rn(z, make_float2(c5, c5), make_float2(c4, c4));
                     q = __ffma2_rn(z, q, make_float2(c3, c3));
@@ -359,15 +371,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int h = 0; h < 2; ++h) {
                   float x = xv[h];
                   if (ALIBI) x = fmaf(-slope2, (float)(c + h), x + abase);
-                  x = ((unsigned)(c + h - clo) < (unsigned)(chi - clo)) ? x : neg_inf();
+                  if (MASKED) x = ((unsigned)(c + h - clo) < (unsigned)(chi - clo)) ? x : neg_inf();
                   r[ch][e + h] = __float_as_uint(x);
                   m4[(e + h) & 3] = fmaxf(m4[(e + h) & 3], x);
                 }
               }
             }
           };
-          if (CAP && cap_small<32>(r[0], cap_in) && cap_small<32>(r[1], cap_in)) form(std::true_type{});
-          else form(std::false_type{});
+          int tier = 0;  // 2: |s/cap| <= 1/8 for the whole warp, 1: <= 1/2, 0: larger
+          if (CAP) {
+            float am = 0.f;
+#pragma unroll
+            for (int ch = 0; ch < 2; ++ch)
+#pragma unroll
+              for (int e = 0; e < 32; e += 2)
+                am = fmax3(am, fabsf(__uint_as_float(r[ch][e])), fabsf(__uint_as_float(r[ch][e + 1])));
+            am *= cap_in;
+            tier = __all_sync(0xffffffffu, am <= 0.125f) ? 2 : __all_sync(0xffffffffu, am <= 0.5f) ? 1 : 0;
+          }
+          using T_ = std::true_type;
+          using F_ = std::false_type;
+          if (full) {
+            if (tier == 2) form(T_{}, T_{}, F_{});
+            else if (tier == 1) form(T_{}, F_{}, F_{});
+            else form(F_{}, F_{}, F_{});
+          } else {
+            if (tier == 2) form(T_{}, T_{}, T_{});
+            else if (tier == 1) form(T_{}, F_{}, T_{});
+            else form(F_{}, F_{}, T_{});
+          }
         }
         pm = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
         if (!store_x) pm *= sl2;

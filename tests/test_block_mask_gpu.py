@@ -100,8 +100,10 @@ def test_block_diagonal_mask_is_separate_calls():
 def test_sparse_mask_skips_work(d):
     """A mask that keeps the diagonal block row only must not cost the dense
     time: the kernels' loops visit the blocks that are on. (Timing bound is
-    loose: half the dense causal forward.)"""
-    B, H, S = 1, 16, 8192
+    loose: half the dense causal forward. S = 16384, so that the dense work,
+    quadratic in S, is well above the per-tile cost both share: loading Q and
+    storing O and the LSE.)"""
+    B, H, S = 1, 16, 16384
     q = torch.randn(B, H, S, d, device=DEV, dtype=torch.bfloat16)
     k = torch.randn(B, H, S, d, device=DEV, dtype=torch.bfloat16)
     v = torch.randn_like(k)
