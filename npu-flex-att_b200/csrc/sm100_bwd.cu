@@ -332,10 +332,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(tSb + 32 * half, sr);
       tmem_ld_wait();
       tmem_ld32(tDb + 32 * half, dr);
-      const bool small = CAP && cap_small<32>(sr, cap_in);
+      const int tier = CAP ? cap_tier<32>(sr, cap_in) : 0;
       auto step = [&](auto masked, auto small_tag) {
         constexpr bool MASKED = decltype(masked)::value;
-        constexpr bool SMALL = decltype(small_tag)::value;
+        constexpr int TIER = decltype(small_tag)::value;
         float pr[32];
         float tt[CAP ? 32 : 1];
         uint32_t ppk[16];
@@ -366,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float raw = __uint_as_float(sr[c + h]);
               float pv, t = 0.f;
               if (CAP || ALIBI) {
-                float x = logit2<CAP, SMALL>(raw, sl2, cap_in, cap_out, &t);
+                float x = logit2<CAP, TIER>(raw, sl2, cap_in, cap_out, &t);
                 if (ALIBI) x += fmaxf(ba, fmaf(slope2, (float)cc, bq));
                 pv = ex2(x - lse_c[h]);
               } else {
@@ -413,12 +413,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_st16(tDb + 32 * half, dpk);
       };
-      if (small) {
-        if (full) step(std::false_type{}, std::true_type{});
-        else step(std::true_type{}, std::true_type{});
+      using I2 = std::integral_constant<int, 2>;
+      using I1 = std::integral_constant<int, 1>;
+      using I0 = std::integral_constant<int, 0>;
+      if (tier == 2) {
+        if (full) step(std::false_type{}, I2{});
+        else step(std::true_type{}, I2{});
+      } else if (tier == 1) {
+        if (full) step(std::false_type{}, I1{});
+        else step(std::true_type{}, I1{});
       } else {
-        if (full) step(std::false_type{}, std::false_type{});
-        else step(std::true_type{}, std::false_type{});
+        if (full) step(std::false_type{}, I0{});
+        else step(std::true_type{}, I0{});
       }
       tmem_st_wait();
       tc_fence_before();
@@ -817,10 +823,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kSRead));
       uint8_t* ds_row = smem + L::kOffDS + eg * (kRows * 128);  // this warpgroup's 64 keys
-      const bool small = CAP && cap_small<64>(sr, cap_in);
+      const int tier = CAP ? cap_tier<64>(sr, cap_in) : 0;
       auto step = [&](auto masked, auto small_tag) {
         constexpr bool MASKED = decltype(masked)::value;
-        constexpr bool SMALL = decltype(small_tag)::value;
+        constexpr int TIER = decltype(small_tag)::value;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           uint32_t dr[32];
@@ -863,7 +869,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               float pr, t = 0.f;
               float x;
               if (CAP || ALIBI) {
-                x = logit2<CAP, SMALL>(raw, sl2, cap_in, cap_out, &t);
+                x = logit2<CAP, TIER>(raw, sl2, cap_in, cap_out, &t);
                 if (ALIBI) x = fmaf(-slope2, (float)cc, x + abase);
                 x -= lse2;
               } else {
@@ -888,8 +894,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         return true;
       };
-      if (small) ok = full ? step(std::false_type{}, std::true_type{}) : step(std::true_type{}, std::true_type{});
-      else ok = full ? step(std::false_type{}, std::false_type{}) : step(std::true_type{}, std::false_type{});
+      using I2 = std::integral_constant<int, 2>;
+      using I1 = std::integral_constant<int, 1>;
+      using I0 = std::integral_constant<int, 0>;
+      if (tier == 2) ok = full ? step(std::false_type{}, I2{}) : step(std::true_type{}, I2{});
+      else if (tier == 1) ok = full ? step(std::false_type{}, I1{}) : step(std::true_type{}, I1{});
+      else ok = full ? step(std::false_type{}, I0{}) : step(std::true_type{}, I0{});
       if (!ok) break;
       fence_async_shared();
       __syncwarp();

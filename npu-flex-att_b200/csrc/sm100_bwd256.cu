@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t pk[16];
       auto body = [&](auto masked, auto small_tag) {
         constexpr bool MASKED = decltype(masked)::value;
-        constexpr bool SMALL = decltype(small_tag)::value;
+        constexpr int TIER = decltype(small_tag)::value;
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
           float v2[2];
@@ -382,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int cc = 32 * eg + c + h;
             const float raw = __uint_as_float(sr[c + h]);
             float t = 0.f;
-            float x = (CAP || ALIBI) ? logit2<CAP, SMALL>(raw, sl2, cap_in, cap_out, &t) : raw * sl2;
+            float x = (CAP || ALIBI) ? logit2<CAP, TIER>(raw, sl2, cap_in, cap_out, &t) : raw * sl2;
             if (ALIBI) x += fmaxf(ba, fmaf(slope2, (float)cc, bq));
             float pr = ex2(x - rowv[cc]);
             if (MASKED) pr = ((unsigned)(cc - clo) < (unsigned)(chi - clo)) ? pr : 0.f;
@@ -397,12 +397,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           pk[c / 2] = pack2<BF16>(v2[0], v2[1]);
         }
       };
-      if (CAP && cap_small<32>(sr, cap_in)) {
-        if (full) body(std::false_type{}, std::true_type{});
-        else body(std::true_type{}, std::true_type{});
+      const int tier = CAP ? cap_tier<32>(sr, cap_in) : 0;
+      using I2 = std::integral_constant<int, 2>;
+      using I1 = std::integral_constant<int, 1>;
+      using I0 = std::integral_constant<int, 0>;
+      if (tier == 2) {
+        if (full) body(std::false_type{}, I2{});
+        else body(std::true_type{}, I2{});
+      } else if (tier == 1) {
+        if (full) body(std::false_type{}, I1{});
+        else body(std::true_type{}, I1{});
       } else {
-        if (full) body(std::false_type{}, std::false_type{});
-        else body(std::true_type{}, std::false_type{});
+        if (full) body(std::false_type{}, I0{});
+        else body(std::true_type{}, I0{});
       }
       // The row statistics are in registers' use: release the entry.
       __syncwarp();
@@ -765,7 +772,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t dpk[16];
       auto body = [&](auto masked, auto small_tag) {
         constexpr bool MASKED = decltype(masked)::value;
-        constexpr bool SMALL = decltype(small_tag)::value;
+        constexpr int TIER = decltype(small_tag)::value;
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
           float ds2[2];
@@ -774,7 +781,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int cc = 32 * eg + c + h;
             const float raw = __uint_as_float(sr[c + h]);
             float t = 0.f;
-            float x = (CAP || ALIBI) ? logit2<CAP, SMALL>(raw, sl2, cap_in, cap_out, &t) : raw * sl2;
+            float x = (CAP || ALIBI) ? logit2<CAP, TIER>(raw, sl2, cap_in, cap_out, &t) : raw * sl2;
             if (ALIBI) x = fmaf(-slope2, (float)cc, x + abase);
             float pr = ex2(x - lse2);
             if (MASKED) pr = ((unsigned)(cc - clo) < (unsigned)(chi - clo)) ? pr : 0.f;
@@ -785,12 +792,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           dpk[c / 2] = pack2<BF16>(ds2[0], ds2[1]);
         }
       };
-      if (CAP && cap_small<32>(sr, cap_in)) {
-        if (full) body(std::false_type{}, std::true_type{});
-        else body(std::true_type{}, std::true_type{});
+      const int tier = CAP ? cap_tier<32>(sr, cap_in) : 0;
+      using I2 = std::integral_constant<int, 2>;
+      using I1 = std::integral_constant<int, 1>;
+      using I0 = std::integral_constant<int, 0>;
+      if (tier == 2) {
+        if (full) body(std::false_type{}, I2{});
+        else body(std::true_type{}, I2{});
+      } else if (tier == 1) {
+        if (full) body(std::false_type{}, I1{});
+        else body(std::true_type{}, I1{});
       } else {
-        if (full) body(std::false_type{}, std::false_type{});
-        else body(std::true_type{}, std::false_type{});
+        if (full) body(std::false_type{}, I0{});
+        else body(std::true_type{}, I0{});
       }
       // dS of this warpgroup's 32 keys -> 16-byte chunks [4h, 4h + 4) of this
       // row of the swizzled [128 rows][64 keys] tile, once dQ(j-1) has read it.

@@ -38,14 +38,14 @@ __device__ __forceinline__ float2 unpack2(uint32_t w) {
 }
 
 // Logit in the base-2 domain: (cap·tanh(s·scale/cap) or s·scale)·log2(e).
-// `t` receives tanh(s·scale/cap) for the soft-cap chain. SMALL selects
-// tanh_small (every |s·scale/cap| of the warp's step is <= 1/2, see
-// cap_small), else tanh_any.
-template <bool CAP, bool SMALL = false>
+// `t` receives tanh(s·scale/cap) for the soft-cap chain. TIER (cap_tier)
+// selects tanh_tiny (every |s·scale/cap| of the warp's step is <= 1/8, 2),
+// tanh_small (<= 1/2, 1) or tanh_any (0).
+template <bool CAP, int TIER = 0>
 __device__ __forceinline__ float logit2(float raw, float sl2, float cap_in, float cap_out, float* t) {
   if (CAP) {
     const float u = raw * cap_in;
-    const float th = SMALL ? tanh_small(u) : tanh_any(u);
+    const float th = TIER == 2 ? tanh_tiny(u) : TIER == 1 ? tanh_small(u) : tanh_any(u);
     *t = th;
     return cap_out * th;
   }

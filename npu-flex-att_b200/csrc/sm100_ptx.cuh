@@ -460,9 +460,31 @@ __device__ __forceinline__ float tanh_small(float x) {
   return x * q;
 }
 
+// The same series to x^7: truncation below 2e-9 relative for |x| <= 1/8.
+__device__ __forceinline__ float tanh_tiny(float x) {
+  const float z = x * x;
+  float q = fmaf(z, kTanhT3, kTanhT2);
+  q = fmaf(z, q, kTanhT1);
+  q = fmaf(z, q, 1.0f);
+  return x * q;
+}
+
 __device__ __forceinline__ float tanh_any(float x) {
   const float e = ex2(fminf(2.0f * 1.4426950408889634f * fabsf(x), 126.0f));
   return copysignf(1.0f - 2.0f * rcp(1.0f + e), x);
+}
+
+// Which tanh serves a warp's step (warp-uniform): 2 (tanh_tiny) when every
+// |raw·cap_in| of the warp's n raw logits is <= 1/8, 1 (tanh_small) when <=
+// 1/2, else 0 (tanh_any).
+template <int N>
+__device__ __forceinline__ int cap_tier(const uint32_t* raw, float cap_in) {
+  float am = 0.f;
+#pragma unroll
+  for (int e = 0; e < N; e += 2)
+    am = fmax3(am, fabsf(__uint_as_float(raw[e])), fabsf(__uint_as_float(raw[e + 1])));
+  am *= cap_in;
+  return __all_sync(0xffffffffu, am <= 0.125f) ? 2 : __all_sync(0xffffffffu, am <= 0.5f) ? 1 : 0;
 }
 
 // True when |raw·cap_in| <= 1/2 for all n raw logits of every thread of the
