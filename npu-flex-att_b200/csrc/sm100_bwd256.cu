@@ -377,6 +377,31 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
           float v2[2];
+          if (CAP && !ALIBI) {
+            // Soft-cap without ALiBi: both keys in packed instructions.
+            const int cc = 32 * eg + c;
+            float2 th;
+            const float2 x = cap_logit2x2<TIER>(make_float2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])),
+                                                 cap_in, cap_out, &th);
+            const float2 l2 = *reinterpret_cast<const float2*>(rowv + cc);
+            float pr0 = ex2(x.x - l2.x), pr1 = ex2(x.y - l2.y);
+            if (MASKED) {
+              pr0 = ((unsigned)(cc - clo) < (unsigned)(chi - clo)) ? pr0 : 0.f;
+              pr1 = ((unsigned)(cc + 1 - clo) < (unsigned)(chi - clo)) ? pr1 : 0.f;
+            }
+            if (DK) {
+              const float2 d2 = *reinterpret_cast<const float2*>(rowv + 64 + cc);
+              const float2 dd = __fadd2_rn(make_float2(__uint_as_float(dr[c]), __uint_as_float(dr[c + 1])),
+                                           make_float2(-d2.x, -d2.y));
+              float2 ds = __fmul2_rn(__fmul2_rn(make_float2(pr0, pr1), dd), make_float2(p.scale, p.scale));
+              ds = __fmul2_rn(ds, __ffma2_rn(make_float2(-th.x, -th.y), th, make_float2(1.f, 1.f)));
+              v2[0] = ds.x;
+              v2[1] = ds.y;
+            } else {
+              v2[0] = pr0;
+              v2[1] = pr1;
+            }
+          } else {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int cc = 32 * eg + c + h;
@@ -393,6 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               v2[h] = pr;
             }
+          }
           }
           pk[c / 2] = pack2<BF16>(v2[0], v2[1]);
         }
@@ -777,6 +803,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 32; c += 2) {
           float ds2[2];
 #pragma unroll
+          if (CAP && !ALIBI) {
+            // Soft-cap without ALiBi: both keys in packed instructions.
+            const int cc = 32 * eg + c;
+            float2 th;
+            const float2 x = cap_logit2x2<TIER>(make_float2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])),
+                                                 cap_in, cap_out, &th);
+            float pr0 = ex2(x.x - lse2), pr1 = ex2(x.y - lse2);
+            if (MASKED) {
+              pr0 = ((unsigned)(cc - clo) < (unsigned)(chi - clo)) ? pr0 : 0.f;
+              pr1 = ((unsigned)(cc + 1 - clo) < (unsigned)(chi - clo)) ? pr1 : 0.f;
+            }
+            const float2 dd = __fadd2_rn(make_float2(__uint_as_float(dr[c]), __uint_as_float(dr[c + 1])),
+                                         make_float2(-dlt, -dlt));
+            float2 ds = __fmul2_rn(__fmul2_rn(make_float2(pr0, pr1), dd), make_float2(p.scale, p.scale));
+            ds = __fmul2_rn(ds, __ffma2_rn(make_float2(-th.x, -th.y), th, make_float2(1.f, 1.f)));
+            ds2[0] = ds.x;
+            ds2[1] = ds.y;
+          } else {
+#pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int cc = 32 * eg + c + h;
             const float raw = __uint_as_float(sr[c + h]);
@@ -788,6 +833,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float ds = pr * (__uint_as_float(dr[c + h]) - dlt) * p.scale;
             if (CAP) ds *= (1.f - t * t);
             ds2[h] = ds;
+          }
           }
           dpk[c / 2] = pack2<BF16>(ds2[0], ds2[1]);
         }
