@@ -359,6 +359,26 @@ __global__ void __launch_bounds__(kThreads, 1)
               pr[c + h] = pr0;
               pr[c + h + 1] = pr1;
             }
+          } else if (CAP && !ALIBI) {
+            // Soft-cap without ALiBi: two keys per packed instruction.
+#pragma unroll
+            for (int h = 0; h < 4; h += 2) {
+              float2 th;
+              const float2 x = cap_logit2x2<TIER>(make_float2(__uint_as_float(sr[c + h]), __uint_as_float(sr[c + h + 1])),
+                                                   cap_in, cap_out, &th);
+              float pr0 = ex2(x.x - lse_c[h]), pr1 = ex2(x.y - lse_c[h + 1]);
+              if (MASKED) {
+                const int cc = 32 * half + c + h;
+                pr0 = ((unsigned)(cc - clo) < (unsigned)(chi - clo)) ? pr0 : 0.f;
+                pr1 = ((unsigned)(cc + 1 - clo) < (unsigned)(chi - clo)) ? pr1 : 0.f;
+              }
+              pr[c + h] = pr0;
+              pr[c + h + 1] = pr1;
+              if (CAP) {
+                tt[c + h] = th.x;
+                tt[c + h + 1] = th.y;
+              }
+            }
           } else {
 #pragma unroll
             for (int h = 0; h < 4; ++h) {
@@ -397,6 +417,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                                            make_float2(-dl_c[h], -dl_c[h + 1]));
               const float2 ds = __fmul2_rn(__fmul2_rn(make_float2(pr[c + h], pr[c + h + 1]), dd),
                                            make_float2(p.scale, p.scale));
+              ds4[h] = ds.x;
+              ds4[h + 1] = ds.y;
+            }
+          } else if (CAP && !ALIBI) {
+#pragma unroll
+            for (int h = 0; h < 4; h += 2) {
+              const float2 dd = __fadd2_rn(make_float2(__uint_as_float(dr[c + h]), __uint_as_float(dr[c + h + 1])),
+                                           make_float2(-dl_c[h], -dl_c[h + 1]));
+              const float2 th = make_float2(tt[c + h], tt[c + h + 1]);
+              float2 ds = __fmul2_rn(__fmul2_rn(make_float2(pr[c + h], pr[c + h + 1]), dd),
+                                     make_float2(p.scale, p.scale));
+              ds = __fmul2_rn(ds, __ffma2_rn(make_float2(-th.x, -th.y), th, make_float2(1.f, 1.f)));
               ds4[h] = ds.x;
               ds4[h + 1] = ds.y;
             }
@@ -856,6 +888,27 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
               const float2 ds = __fmul2_rn(make_float2(pr0, pr1),
                                            __ffma2_rn(make_float2(__uint_as_float(dr[c]), __uint_as_float(dr[c + 1])), sc2, nds2));
+              dpk[c / 2] = pack2<BF16>(ds.x, ds.y);
+            }
+          } else if (CAP && !ALIBI) {
+            // Soft-cap without ALiBi: two keys per packed instruction;
+            // dS = P (dP - Δ)·scale·(1 - tanh²).
+            const float2 sc2 = make_float2(p.scale, p.scale), ndl2 = make_float2(-dlt, -dlt);
+#pragma unroll
+            for (int c = 0; c < 32; c += 2) {
+              float2 th;
+              const float2 x = cap_logit2x2<TIER>(make_float2(__uint_as_float(sr[32 * half + c]),
+                                                               __uint_as_float(sr[32 * half + c + 1])),
+                                                   cap_in, cap_out, &th);
+              float pr0 = ex2(x.x - lse2), pr1 = ex2(x.y - lse2);
+              if (MASKED) {
+                const int cc = 64 * eg + 32 * half + c;
+                pr0 = ((unsigned)(cc - clo) < (unsigned)(chi - clo)) ? pr0 : 0.f;
+                pr1 = ((unsigned)(cc + 1 - clo) < (unsigned)(chi - clo)) ? pr1 : 0.f;
+              }
+              const float2 dd = __fadd2_rn(make_float2(__uint_as_float(dr[c]), __uint_as_float(dr[c + 1])), ndl2);
+              float2 ds = __fmul2_rn(__fmul2_rn(make_float2(pr0, pr1), dd), sc2);
+              ds = __fmul2_rn(ds, __ffma2_rn(make_float2(-th.x, -th.y), th, make_float2(1.f, 1.f)));
               dpk[c / 2] = pack2<BF16>(ds.x, ds.y);
             }
           } else
