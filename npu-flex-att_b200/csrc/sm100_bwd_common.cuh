@@ -53,34 +53,6 @@ __device__ __forceinline__ float logit2(float raw, float sl2, float cap_in, floa
   return raw * sl2;
 }
 
-// logit2 for a pair of raw logits with a soft-cap and no ALiBi, in packed
-// f32x2 instructions (half the issue slots of two scalar calls): returns
-// cap·tanh(raw·cap_in)·log2(e) and the two tanh values in *th.
-template <int TIER>
-__device__ __forceinline__ float2 cap_logit2x2(float2 raw, float cap_in, float cap_out, float2* th) {
-  const float2 u = __fmul2_rn(raw, make_float2(cap_in, cap_in));
-  float2 t;
-  if (TIER == 2) {
-    const float2 z = __fmul2_rn(u, u);
-    float2 q = __ffma2_rn(z, make_float2(kTanhT3, kTanhT3), make_float2(kTanhT2, kTanhT2));
-    q = __ffma2_rn(z, q, make_float2(kTanhT1, kTanhT1));
-    q = __ffma2_rn(z, q, make_float2(1.f, 1.f));
-    t = __fmul2_rn(u, q);
-  } else if (TIER == 1) {
-    const float2 z = __fmul2_rn(u, u);
-    float2 q = __ffma2_rn(z, make_float2(kTanhT5, kTanhT5), make_float2(kTanhT4, kTanhT4));
-    q = __ffma2_rn(z, q, make_float2(kTanhT3, kTanhT3));
-    q = __ffma2_rn(z, q, make_float2(kTanhT2, kTanhT2));
-    q = __ffma2_rn(z, q, make_float2(kTanhT1, kTanhT1));
-    q = __ffma2_rn(z, q, make_float2(1.f, 1.f));
-    t = __fmul2_rn(u, q);
-  } else {
-    t = make_float2(tanh_any(u.x), tanh_any(u.y));
-  }
-  *th = t;
-  return __fmul2_rn(t, make_float2(cap_out, cap_out));
-}
-
 // Read a TMEM row of D fp32 columns, convert, and write it into a staging
 // area of D/64 swizzled sub-tiles of 128 rows (for a TMA store).
 template <int D, bool BF16>

@@ -341,37 +341,65 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int e = 0; e < 32; e += 2)
               m4[(e >> 1) & 3] = fmax3(m4[(e >> 1) & 3], __uint_as_float(r[ch][e]), __uint_as_float(r[ch][e + 1]));
         } else {
-          // Soft-cap tanh: tanh_small on the FMA pipe when every raw logit
-          // of the warp's step has |s/cap| <= 1/2, else tanh_any.
-          auto form = [&](auto small_tag) {
-            constexpr bool SMALL = decltype(small_tag)::value;
+          // Logits in base 2, formed in place: cap, ALiBi, mask. The cap's
+          // tanh (cap_tier, warp-uniform per step): the odd Taylor series on
+          // the FMA pipe when every |s/cap| of the warp's step is <= 1/8 (to
+          // u^7) or <= 1/2 (to u^11), else the closed form on MUFU; without
+          // ALiBi two keys per packed instruction. The mask select runs only
+          // on tiles that are not fully kept.
+          auto form = [&](auto tier_tag, auto masked_tag) {
+            constexpr int TIER = decltype(tier_tag)::value;
+            constexpr bool MASKED = decltype(masked_tag)::value;
 #pragma unroll
             for (int ch = 0; ch < kBN / 32; ++ch) {
 #pragma unroll
-              for (int e = 0; e < 32; ++e) {
+              for (int e = 0; e < 32; e += 2) {
                 const int c = 32 * ch + e;
-                const float raw = __uint_as_float(r[ch][e]);
-                float x = raw * sl2;
-                if (CAP) x = cap_out * (SMALL ? tanh_small(raw * cap_in) : tanh_any(raw * cap_in));
-                if (ALIBI) x = fmaf(-slope2, (float)c, x + abase);
-                x = ((unsigned)(c - clo) < (unsigned)(chi - clo)) ? x : neg_inf();
-                r[ch][e] = __float_as_uint(x);
-                m4[e & 3] = fmaxf(m4[e & 3], x);
+                const float2 raw2 = make_float2(__uint_as_float(r[ch][e]), __uint_as_float(r[ch][e + 1]));
+                float xv[2];
+                if (CAP && !ALIBI) {
+                  float2 th;
+                  const float2 x2 = cap_logit2x2<TIER>(raw2, cap_in, cap_out, &th);
+                  xv[0] = x2.x;
+                  xv[1] = x2.y;
+                } else {
+#pragma unroll
+                  for (int h = 0; h < 2; ++h) {
+                    const float raw = h ? raw2.y : raw2.x;
+                    float x = raw * sl2;
+                    if (CAP) {
+                      const float u = raw * cap_in;
+                      x = cap_out * (TIER == 2 ? tanh_tiny(u) : TIER == 1 ? tanh_small(u) : tanh_any(u));
+                    }
+                    if (ALIBI) x = fmaf(-slope2, (float)(c + h), x + abase);
+                    xv[h] = x;
+                  }
+                }
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  float x = xv[h];
+                  if (MASKED) x = ((unsigned)(c + h - clo) < (unsigned)(chi - clo)) ? x : neg_inf();
+                  r[ch][e + h] = __float_as_uint(x);
+                  m4[(e + h) & 3] = fmaxf(m4[(e + h) & 3], x);
+                }
               }
             }
           };
-          bool small = false;
-          if (CAP) {
-            float am = 0.f;
-#pragma unroll
-            for (int ch = 0; ch < kBN / 32; ++ch)
-#pragma unroll
-              for (int e = 0; e < 32; e += 2)
-                am = fmax3(am, fabsf(__uint_as_float(r[ch][e])), fabsf(__uint_as_float(r[ch][e + 1])));
-            small = __all_sync(0xffffffffu, am * cap_in <= 0.5f);
+          const int tier = CAP ? cap_tier<kBN>(&r[0][0], cap_in) : 0;
+          using I2 = std::integral_constant<int, 2>;
+          using I1 = std::integral_constant<int, 1>;
+          using I0 = std::integral_constant<int, 0>;
+          // (Plain logits reach here on a full tile only with scale <= 0:
+          // they keep the one masked form.)
+          if ((CAP || ALIBI) && full) {
+            if (tier == 2) form(I2{}, std::false_type{});
+            else if (tier == 1) form(I1{}, std::false_type{});
+            else form(I0{}, std::false_type{});
+          } else {
+            if (tier == 2) form(I2{}, std::true_type{});
+            else if (tier == 1) form(I1{}, std::true_type{});
+            else form(I0{}, std::true_type{});
           }
-          if (small) form(std::true_type{});
-          else form(std::false_type{});
         }
         mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
         if (!store_x) mx *= sl2;

@@ -487,15 +487,32 @@ __device__ __forceinline__ int cap_tier(const uint32_t* raw, float cap_in) {
   return __all_sync(0xffffffffu, am <= 0.125f) ? 2 : __all_sync(0xffffffffu, am <= 0.5f) ? 1 : 0;
 }
 
-// True when |raw·cap_in| <= 1/2 for all n raw logits of every thread of the
-// warp (warp-uniform), i.e. when tanh_small serves the whole step.
-template <int N>
-__device__ __forceinline__ bool cap_small(const uint32_t* raw, float cap_in) {
-  float am = 0.f;
-#pragma unroll
-  for (int e = 0; e < N; e += 2)
-    am = fmax3(am, fabsf(__uint_as_float(raw[e])), fabsf(__uint_as_float(raw[e + 1])));
-  return __all_sync(0xffffffffu, am * cap_in <= 0.5f);
+// logit2 for a pair of raw logits with a soft-cap and no ALiBi, in packed
+// f32x2 instructions (half the issue slots of two scalar calls): returns
+// cap·tanh(raw·cap_in)·log2(e) and the two tanh values in *th.
+template <int TIER>
+__device__ __forceinline__ float2 cap_logit2x2(float2 raw, float cap_in, float cap_out, float2* th) {
+  const float2 u = __fmul2_rn(raw, make_float2(cap_in, cap_in));
+  float2 t;
+  if (TIER == 2) {
+    const float2 z = __fmul2_rn(u, u);
+    float2 q = __ffma2_rn(z, make_float2(kTanhT3, kTanhT3), make_float2(kTanhT2, kTanhT2));
+    q = __ffma2_rn(z, q, make_float2(kTanhT1, kTanhT1));
+    q = __ffma2_rn(z, q, make_float2(1.f, 1.f));
+    t = __fmul2_rn(u, q);
+  } else if (TIER == 1) {
+    const float2 z = __fmul2_rn(u, u);
+    float2 q = __ffma2_rn(z, make_float2(kTanhT5, kTanhT5), make_float2(kTanhT4, kTanhT4));
+    q = __ffma2_rn(z, q, make_float2(kTanhT3, kTanhT3));
+    q = __ffma2_rn(z, q, make_float2(kTanhT2, kTanhT2));
+    q = __ffma2_rn(z, q, make_float2(kTanhT1, kTanhT1));
+    q = __ffma2_rn(z, q, make_float2(1.f, 1.f));
+    t = __fmul2_rn(u, q);
+  } else {
+    t = make_float2(tanh_any(u.x), tanh_any(u.y));
+  }
+  *th = t;
+  return __fmul2_rn(t, make_float2(cap_out, cap_out));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
