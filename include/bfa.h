@@ -12,9 +12,11 @@
  *                     + flash_attn_bwd_dkdv_kernel launch (:714-732)
  *                     + host GQA sum of dK/dV (:735-737)
  *   bfa_merge_partial  (no reference counterpart: LSE merge of two partial
- *                     attention results, used by the context-parallel ring;
- *                     the idea follows the reference's unused split-KV reduce
- *                     kernel, npu_flash_attention.py:255-293)
+ *                     attention results in memory; the context-parallel ring
+ *                     has bfa_fwd merge its own result instead, with
+ *                     bfa_fwd_args.accumulate. The idea follows the
+ *                     reference's unused split-KV reduce kernel,
+ *                     npu_flash_attention.py:255-293)
  *
  * Conventions
  *  - Plain C: pointers, sizes, int64 element strides. No torch or CUDA types;
@@ -47,7 +49,7 @@
 extern "C" {
 #endif
 
-#define BFA_ABI_VERSION 4
+#define BFA_ABI_VERSION 5
 
 typedef enum bfa_dtype {
   BFA_DTYPE_F32 = 0,
@@ -126,6 +128,14 @@ typedef struct bfa_fwd_args {
                               decoding path (NULL: the regular forward runs) */
   size_t workspace_bytes;  /* size of `workspace`; the decoding path needs
                               bfa_fwd_workspace_bytes(problem) */
+  uint32_t accumulate;     /* 0: `o` has the input dtype and is overwritten, `lse` is
+                              written. 1: `o` is an fp32 running output and `lse` its
+                              running LSE (-inf: no key yet); the call merges its own
+                              result into both in its epilogue,
+                                lse' = logaddexp(lse, lse_call),
+                                o'   = o·e^(lse - lse') + o_call·e^(lse_call - lse'),
+                              as bfa_merge_partial does, with no partial result in
+                              memory (one block of a context-parallel ring). */
 } bfa_fwd_args;
 
 typedef struct bfa_bwd_args {

@@ -14,7 +14,7 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libbfa.so")
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 DEBUG_INJECT_STALL = 1
@@ -51,7 +51,8 @@ class FwdArgs(ctypes.Structure):
     _fields_ = [("q", Tensor), ("k", Tensor), ("v", Tensor), ("o", Tensor),
                 ("lse", ctypes.c_void_p), ("status", ctypes.c_void_p),
                 ("wait_timeout_ns", ctypes.c_int64), ("debug_flags", ctypes.c_uint32),
-                ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t)]
+                ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+                ("accumulate", ctypes.c_uint32)]
 
 
 class BwdArgs(ctypes.Structure):

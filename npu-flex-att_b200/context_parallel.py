@@ -11,8 +11,9 @@ every rank then owns the same amount of work.
 
 Forward. At step t = 0..N-1 rank r holds the K/V shard of rank (r - t) mod N;
 for each of its two query chunks and each visiting key chunk that the mask
-does not hide entirely it runs one attention call and folds the partial
-(O, LSE) into fp32 accumulators with ``bfa_merge_partial``:
+does not hide entirely it runs one attention call whose epilogue folds its
+result into the fp32 running (O, LSE) of the query chunk
+(``bfa_fwd_args.accumulate``; no partial result goes through memory):
     lse' = logaddexp(lse_acc, lse_p),  o' = o_acc e^(lse_acc-lse') + o_p e^(lse_p-lse').
 The next K/V shard is in flight (NCCL send/recv) while the current one is used.
 
@@ -125,6 +126,15 @@ class CudaBlockOps:
             alibi_slope=m.alibi_slope, scale=m.scale, soft_cap=m.soft_cap,
             return_lse=True, q_pos_offset=q_off, k_pos_offset=k_off)
 
+    def fwd_merge(self, o_acc, lse_acc, q, k, v, q_off, k_off, m: MaskArgs):
+        """One block's forward merged into the fp32 running (o_acc, lse_acc)
+        by the forward kernel's epilogue: no partial (O, LSE) is written."""
+        _nfa.npu_flash_attention_forward(
+            q, k, v, causal=m.causal, sliding_window=m.sliding_window,
+            alibi_slope=m.alibi_slope, scale=m.scale, soft_cap=m.soft_cap,
+            return_lse=True, q_pos_offset=q_off, k_pos_offset=k_off,
+            _merge_into=(o_acc, lse_acc))
+
     def merge(self, o_acc, lse_acc, o_part, lse_part):
         """In place: (o_acc, lse_acc) <- LSE merge with (o_part, lse_part)."""
         B, H, S, D = o_acc.shape
@@ -193,9 +203,8 @@ def ring_forward(q, k, v, rank: int, world: int, m: MaskArgs, ops):
             for ib, kb in enumerate(lay.chunks(src)):
                 if not block_visible(qa, kb, C, m):
                     continue
-                o_p, lse_p = ops.fwd(q.narrow(2, ia * C, C), kc.narrow(2, ib * C, C),
-                                     vc.narrow(2, ib * C, C), qa * C, kb * C, m)
-                ops.merge(o_acc[ia], lse_acc[ia], o_p, lse_p)
+                ops.fwd_merge(o_acc[ia], lse_acc[ia], q.narrow(2, ia * C, C),
+                              kc.narrow(2, ib * C, C), vc.narrow(2, ib * C, C), qa * C, kb * C, m)
         if t + 1 < world:
             kv = yield ("finish",)
     return torch.cat(o_acc, dim=2).to(q.dtype), torch.cat(lse_acc, dim=2)

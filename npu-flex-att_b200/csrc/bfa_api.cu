@@ -125,11 +125,14 @@ int bfa_fwd(const bfa_problem* pr, const bfa_fwd_args* a, void* stream) {
   p.status = a->status;
   p.timeout_ns = a->wait_timeout_ns > 0 ? (uint64_t)a->wait_timeout_ns : 1000000000ull;
   p.debug_flags = a->debug_flags;
+  if (a->accumulate > 1) return BFA_ERR_INVALID_ARGUMENT;
+  p.out_acc = a->accumulate;
   cudaStream_t st = (cudaStream_t)stream;
   // Few query rows per KV head (decoding): the split-KV path streams K/V once
   // per KV head across the whole GPU. The fault-injection flags exercise the
-  // tcgen05 kernels' bounded waits, so they keep the regular path.
-  if (p.debug_flags == 0 && a->workspace && bfa::decode_eligible(p, pr->dtype)) {
+  // tcgen05 kernels' bounded waits, so they keep the regular path, and so
+  // does a merging call (the decoding path writes its own output).
+  if (p.debug_flags == 0 && !p.out_acc && a->workspace && bfa::decode_eligible(p, pr->dtype)) {
     const int rc = bfa::decode_fwd(p, pr->dtype, a->workspace, a->workspace_bytes, st);
     if (rc != -1) return rc;
   }

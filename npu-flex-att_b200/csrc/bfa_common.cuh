@@ -55,7 +55,29 @@ struct Params {
   // backward: the dQ kernel forms Δ and lse2 of its rows itself and writes
   // them for the dK/dV kernel that runs after it (no separate Δ pass).
   uint32_t fuse_delta;
+  // forward: `o` is an fp32 running output and `lse` its running LSE; the
+  // epilogue merges the call's result into both (merge_weights).
+  uint32_t out_acc;
 };
+
+// The LSE merge of a block's result (LSE lp) into a running one (LSE la):
+// ln = logaddexp(la, lp), the running output's weight wa = e^(la − ln) and the
+// block's wp = e^(lp − ln); both weights 0 and ln = −inf when neither has a key.
+struct MergeWeights {
+  float wa, wp, ln;
+};
+
+__device__ __forceinline__ MergeWeights merge_weights(float la, float lp) {
+  MergeWeights w{0.f, 0.f, neg_inf()};
+  const float mx = fmaxf(la, lp);
+  if (mx != neg_inf()) {
+    const float ea = expf(la - mx), ep = expf(lp - mx);
+    w.ln = mx + logf(ea + ep);
+    w.wa = expf(la - w.ln);
+    w.wp = expf(lp - w.ln);
+  }
+  return w;
+}
 
 template <typename T> __device__ __forceinline__ float to_f32(T x);
 template <> __device__ __forceinline__ float to_f32<float>(float x) { return x; }

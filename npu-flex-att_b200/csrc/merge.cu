@@ -1,9 +1,10 @@
 // merge.cu -- LSE merge of a partial attention result into a running one.
 //
 // lse' = logaddexp(lse_a, lse_p);  o' = o_a·e^(lse_a−lse') + o_p·e^(lse_p−lse').
-// Used by the context-parallel ring, where each visiting K/V shard yields a
-// partial (O, LSE). The reference has the same idea in its unused split-KV
-// reduce kernel (npu_flash_attention.py:255-293).
+// The forward merges its own result this way when called with
+// bfa_fwd_args.accumulate (the context-parallel ring's path); this entry
+// point merges two results already in memory. The reference has the same
+// idea in its unused split-KV reduce kernel (npu_flash_attention.py:255-293).
 #include <cuda_runtime.h>
 
 #include "bfa_internal.h"
@@ -19,15 +20,8 @@ __global__ void __launch_bounds__(256) merge_kernel(int B, int H, int S, int D, 
   const int lane = threadIdx.x & 31;
   if (row >= (int64_t)B * H * S) return;
   const int i = (int)(row % S), h = (int)((row / S) % H), b = (int)(row / ((int64_t)S * H));
-  const float la = lse_a[row], lp = lse_p[row];
-  const float mx = fmaxf(la, lp);
-  float wa = 0.f, wp = 0.f, ln = neg_inf();
-  if (mx != neg_inf()) {
-    const float ea = expf(la - mx), ep = expf(lp - mx);
-    ln = mx + logf(ea + ep);
-    wa = expf(la - ln);
-    wp = expf(lp - ln);
-  }
+  const MergeWeights w = merge_weights(lse_a[row], lse_p[row]);
+  const float wa = w.wa, wp = w.wp, ln = w.ln;
   TA* A = (TA*)oa.data + b * oa.stride[0] + h * oa.stride[1] + i * oa.stride[2];
   const TP* P = (const TP*)op.data + b * op.stride[0] + h * op.stride[1] + i * op.stride[2];
   for (int d = lane; d < D; d += 32) {

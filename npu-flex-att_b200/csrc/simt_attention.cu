@@ -171,6 +171,26 @@ __global__ void __launch_bounds__(NT) simt_fwd_kernel(Params p) {
     }
   }
 
+  if (p.out_acc) {
+    // Merge into the running fp32 output and LSE (bfa_fwd_args.accumulate).
+    float* lse_p = p.lse + ((int64_t)b * p.Hq + hq) * p.Sq + r0 + r;
+    const MergeWeights w = merge_weights((r < rows) ? *lse_p : neg_inf(), (l > 0.f) ? m + logf(l) : neg_inf());
+    __syncwarp();  // the row's four threads have read the running LSE
+    if (r < rows) {
+      const float sp = (l > 0.f) ? w.wp / l : 0.f;
+      float* O = (float*)p.o + (int64_t)b * p.so_[0] + (int64_t)hq * p.so_[1] + (int64_t)(r0 + r) * p.so_[2];
+#pragma unroll
+      for (int e = 0; e < DP / 4; ++e) {
+        const int d = acc_col(e, c);
+        if (d < p.D) {
+          float* dst = O + (int64_t)d * p.so_[3];
+          *dst = fmaf(acc[e], sp, w.wa != 0.f ? *dst * w.wa : 0.f);
+        }
+      }
+      if (c == 0) *lse_p = w.ln;
+    }
+    return;
+  }
   if (r < rows) {
     const float inv = (l > 0.f) ? 1.f / l : 0.f;
     T* O = (T*)p.o + (int64_t)b * p.so_[0] + (int64_t)hq * p.so_[1] + (int64_t)(r0 + r) * p.so_[2];

@@ -480,7 +480,44 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (good && n_iter > 0) good = warp_wait(bar(kODone + t), (uint32_t)((n_iter - 1) & 1), ctl);
     // Q_t's smem tile is free once the last S_t MMA has run; it stages O_t.
     uint8_t* Ot = smem + L::kOffQ + t * L::kQBytes;
-    if (good) {
+    // This row's LSE (natural log); -inf when it sees no key.
+    const float lse_row = (l > 0.f) ? fmaf(slope, (float)(gi - g0), (m + lg2(l)) * kLn2) : neg_inf();
+    if (good && p.out_acc) {
+      // Merge into the running fp32 output and LSE (bfa_fwd_args.accumulate):
+      // each thread owns its row, so it reads and rewrites it directly, 16
+      // bytes at a time. The TMEM loads are warp-collective: every lane takes
+      // part, rows past Sq skip only the memory accesses.
+      tc_fence_after();
+      const bool live = r_local < p.Sq;
+      float* lse_p = p.lse + ((int64_t)b * p.Hq + hq) * p.Sq + r_local;
+      const MergeWeights w = merge_weights(live ? *lse_p : neg_inf(), lse_row);
+      const float sp = (l > 0.f) ? w.wp / l : 0.f;
+      float* orow = (float*)p.o + (int64_t)b * p.so_[0] + (int64_t)hq * p.so_[1] + (int64_t)r_local * p.so_[2];
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        if (n_iter > 0) {
+          tmem_ld32(tO + 32 * c, r);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = 0u;
+        }
+        if (live) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            float4* dst = reinterpret_cast<float4*>(orow + 32 * c + 4 * q);
+            float4 a = w.wa != 0.f ? *dst : make_float4(0.f, 0.f, 0.f, 0.f);
+            a.x = fmaf(__uint_as_float(r[4 * q + 0]), sp, a.x * w.wa);
+            a.y = fmaf(__uint_as_float(r[4 * q + 1]), sp, a.y * w.wa);
+            a.z = fmaf(__uint_as_float(r[4 * q + 2]), sp, a.z * w.wa);
+            a.w = fmaf(__uint_as_float(r[4 * q + 3]), sp, a.w * w.wa);
+            *dst = a;
+          }
+        }
+      }
+      if (live) *lse_p = w.ln;
+    } else if (good) {
       tc_fence_after();
       const float inv = (l > 0.f) ? 1.f / l : 0.f;
 #pragma unroll 1
@@ -508,7 +545,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (lane == 0) warp_ok[warp - 4] = good ? 1 : 0;
     named_sync(1 + t, 128);
-    if (wq == 0 && lane == 0) {
+    if (wq == 0 && lane == 0 && !p.out_acc) {
       const bool all = warp_ok[4 * t] && warp_ok[4 * t + 1] && warp_ok[4 * t + 2] && warp_ok[4 * t + 3];
       if (all) {
         for (int s = 0; s < L::kSub; ++s)
@@ -517,10 +554,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_store_wait_all();
       }
     }
-    if (good && r_local < p.Sq) {
-      p.lse[((int64_t)b * p.Hq + hq) * p.Sq + r_local] =
-          (l > 0.f) ? fmaf(slope, (float)(gi - g0), (m + lg2(l)) * kLn2) : neg_inf();
-    }
+    if (good && r_local < p.Sq && !p.out_acc) p.lse[((int64_t)b * p.Hq + hq) * p.Sq + r_local] = lse_row;
   }
 
   tc_fence_before();
@@ -570,8 +604,9 @@ bool sm100_fwd_eligible(const Params& p, int dtype) {
   if (p.D != 64 && p.D != 128 && p.D != 256) return false;
   if (p.Sq < 1 || p.Sk < 1 || p.B < 1 || p.Hq < 1) return false;
   if (!device_is_sm100()) return false;
+  // A merging call's fp32 output is read and written 16 bytes at a time.
   return tma_layout_ok(p.q, p.sq_, 2) && tma_layout_ok(p.k, p.sk_, 2) &&
-         tma_layout_ok(p.v, p.sv_, 2) && tma_layout_ok(p.o, p.so_, 2);
+         tma_layout_ok(p.v, p.sv_, 2) && tma_layout_ok(p.o, p.so_, p.out_acc ? 4 : 2);
 }
 
 int sm100_fwd(const Params& p, int dtype, cudaStream_t st) {
@@ -580,7 +615,8 @@ int sm100_fwd(const Params& p, int dtype, cudaStream_t st) {
   if (!make_tmap_bhsd(&tm.m[0], p.q, dtype, p.D, p.Sq, p.Hq, p.B, p.sq_, kBM) ||
       !make_tmap_bhsd(&tm.m[1], p.k, dtype, p.D, p.Sk, p.Hkv, p.B, p.sk_, kBN) ||
       !make_tmap_bhsd(&tm.m[2], p.v, dtype, p.D, p.Sk, p.Hkv, p.B, p.sv_, kBN) ||
-      !make_tmap_bhsd(&tm.m[3], p.o, dtype, p.D, p.Sq, p.Hq, p.B, p.so_, kBM))
+      !(p.out_acc ? (tm.m[3] = tm.m[0], true)  // no TMA store of O when merging
+                  : make_tmap_bhsd(&tm.m[3], p.o, dtype, p.D, p.Sq, p.Hq, p.B, p.so_, kBM)))
     return simt_fwd(p, dtype, st);
   const bool bf16 = dtype == BFA_DTYPE_BF16;
   if (p.D == 64) return bf16 ? dispatch_flags<64, true>(p, tm, st) : dispatch_flags<64, false>(p, tm, st);

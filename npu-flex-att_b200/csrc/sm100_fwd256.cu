@@ -492,7 +492,47 @@ __global__ void __launch_bounds__(kThreads, 1)
     // order, and PV(n-1) came after it): it stages O, warpgroup h its
     // columns [128h, 128h + 128) (sub-tiles 2h, 2h + 1).
     uint8_t* Ot = smem + kOffQ;
-    if (good) {
+    // This row's LSE (natural log); -inf when it sees no key.
+    const float lse_row =
+        (l_tot > 0.f) ? fmaf(slope, (float)(gi - g0), (m + lg2(l_tot)) * kLn2) : neg_inf();
+    float* lse_p = p.lse + ((int64_t)b * p.Hq + hq) * p.Sq + r_local;
+    const bool live = r_local < p.Sq;
+    MergeWeights mw{0.f, 0.f, neg_inf()};
+    if (good && p.out_acc) {
+      // Merge into the running fp32 output and LSE (bfa_fwd_args.accumulate):
+      // each thread reads and rewrites its row's 128 columns directly, 16
+      // bytes at a time; both warpgroups read the running LSE before the
+      // barrier below, after which warpgroup 0 rewrites it. The TMEM loads
+      // are warp-collective: rows past Sq skip only the memory accesses.
+      tc_fence_after();
+      mw = merge_weights(live ? *lse_p : neg_inf(), lse_row);
+      const float sp = (l_tot > 0.f) ? mw.wp / l_tot : 0.f;
+      float* orow = (float*)p.o + (int64_t)b * p.so_[0] + (int64_t)hq * p.so_[1] +
+                    (int64_t)r_local * p.so_[2] + 128 * eg;
+#pragma unroll 1
+      for (int c = 0; c < 128 / 32; ++c) {
+        uint32_t o[32];
+        if (n_iter > 0) {
+          tmem_ld32(tO + 32 * c, o);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0u;
+        }
+        if (live) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            float4* dst = reinterpret_cast<float4*>(orow + 32 * c + 4 * q);
+            float4 a = mw.wa != 0.f ? *dst : make_float4(0.f, 0.f, 0.f, 0.f);
+            a.x = fmaf(__uint_as_float(o[4 * q + 0]), sp, a.x * mw.wa);
+            a.y = fmaf(__uint_as_float(o[4 * q + 1]), sp, a.y * mw.wa);
+            a.z = fmaf(__uint_as_float(o[4 * q + 2]), sp, a.z * mw.wa);
+            a.w = fmaf(__uint_as_float(o[4 * q + 3]), sp, a.w * mw.wa);
+            *dst = a;
+          }
+        }
+      }
+    } else if (good) {
       tc_fence_after();
       const float inv = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
 #pragma unroll 1
@@ -520,7 +560,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (lane == 0) warp_ok[warp - 4] = good ? 1 : 0;
     named_sync(3, 256);
-    if (warp == 4 && lane == 0) {
+    if (warp == 4 && lane == 0 && !p.out_acc) {
       bool all = true;
       for (int w = 0; w < 8; ++w) all = all && warp_ok[w];
       if (all) {
@@ -529,10 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_store_wait_all();
       }
     }
-    if (good && eg == 0 && r_local < p.Sq) {
-      p.lse[((int64_t)b * p.Hq + hq) * p.Sq + r_local] =
-          (l_tot > 0.f) ? fmaf(slope, (float)(gi - g0), (m + lg2(l_tot)) * kLn2) : neg_inf();
-    }
+    if (good && eg == 0 && live) *lse_p = p.out_acc ? mw.ln : lse_row;
   }
   tc_fence_before();
   __syncthreads();
@@ -576,7 +613,8 @@ int sm100_fwd256(const Params& p, int dtype, cudaStream_t st) {
   if (!make_tmap_bhsd(&tm.m[0], p.q, dtype, kD, p.Sq, p.Hq, p.B, p.sq_, kBM) ||
       !make_tmap_bhsd(&tm.m[1], p.k, dtype, kD, p.Sk, p.Hkv, p.B, p.sk_, kBN) ||
       !make_tmap_bhsd(&tm.m[2], p.v, dtype, kD, p.Sk, p.Hkv, p.B, p.sv_, 64) ||
-      !make_tmap_bhsd(&tm.m[3], p.o, dtype, kD, p.Sq, p.Hq, p.B, p.so_, kBM))
+      !(p.out_acc ? (tm.m[3] = tm.m[0], true)  // no TMA store of O when merging
+                  : make_tmap_bhsd(&tm.m[3], p.o, dtype, kD, p.Sq, p.Hq, p.B, p.so_, kBM)))
     return simt_fwd(p, dtype, st);
   return dtype == BFA_DTYPE_BF16 ? dispatch<true>(p, tm, st) : dispatch<false>(p, tm, st);
 }

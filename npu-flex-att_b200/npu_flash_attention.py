@@ -176,6 +176,7 @@ def npu_flash_attention_forward(
     block_mask=None,
     _wait_timeout_ns=0,
     _debug_flags=0,
+    _merge_into=None,
 ):
     """Attention forward: O (and the fp32 natural-log LSE when `return_lse`).
 
@@ -188,6 +189,11 @@ def npu_flash_attention_forward(
     ceil(Sk/128)]) computes only the 128x128 blocks of the score matrix it
     marks, again on top of the other masks; the kernels skip the other
     blocks. Rows left with no key give O = 0 and LSE = -inf.
+
+    ``_merge_into`` (internal: the context-parallel ring) is a pair (O_acc
+    fp32 [B, Hq, Sq, D], LSE_acc fp32 contiguous [B, Hq, Sq]) holding a
+    running result; the call merges its own result into both in place (the
+    library's epilogue merge, bfa_fwd_args.accumulate) and returns them.
     """
     B, Hq, Sq, D = query.shape
     Bk, Hkv, Sk, Dk = key.shape
@@ -201,9 +207,18 @@ def npu_flash_attention_forward(
     dev = query.device
     alibi = _alibi(alibi_slope, Hq, dev)
     q, k, v = _fast_layout(query), _fast_layout(key), _fast_layout(value)
-    O = torch.empty_like(query)
-    o_k = _fast_layout(O) if O.data_ptr() else O
-    LSE = torch.empty(B, Hq, Sq, device=dev, dtype=torch.float32)
+    if _merge_into is not None:
+        O, LSE = _merge_into
+        if (O.dtype != torch.float32 or tuple(O.shape) != (B, Hq, Sq, D) or O.device != dev
+                or LSE.dtype != torch.float32 or tuple(LSE.shape) != (B, Hq, Sq)
+                or LSE.device != dev or not LSE.is_contiguous()):
+            raise ValueError("_merge_into takes fp32 O [B, Hq, Sq, D] and contiguous fp32 LSE "
+                             "[B, Hq, Sq] on the query's device")
+        o_k = O
+    else:
+        O = torch.empty_like(query)
+        o_k = _fast_layout(O) if O.data_ptr() else O
+        LSE = torch.empty(B, Hq, Sq, device=dev, dtype=torch.float32)
     lib = _bfa.load()
     docs = _documents(cu_seqlens, max(q_pos_offset + Sq, k_pos_offset + Sk), dev)
     blk = _block_mask(block_mask, B, Hq, Sq, Sk, dev)
@@ -215,10 +230,12 @@ def npu_flash_attention_forward(
     args.status = _bfa.status_word(dev).data_ptr()
     args.wait_timeout_ns = int(_wait_timeout_ns)
     args.debug_flags = int(_debug_flags)
+    args.accumulate = 1 if _merge_into is not None else 0
     with torch.cuda.device(dev):
         # Scratch of the split-KV decoding path (few query rows per KV head),
-        # from torch's caching allocator: the library allocates nothing.
-        ws_bytes = lib.bfa_fwd_workspace_bytes(pr)
+        # from torch's caching allocator: the library allocates nothing. A
+        # merging call never takes that path.
+        ws_bytes = 0 if _merge_into is not None else lib.bfa_fwd_workspace_bytes(pr)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
         if ws is not None:
             args.workspace, args.workspace_bytes = ws.data_ptr(), ws_bytes

@@ -74,6 +74,18 @@ def test_null_arguments_are_rejected():
     assert lib.bfa_bwd(ctypes.byref(_problem()), ctypes.byref(bfa_lib.BwdArgs()), None, 0, None) == -1
 
 
+def test_fwd_accumulate_flag_is_checked():
+    """bfa_fwd_args.accumulate is 0 or 1; any other value is rejected before
+    any CUDA work (the pointers here are never dereferenced)."""
+    lib = bfa_lib.load()
+    args = bfa_lib.FwdArgs()
+    for t in (args.q, args.k, args.v, args.o):
+        t.data = 16
+    args.lse = 16
+    args.accumulate = 2
+    assert lib.bfa_fwd(ctypes.byref(_problem()), ctypes.byref(args), None) == -1
+
+
 def test_empty_problem_is_a_no_op():
     lib = bfa_lib.load()
     # B*Hq*Sq == 0: nothing to compute, nothing launched.

@@ -29,6 +29,10 @@ class OracleBlockOps:
     def fwd(self, q, k, v, q_off, k_off, m):
         return attention_forward(q, k, v, **self._kw(m, q_off, k_off))
 
+    def fwd_merge(self, o_acc, lse_acc, q, k, v, q_off, k_off, m):
+        o_p, lse_p = self.fwd(q, k, v, q_off, k_off, m)
+        self.merge(o_acc, lse_acc, o_p, lse_p)
+
     def merge(self, o_acc, lse_acc, o_part, lse_part):
         new = torch.logaddexp(lse_acc, lse_part.to(lse_acc.dtype))
         safe = torch.where(torch.isfinite(new), new, torch.zeros_like(new))

@@ -1,8 +1,9 @@
 """Context-parallel ring on the GPU.
 
 Simulated ranks (one GPU, one process) run the ring with the CUDA block ops:
-every block is a libbfa forward / accumulate-mode backward with absolute
-position offsets, merged with bfa_merge_partial. The gathered result is
+every block is a libbfa forward that merges its result into the running
+(O, LSE) in its epilogue and an accumulate-mode backward, with absolute
+position offsets. The gathered result is
 checked against the oracle over the whole sequence. With two or more GPUs the
 same ring runs over NCCL between processes (tests/cp_ring_check.py).
 """
