@@ -33,6 +33,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import time
 from dataclasses import dataclass
 from typing import Optional
 
@@ -252,6 +253,123 @@ def ring_backward(q, k, v, o, lse, do, rank: int, world: int, m: MaskArgs, ops):
     return dq_acc.to(q.dtype), dk_acc.to(k.dtype), dv_acc.to(v.dtype)
 
 
+# ---------------------------------------------------------------- failure detection
+class PeerFailure(RuntimeError):
+    """A rank stopped taking part in the ring or the all-to-alls (it left,
+    crashed or hangs in host code) before a communication step."""
+
+
+class RingWatchdog:
+    """Host-side failure detection for the context-parallel drivers; no GPU
+    work is involved.
+
+    Before each communication step a rank publishes a heartbeat (its step
+    count) in a key-value store the ranks share (the process group's store,
+    ``for_group``) and waits, up to ``timeout_s``, until the peers it
+    exchanges data with in that step have published the same count. A peer
+    that left between steps, crashed or hangs in host code never does. The
+    rank that notices writes the reason into the store, so every other rank
+    stops at its own next check at once instead of waiting out its timeout;
+    it then runs ``abort`` (``for_group``: abort the NCCL communicator, so no
+    call of the group stays posted and the process can exit) and raises
+    PeerFailure. Nothing is posted after a failed check, so none of this
+    rank's transfers is in flight when it raises. A rank that stops on
+    purpose calls ``leave()``.
+
+    The ranks must create their watchdogs in the same order (the store keys
+    come from a per-process counter) or give them the same ``name``.
+    """
+
+    _created = 0
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 30.0,
+                 poll_s: float = 0.001, name: Optional[str] = None, abort=None):
+        if name is None:
+            name = str(RingWatchdog._created)
+            RingWatchdog._created += 1
+        self.store, self.rank, self.world = store, rank, world
+        self.prefix = f"bfa_cp_watchdog/{name}"
+        self.timeout_s, self.poll_s = float(timeout_s), float(poll_s)
+        self.abort = abort
+        self.steps = 0
+        self.failed: Optional[str] = None
+
+    @classmethod
+    def for_group(cls, group=None, timeout_s: float = 30.0, name: Optional[str] = None):
+        """A watchdog over the store, ranks and communicator of ``group``."""
+        import torch.distributed as dist
+        import torch.distributed.distributed_c10d as c10d
+        abort = None
+        if dist.get_backend(group) == "nccl":
+            def abort():
+                c10d._abort_process_group(group)  # None: every group of this process
+        return cls(c10d._get_default_store(), dist.get_rank(group), dist.get_world_size(group),
+                   timeout_s=timeout_s, name=name, abort=abort)
+
+    def _key(self, what: str) -> str:
+        return f"{self.prefix}/{what}"
+
+    def _fail(self, reason: str):
+        self.failed = reason
+        if self.abort is not None:
+            try:
+                self.abort()
+            except Exception:  # the failure below is the one to report
+                pass
+        raise PeerFailure(reason)
+
+    def _check_failed(self):
+        if self.failed is not None:
+            raise PeerFailure(self.failed)
+        key = self._key("failed")
+        if self.store.check([key]):
+            self._fail(self.store.get(key).decode())
+
+    def step(self, peers):
+        """Publish this rank's next step and wait until every rank in
+        ``peers`` (ranks of the group; this rank is ignored) has reached it.
+        A store that stops answering (its host process ended) is a failure
+        too."""
+        import torch.distributed as dist
+        try:
+            self._step(peers)
+        except dist.DistError as e:
+            self._fail(f"the ranks' store stopped answering ({e}): the process that holds it ended")
+
+    def _step(self, peers):
+        self._check_failed()
+        self.steps += 1
+        self.store.set(self._key(f"hb/{self.rank}"), str(self.steps))
+        waiting = sorted({p % self.world for p in peers} - {self.rank})
+        deadline = time.monotonic() + self.timeout_s
+        while waiting:
+            still = []
+            for p in waiting:
+                key = self._key(f"hb/{p}")
+                if not (self.store.check([key]) and int(self.store.get(key)) >= self.steps):
+                    still.append(p)
+            waiting = still
+            if not waiting:
+                break
+            self._check_failed()
+            if time.monotonic() > deadline:
+                reason = (f"rank {waiting[0]} did not reach communication step {self.steps} "
+                          f"within {self.timeout_s:g} s (noticed by rank {self.rank})")
+                self.store.set(self._key("failed"), reason)
+                self._fail(reason)
+            time.sleep(self.poll_s)
+
+    def neighbours(self):
+        """The ring's peers: the next rank (send) and the previous one (receive)."""
+        return (self.rank + 1, self.rank - 1)
+
+    def leave(self, reason: Optional[str] = None):
+        """Stop on purpose: the other ranks raise PeerFailure at their next check."""
+        reason = reason or f"rank {self.rank} left"
+        self.store.set(self._key("failed"), reason)
+        self.failed = reason
+
+
 # ---------------------------------------------------------------- drivers
 class DistRing:
     """Ring transfers over torch.distributed point-to-point (NCCL or gloo)."""
@@ -296,13 +414,17 @@ class DistRing:
         return recv
 
 
-def run_dist(gen, group=None):
-    """Drive one rank's ring generator over torch.distributed."""
+def run_dist(gen, group=None, watchdog: Optional[RingWatchdog] = None):
+    """Drive one rank's ring generator over torch.distributed. With a
+    ``watchdog``, each transfer is posted only after both ring neighbours
+    have reached the same step (PeerFailure otherwise)."""
     ring = DistRing(group)
     try:
         step = next(gen)
         while True:
             kind = step[0]
+            if kind in ("start", "swap") and watchdog is not None:
+                watchdog.step(watchdog.neighbours())
             if kind == "start":
                 ring.start(step[1])
                 step = gen.send(None)
@@ -437,10 +559,12 @@ def _local_mask(m: MaskArgs, rank: int, hq: int, world: int) -> MaskArgs:
     return MaskArgs(m.causal, m.sliding_window, slopes, m.scale, m.soft_cap)
 
 
-def _dist_a2a(group):
+def _dist_a2a(group, watchdog: Optional[RingWatchdog] = None):
     import torch.distributed as dist
 
     def a2a(send):
+        if watchdog is not None:
+            watchdog.step(range(watchdog.world))
         recv = torch.empty_like(send)
         dist.all_to_all_single(recv, send, group=group)
         return recv
@@ -451,12 +575,13 @@ class UlyssesFlexAttention(torch.autograd.Function):
     """Autograd over Ulysses: inputs and outputs are this rank's sequence shard."""
 
     @staticmethod
-    def forward(ctx, q, k, v, causal, sliding_window, alibi_slope, scale, soft_cap, group, layout, ops):
+    def forward(ctx, q, k, v, causal, sliding_window, alibi_slope, scale, soft_cap, group, layout, ops,
+                watchdog):
         import torch.distributed as dist
         rank, world = dist.get_rank(group), dist.get_world_size(group)
         _ulysses_check(q.shape[1], k.shape[1], world)
         lay = make_layout(layout, q.shape[2] * world, world)
-        a2a = _dist_a2a(group)
+        a2a = _dist_a2a(group, watchdog)
         m = _local_mask(MaskArgs(causal, int(sliding_window), alibi_slope, scale, float(soft_cap)),
                         rank, q.shape[1], world)
         qf, kf, vf = (heads_to_sequence(t.contiguous(), world, lay, a2a) for t in (q, k, v))
@@ -472,19 +597,21 @@ class UlyssesFlexAttention(torch.autograd.Function):
         dof = heads_to_sequence(grad_out.to(qf.dtype).contiguous(), world, lay, a2a)
         dqf, dkf, dvf = ctx.ops.bwd(qf, kf, vf, of, lsef, dof, ctx.m)
         grads = [sequence_to_heads(t, world, lay, a2a) for t in (dqf, dkf, dvf)]
-        return (*grads, None, None, None, None, None, None, None, None)
+        return (*grads, None, None, None, None, None, None, None, None, None)
 
 
 def ulysses_attention(q, k, v, causal=False, sliding_window=0, alibi_slope=None, scale=None,
-                      soft_cap=0.0, group=None, layout="zigzag", _ops=None):
+                      soft_cap=0.0, group=None, layout="zigzag", _ops=None, watchdog=None):
     """Attention over a sequence sharded across the ranks of ``group`` by
     head-sequence all-to-alls (Ulysses). q [B, Hq, S/N, D], k/v
     [B, Hkv, S/N, D] are this rank's rows in ``layout`` ("zigzag", as for
     context_parallel_attention, or "contiguous"); Hq and Hkv must be divisible
     by N. Returns this rank's rows of O; differentiable. ``alibi_slope`` holds
-    all Hq slopes on every rank."""
+    all Hq slopes on every rank. With a ``watchdog`` (RingWatchdog) every
+    all-to-all waits for all ranks on the host first and raises PeerFailure
+    when one has stopped."""
     return UlyssesFlexAttention.apply(q, k, v, causal, sliding_window, alibi_slope, scale, soft_cap,
-                                      group, layout, _ops or CudaAttentionOps())
+                                      group, layout, _ops or CudaAttentionOps(), watchdog)
 
 
 def ulysses_simulated(qs, ks, vs, dos, m: MaskArgs, ops, layout="zigzag"):
@@ -518,13 +645,13 @@ class RingFlexAttention(torch.autograd.Function):
     """Autograd over the ring: inputs and outputs are this rank's zigzag shard."""
 
     @staticmethod
-    def forward(ctx, q, k, v, causal, sliding_window, alibi_slope, scale, soft_cap, group):
+    def forward(ctx, q, k, v, causal, sliding_window, alibi_slope, scale, soft_cap, group, watchdog):
         import torch.distributed as dist
         m = MaskArgs(causal, int(sliding_window), alibi_slope, scale, float(soft_cap))
         rank, world = dist.get_rank(group), dist.get_world_size(group)
-        o, lse = run_dist(ring_forward(q, k, v, rank, world, m, CudaBlockOps()), group)
+        o, lse = run_dist(ring_forward(q, k, v, rank, world, m, CudaBlockOps()), group, watchdog)
         ctx.save_for_backward(q, k, v, o, lse)
-        ctx.m, ctx.group, ctx.rank, ctx.world = m, group, rank, world
+        ctx.m, ctx.group, ctx.rank, ctx.world, ctx.watchdog = m, group, rank, world, watchdog
         return o
 
     @staticmethod
@@ -532,14 +659,16 @@ class RingFlexAttention(torch.autograd.Function):
         q, k, v, o, lse = ctx.saved_tensors
         do = grad_out.to(q.dtype).contiguous()
         dq, dk, dv = run_dist(ring_backward(q, k, v, o, lse, do, ctx.rank, ctx.world, ctx.m,
-                                            CudaBlockOps()), ctx.group)
-        return dq, dk, dv, None, None, None, None, None, None
+                                            CudaBlockOps()), ctx.group, ctx.watchdog)
+        return dq, dk, dv, None, None, None, None, None, None, None
 
 
 def context_parallel_attention(q, k, v, causal=False, sliding_window=0, alibi_slope=None,
-                               scale=None, soft_cap=0.0, group=None):
+                               scale=None, soft_cap=0.0, group=None, watchdog=None):
     """Attention over a sequence sharded across the ranks of ``group`` in the
     zigzag layout (``ZigzagLayout.shard``): q [B, Hq, 2C, D], k/v [B, Hkv, 2C, D]
-    on this rank's GPU. Returns this rank's rows of O; differentiable."""
+    on this rank's GPU. Returns this rank's rows of O; differentiable. With a
+    ``watchdog`` (RingWatchdog) each K/V transfer waits for both ring
+    neighbours on the host first and raises PeerFailure when one has stopped."""
     return RingFlexAttention.apply(q, k, v, causal, sliding_window, alibi_slope, scale,
-                                   soft_cap, group)
+                                   soft_cap, group, watchdog)

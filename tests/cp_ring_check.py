@@ -6,9 +6,16 @@ backward through an autograd entry point -- the K/V ring
 argument "ulysses" -- and rank 0 compares the gathered O, dQ, dK, dV with the
 single-GPU kernels on the whole sequence. Prints "cp ring ok" / "cp ulysses
 ok" on success; exits non-zero otherwise.
+
+With the argument "leave" the ring runs under a RingWatchdog: after one full
+step (forward and backward, device synchronised) the last rank leaves between
+steps, with nothing in flight. Every other rank must raise PeerFailure at its
+next transfer -- learned on the host, through the store -- abort its NCCL
+communicator and exit; rank 0 then prints "cp leave ok".
 """
 import os
 import sys
+import time
 from datetime import timedelta
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -23,6 +30,37 @@ import context_parallel as cp  # noqa: E402
 import npu_flash_attention as nfa  # noqa: E402
 
 
+def leave_check(rank, world, dev):
+    B, Hq, Hkv, S, D = 1, 4, 2, 1024, 128
+    g = torch.Generator().manual_seed(5)
+    q, k, v, go = (torch.randn(B, h, S, D, generator=g).to(torch.bfloat16).to(dev)
+                   for h in (Hq, Hkv, Hkv, Hq))
+    lay = cp.ZigzagLayout(S, world)
+    wd = cp.RingWatchdog.for_group(timeout_s=5.0)
+
+    def step():
+        qs, ks, vs = (lay.shard(t, rank).requires_grad_(True) for t in (q, k, v))
+        o = cp.context_parallel_attention(qs, ks, vs, causal=True, watchdog=wd)
+        o.backward(lay.shard(go, rank))
+        torch.cuda.synchronize()
+
+    step()
+    if rank == world - 1:
+        print(f"rank {rank}: leaving between steps", flush=True)
+        os._exit(0)
+    t0 = time.monotonic()
+    try:
+        step()
+        print(f"rank {rank}: no failure seen", file=sys.stderr, flush=True)
+        os._exit(1)
+    except cp.PeerFailure as e:
+        dt = time.monotonic() - t0
+        print(f"rank {rank}: PeerFailure after {dt:.2f} s: {e}", flush=True)
+        if rank == 0:
+            print("cp leave ok", flush=True)
+        os._exit(0 if dt < 30 else 1)
+
+
 def main():
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
@@ -31,6 +69,8 @@ def main():
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=dev)
     mode = sys.argv[1] if len(sys.argv) > 1 else "ring"
+    if mode == "leave":
+        leave_check(rank, world, dev)
     attn = cp.ulysses_attention if mode == "ulysses" else cp.context_parallel_attention
     ok = True
     try:

@@ -104,6 +104,20 @@ def test_ring_over_nccl_two_gpus():
     assert "cp ring ok" in r.stdout
 
 
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ring_rank_that_leaves_is_detected_over_nccl():
+    """Two GPUs, NVLS off: after one full step rank 1 leaves between steps
+    (device synchronised, nothing in flight); rank 0's RingWatchdog sees it on
+    the host before its next transfer, aborts its communicator and exits."""
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", "--nproc-per-node=2", "--master-addr", "127.0.0.1",
+           "--master-port", "29533", os.path.join(ROOT, "tests", "cp_ring_check.py"), "leave"]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "cp leave ok" in r.stdout
+
+
 @pytest.mark.parametrize("world", [2, 4])
 @pytest.mark.parametrize("case", ["causal", "alibi", "full_cap"])
 def test_simulated_ulysses_cuda_matches_single_gpu(world, case):
