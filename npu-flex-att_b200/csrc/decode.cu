@@ -443,6 +443,12 @@ __global__ void __launch_bounds__(kDecThreads)
   // Rows R..15 keep P = 0 (the S phase writes only rows < R).
   for (int idx = tid; idx < kMaxRows * kPRow; idx += kDecThreads) ps[idx] = 0.f;
 
+  // Chunks whose 64 keys every row of the KV head keeps (all but the edges
+  // of the causal / window range, without documents or a block mask) skip
+  // the per-element mask and position arithmetic in the S phase.
+  const KeptRange kept = kept_keys(p, 0, p.Sq, kChunk, false);
+  const bool may_skip = p.doc_lo == nullptr && p.blk == nullptr;
+
   const int col0 = warp * (D / 8);  // this warp's O columns in P·V
   float o[NT][4];
 #pragma unroll
@@ -472,11 +478,15 @@ __global__ void __launch_bounds__(kDecThreads)
       }
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[e] += acc2[e];
+      const int key0 = kb + c * kChunk;
+      const bool full = may_skip && key0 + kChunk <= ke && kept.has(key0);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int r = g + 8 * (e >> 1);
         const int n = 8 * warp + 2 * t + (e & 1);
-        if (r < R) {
+        if (PLAIN && full) {
+          if (r < R) ps[r * kPRow + n] = acc[e] * sl2;
+        } else if (r < R) {
           const int key = kb + c * kChunk + n;
           const int gg = (row0 + r) / p.Sq, s = (row0 + r) - gg * p.Sq;
           const int64_t gi = (int64_t)s + p.q_off, gj = (int64_t)key + p.k_off;
