@@ -363,7 +363,7 @@ __device__ __forceinline__ void ldsm_x2_trans(uint32_t addr, uint32_t& r0, uint3
 }
 
 template <typename T, int D, bool PLAIN>
-__global__ void __launch_bounds__(kDecThreads)
+__global__ void __launch_bounds__(kDecThreads, D <= 128 ? 3 : 1)
     decode_mma_kernel(const Params p, int n_split, int kvis_lo, int split_len, float* __restrict__ part_o,
                       float* __restrict__ part_lse) {
   using L = DecLayoutM<T, D>;
@@ -395,21 +395,32 @@ __global__ void __launch_bounds__(kDecThreads)
   const T* vg = static_cast<const T*>(p.v);
   const float sl2 = p.scale * kLog2e;
 
+  // K/V chunk loads: thread tid copies 16-byte piece tid % kPieces of rows
+  // tid / kPieces + kRowsPerPass·i (K and V alike). The addresses come from
+  // the launch parameters at each call (few live registers: three CTAs per
+  // SM at head dim <= 128). Keys past the split's end (only in its last
+  // chunk) are zero-filled.
+  constexpr int kPieces = D * 2 / 16;
+  constexpr int kRowsPerPass = kDecThreads / kPieces;
+  constexpr int kPasses = kChunk / kRowsPerPass;
+  static_assert(kDecThreads % kPieces == 0 && kChunk % kRowsPerPass == 0, "piece mapping");
   auto load_chunk = [&](int c, int stage) {
-    constexpr int kPieces = D * 2 / 16;
+    const int n0 = tid / kPieces, pc = tid % kPieces;
     const int key0 = kb + c * kChunk;
-    for (int idx = tid; idx < 2 * kChunk * kPieces; idx += kDecThreads) {
-      const int which = idx / (kChunk * kPieces);  // 0: K, 1: V
-      const int rem = idx - which * (kChunk * kPieces);
-      const int n = rem / kPieces, pc = rem - n * kPieces;
-      const int key = key0 + n;
-      uint8_t* dst = smem + (which ? L::kOffV : L::kOffK) + stage * L::kTileBytes + n * L::kRowBytes + pc * 16;
-      if (key < ke) {
-        const T* src = which ? vg + (int64_t)b * p.sv_[0] + (int64_t)hkv * p.sv_[1] + (int64_t)key * p.sv_[2]
-                             : kg + (int64_t)b * p.sk_[0] + (int64_t)hkv * p.sk_[1] + (int64_t)key * p.sk_[2];
-        cp_async16(dst, src + pc * 8);
+    const bool whole = key0 + kChunk <= ke;
+    const int64_t kr = key0 + n0;
+    const T* kp = kg + (int64_t)b * p.sk_[0] + (int64_t)hkv * p.sk_[1] + kr * p.sk_[2] + pc * 8;
+    const T* vp = vg + (int64_t)b * p.sv_[0] + (int64_t)hkv * p.sv_[1] + kr * p.sv_[2] + pc * 8;
+    uint8_t* kd = smem + L::kOffK + stage * L::kTileBytes + n0 * L::kRowBytes + pc * 16;
+    uint8_t* vd = kd + (L::kOffV - L::kOffK);
+#pragma unroll
+    for (int i = 0; i < kPasses; ++i) {
+      if (whole || key0 + n0 + i * kRowsPerPass < ke) {
+        cp_async16(kd + i * kRowsPerPass * L::kRowBytes, kp + (int64_t)(i * kRowsPerPass) * p.sk_[2]);
+        cp_async16(vd + i * kRowsPerPass * L::kRowBytes, vp + (int64_t)(i * kRowsPerPass) * p.sv_[2]);
       } else {
-        *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(kd + i * kRowsPerPass * L::kRowBytes) = make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(vd + i * kRowsPerPass * L::kRowBytes) = make_uint4(0u, 0u, 0u, 0u);
       }
     }
     cp_async_commit();
