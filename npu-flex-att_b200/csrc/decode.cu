@@ -314,7 +314,10 @@ __global__ void __launch_bounds__(kDecThreads)
 //        via ldmatrix.trans.
 // This takes about a quarter of the instructions of the CUDA-core version,
 // whose issue rate bounds it, so the kernel can run at HBM speed.
-constexpr int kPRow = kChunk + 8;  // P row pitch (floats): conflict-free float2 reads
+constexpr int kPRow = kChunk + 8;  // logit row pitch (floats)
+// P (16-bit pairs) row pitch in 32-bit words: rows g and g + 1 four banks
+// apart, so the A-fragment reads of P·V are conflict-free.
+constexpr int kP16Row = kChunk / 2 + 4;
 // K/V chunks per CTA: a double buffer. Two stages (three CTAs per SM at
 // D = 128) measured faster than three (two CTAs per SM) on every decode shape
 // tried: more CTAs per SM keep more loads in flight than a deeper ring.
@@ -328,7 +331,8 @@ struct DecLayoutM {
   static constexpr int kOffV = kStagesM * kTileBytes;
   static constexpr int kOffP = 2 * kStagesM * kTileBytes;      // fp32 [16][kPRow]
   static constexpr int kOffRow = kOffP + kMaxRows * kPRow * 4;   // m, l, alpha per row
-  static constexpr int kSmemBytes = kOffRow + 3 * kMaxRows * 4;
+  static constexpr int kOffP16 = kOffRow + 3 * kMaxRows * 4;     // P packed to 16 bits, [16][kP16Row] words
+  static constexpr int kSmemBytes = kOffP16 + kMaxRows * kP16Row * 4;
   static constexpr int kNT = D / 64;                           // 8-column n-tiles per warp in P·V
   static_assert(sizeof(T) == 2 && D % 64 == 0, "16-bit, D multiple of 64");
   static_assert(kSmemBytes <= 232448, "smem budget");
@@ -356,6 +360,11 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint3
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(addr));
 }
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
 __device__ __forceinline__ void ldsm_x2_trans(uint32_t addr, uint32_t& r0, uint32_t& r1) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
                : "=r"(r0), "=r"(r1)
@@ -374,6 +383,7 @@ __global__ void __launch_bounds__(kDecThreads, D <= 128 ? 3 : 1)
   float* row_m = reinterpret_cast<float*>(smem + L::kOffRow);
   float* row_l = row_m + kMaxRows;
   float* row_a = row_l + kMaxRows;
+  uint32_t* p16 = reinterpret_cast<uint32_t*>(smem + L::kOffP16);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
@@ -451,8 +461,8 @@ __global__ void __launch_bounds__(kDecThreads, D <= 128 ? 3 : 1)
     row_l[tid] = 0.f;
     row_a[tid] = 1.f;
   }
-  // Rows R..15 keep P = 0 (the S phase writes only rows < R).
-  for (int idx = tid; idx < kMaxRows * kPRow; idx += kDecThreads) ps[idx] = 0.f;
+  // Rows R..15 keep P = 0 (the softmax writes only rows < R).
+  for (int idx = tid; idx < kMaxRows * kP16Row; idx += kDecThreads) p16[idx] = 0u;
 
   // Chunks whose 64 keys every row of the KV head keeps (all but the edges
   // of the causal / window range, without documents or a block mask) skip
@@ -476,14 +486,16 @@ __global__ void __launch_bounds__(kDecThreads, D <= 128 ? 3 : 1)
 
     // S for keys [8w, 8w + 8) of the chunk, in two independent MMA chains.
     {
-      const uint8_t* krow = smem + L::kOffK + stage * L::kTileBytes + (8 * warp + g) * L::kRowBytes;
+      // B fragments of keys [8w, 8w + 8) for two k-steps with one
+      // ldmatrix: lanes 8m..8m+7 address key 8w + (lane & 7) at columns
+      // 16ks + 8m, so fragment m is b_m.
+      const uint32_t krow = sm100::smem_u32(smem + L::kOffK + stage * L::kTileBytes +
+                                            (8 * warp + (lane & 7)) * L::kRowBytes) + 16u * (lane >> 3);
       float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int ks = 0; ks < D / 16; ks += 2) {
-        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow + (16 * ks + 2 * t) * 2);
-        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(krow + (16 * ks + 8 + 2 * t) * 2);
-        const uint32_t b2 = *reinterpret_cast<const uint32_t*>(krow + (16 * ks + 16 + 2 * t) * 2);
-        const uint32_t b3 = *reinterpret_cast<const uint32_t*>(krow + (16 * ks + 24 + 2 * t) * 2);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(krow + 32u * ks, b0, b1, b2, b3);
         mma16816<BF16>(acc, qa[ks], b0, b1);
         mma16816<BF16>(acc2, qa[ks + 1], b2, b3);
       }
@@ -517,14 +529,13 @@ __global__ void __launch_bounds__(kDecThreads, D <= 128 ? 3 : 1)
 
     // Online softmax: one warp per row, two keys per lane.
     for (int r = warp; r < R; r += kDecThreads / 32) {
-      const float x0 = ps[r * kPRow + lane], x1 = ps[r * kPRow + lane + 32];
-      const float mx = warp_max(fmaxf(x0, x1));
+      const float2 x = *reinterpret_cast<const float2*>(ps + r * kPRow + 2 * lane);
+      const float mx = warp_max(fmaxf(x.x, x.y));
       const float m_old = row_m[r];
       const float m_new = fmaxf(m_old, mx);
       const float m_use = (m_new == neg_inf()) ? 0.f : m_new;
-      const float p0 = fast_ex2(x0 - m_use), p1 = fast_ex2(x1 - m_use);
-      ps[r * kPRow + lane] = p0;
-      ps[r * kPRow + lane + 32] = p1;
+      const float p0 = fast_ex2(x.x - m_use), p1 = fast_ex2(x.y - m_use);
+      p16[r * kP16Row + lane] = BF16 ? sm100::pack_bf16(p0, p1) : sm100::pack_f16(p0, p1);
       const float sum = warp_sum(p0 + p1);
       if (lane == 0) {
         const float alpha = fast_ex2(m_old - m_use);
@@ -548,22 +559,13 @@ __global__ void __launch_bounds__(kDecThreads, D <= 128 ? 3 : 1)
       const uint32_t vtile = sm100::smem_u32(smem + L::kOffV + stage * L::kTileBytes);
 #pragma unroll
       for (int kk = 0; kk < kChunk / 16; ++kk) {
-        const float2 p00 = *reinterpret_cast<const float2*>(ps + g * kPRow + 16 * kk + 2 * t);
-        const float2 p10 = *reinterpret_cast<const float2*>(ps + (g + 8) * kPRow + 16 * kk + 2 * t);
-        const float2 p01 = *reinterpret_cast<const float2*>(ps + g * kPRow + 16 * kk + 8 + 2 * t);
-        const float2 p11 = *reinterpret_cast<const float2*>(ps + (g + 8) * kPRow + 16 * kk + 8 + 2 * t);
+        // A fragments: P of rows g, g + 8 at keys 16kk + 2t (+1) and
+        // 16kk + 8 + 2t (+1), packed by the softmax.
         uint32_t pa[4];
-        if constexpr (BF16) {
-          pa[0] = sm100::pack_bf16(p00.x, p00.y);
-          pa[1] = sm100::pack_bf16(p10.x, p10.y);
-          pa[2] = sm100::pack_bf16(p01.x, p01.y);
-          pa[3] = sm100::pack_bf16(p11.x, p11.y);
-        } else {
-          pa[0] = sm100::pack_f16(p00.x, p00.y);
-          pa[1] = sm100::pack_f16(p10.x, p10.y);
-          pa[2] = sm100::pack_f16(p01.x, p01.y);
-          pa[3] = sm100::pack_f16(p11.x, p11.y);
-        }
+        pa[0] = p16[g * kP16Row + 8 * kk + t];
+        pa[1] = p16[(g + 8) * kP16Row + 8 * kk + t];
+        pa[2] = p16[g * kP16Row + 8 * kk + 4 + t];
+        pa[3] = p16[(g + 8) * kP16Row + 8 * kk + 4 + t];
         // B fragments: keys 16kk + (lane & 15), columns col0 + 8nt (+8 for
         // the upper lanes), transposed on the way in.
         const uint32_t rowaddr = vtile + (uint32_t)((16 * kk + (lane & 15)) * L::kRowBytes);
