@@ -119,8 +119,13 @@ __global__ void __launch_bounds__(NT) simt_fwd_kernel(Params p) {
 
   int lo, hi;
   key_range(p, r0, r0 + rows, &lo, &hi);
+  // Key tiles every row of the block keeps (inside Sk; no documents or
+  // block mask) skip the per-element mask.
+  const KeptRange kept = kept_keys(p, r0, rows, TN, false);
+  const bool may_skip = p.doc_lo == nullptr && p.blk == nullptr;
   for (int k0 = (lo / TN) * TN; k0 < hi; k0 += TN) {
     const int kn = min(TN, p.Sk - k0);
+    const bool full = may_skip && kept.has(k0);
     __syncthreads();
     stage_rows<T, DP>(sK, K, p.sk_[2], p.sk_[3], k0, kn, p.D, TN);
     stage_rows<T, DP>(sV, V, p.sv_[2], p.sv_[3], k0, kn, p.D, TN);
@@ -135,7 +140,7 @@ __global__ void __launch_bounds__(NT) simt_fwd_kernel(Params p) {
       const int64_t gj = (int64_t)k0 + jj + p.k_off;
       const float dot = dot8[u];
       const float val = transform_logit(dot, p.scale, p.soft_cap, slope, gi, gj, nullptr);
-      const bool ok = (jj < kn) && (r < rows) && keep_elem(p, b, hq, gi, gj);
+      const bool ok = (r < rows) && (full || ((jj < kn) && keep_elem(p, b, hq, gi, gj)));
       s[u] = ok ? val : neg_inf();
       mx = fmaxf(mx, s[u]);
     }
@@ -235,8 +240,13 @@ __global__ void __launch_bounds__(NT) simt_bwd_dq_kernel(Params p) {
 
   int lo, hi;
   key_range(p, r0, r0 + rows, &lo, &hi);
+  // Key tiles every row of the block keeps (inside Sk; no documents or
+  // block mask) skip the per-element mask.
+  const KeptRange kept = kept_keys(p, r0, rows, TN, false);
+  const bool may_skip = p.doc_lo == nullptr && p.blk == nullptr;
   for (int k0 = (lo / TN) * TN; k0 < hi; k0 += TN) {
     const int kn = min(TN, p.Sk - k0);
+    const bool full = may_skip && kept.has(k0);
     __syncthreads();
     stage_rows<T, DP>(sK, K, p.sk_[2], p.sk_[3], k0, kn, p.D, TN);
     stage_rows<T, DP>(sV, V, p.sv_[2], p.sv_[3], k0, kn, p.D, TN);
@@ -249,7 +259,7 @@ __global__ void __launch_bounds__(NT) simt_bwd_dq_kernel(Params p) {
       const int jj = c + 4 * u;
       const int64_t gj = (int64_t)k0 + jj + p.k_off;
       float ds = 0.f;
-      if (row_live && jj < kn && keep_elem(p, b, hq, gi, gj)) {
+      if (row_live && (full || (jj < kn && keep_elem(p, b, hq, gi, gj)))) {
         float t;
         const float dot = sdot[u];
         const float val = transform_logit(dot, p.scale, p.soft_cap, slope, gi, gj, &t);
