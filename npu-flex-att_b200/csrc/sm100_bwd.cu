@@ -379,6 +379,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tt[c + h + 1] = th.y;
               }
             }
+          } else if (ALIBI && !CAP) {
+            // ALiBi without cap: the bias per key (its reference point
+            // clamped as alibi_ref does), the rest two keys per packed
+            // instruction.
+#pragma unroll
+            for (int h = 0; h < 4; h += 2) {
+              const int cc = 32 * half + c + h;
+              const float2 bias = __fadd2_rn(make_float2(fmaxf(ba, fmaf(slope2, (float)cc, bq)),
+                                                         fmaxf(ba, fmaf(slope2, (float)(cc + 1), bq))),
+                                             make_float2(-lse_c[h], -lse_c[h + 1]));
+              const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[c + h]), __uint_as_float(sr[c + h + 1])),
+                                          make_float2(sl2, sl2), bias);
+              float pr0 = ex2(x.x), pr1 = ex2(x.y);
+              if (MASKED) {
+                pr0 = ((unsigned)(cc - clo) < (unsigned)(chi - clo)) ? pr0 : 0.f;
+                pr1 = ((unsigned)(cc + 1 - clo) < (unsigned)(chi - clo)) ? pr1 : 0.f;
+              }
+              pr[c + h] = pr0;
+              pr[c + h + 1] = pr1;
+            }
           } else {
 #pragma unroll
             for (int h = 0; h < 4; ++h) {
@@ -410,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float4 d4 = *reinterpret_cast<const float4*>(rowv + 64 + 32 * half + c);
           const float dl_c[4] = {d4.x, d4.y, d4.z, d4.w};
           float ds4[4];
-          if (!CAP && !ALIBI) {
+          if (!CAP) {
 #pragma unroll
             for (int h = 0; h < 4; h += 2) {
               const float2 dd = __fadd2_rn(make_float2(__uint_as_float(dr[c + h]), __uint_as_float(dr[c + h + 1])),
@@ -909,6 +929,26 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float2 dd = __fadd2_rn(make_float2(__uint_as_float(dr[c]), __uint_as_float(dr[c + 1])), ndl2);
               float2 ds = __fmul2_rn(__fmul2_rn(make_float2(pr0, pr1), dd), sc2);
               ds = __fmul2_rn(ds, __ffma2_rn(make_float2(-th.x, -th.y), th, make_float2(1.f, 1.f)));
+              dpk[c / 2] = pack2<BF16>(ds.x, ds.y);
+            }
+          } else if (ALIBI && !CAP) {
+            // ALiBi without cap: x = s·scale·log2(e) + (abase - lse2 -
+            // slope·log2(e)·c), two keys per packed instruction.
+            const float2 sc2 = make_float2(p.scale, p.scale), ndl2 = make_float2(-dlt, -dlt);
+            const float2 base2 = make_float2(abase - lse2, abase - lse2), nsl2 = make_float2(-slope2, -slope2);
+#pragma unroll
+            for (int c = 0; c < 32; c += 2) {
+              const int cc = 64 * eg + 32 * half + c;
+              const float2 bias = __ffma2_rn(nsl2, make_float2((float)cc, (float)(cc + 1)), base2);
+              const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[32 * half + c]), __uint_as_float(sr[32 * half + c + 1])),
+                                          make_float2(sl2, sl2), bias);
+              float pr0 = ex2(x.x), pr1 = ex2(x.y);
+              if (MASKED) {
+                pr0 = ((unsigned)(cc - clo) < (unsigned)(chi - clo)) ? pr0 : 0.f;
+                pr1 = ((unsigned)(cc + 1 - clo) < (unsigned)(chi - clo)) ? pr1 : 0.f;
+              }
+              const float2 dd = __fadd2_rn(make_float2(__uint_as_float(dr[c]), __uint_as_float(dr[c + 1])), ndl2);
+              const float2 ds = __fmul2_rn(__fmul2_rn(make_float2(pr0, pr1), dd), sc2);
               dpk[c / 2] = pack2<BF16>(ds.x, ds.y);
             }
           } else

@@ -362,6 +362,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const float2 x2 = cap_logit2x2<TIER>(raw2, cap_in, cap_out, &th);
                   xv[0] = x2.x;
                   xv[1] = x2.y;
+                } else if (ALIBI && !CAP) {
+                  // ALiBi without cap, two keys per packed instruction:
+                  // x = s·scale·log2(e) + (abase - slope·log2(e)·c).
+                  const float2 bias = __ffma2_rn(make_float2(-slope2, -slope2), make_float2((float)c, (float)(c + 1)),
+                                                 make_float2(abase, abase));
+                  const float2 x2 = __ffma2_rn(raw2, make_float2(sl2, sl2), bias);
+                  xv[0] = x2.x;
+                  xv[1] = x2.y;
                 } else {
 #pragma unroll
                   for (int h = 0; h < 2; ++h) {
