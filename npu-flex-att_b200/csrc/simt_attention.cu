@@ -331,6 +331,11 @@ __global__ void __launch_bounds__(NT) simt_bwd_dkdv_kernel(Params p) {
 
   int qlo, qhi;
   query_range(p, c0, c0 + cols, &qlo, &qhi);
+  // Head dims <= 64: query tiles that keep every key of this tile (inside Sq
+  // and Sk; no documents or block mask) skip the per-element mask. (At 128
+  // the extra state cost more than it saved.)
+  const KeptRange kq = kept_queries(p, c0, TN, TM);
+  const bool may_skip = DP <= 64 && p.doc_lo == nullptr && p.blk == nullptr;
   int work = 0;  // work item index over (q-head, query tile)
   for (int g = 0; g < p.G; ++g) {
     const int hq = hkv * p.G + g;
@@ -340,6 +345,7 @@ __global__ void __launch_bounds__(NT) simt_bwd_dkdv_kernel(Params p) {
     for (int q0 = (qlo / TM) * TM; q0 < qhi; q0 += TM) {
       if ((work++ % nsplit) != split) continue;  // another CTA of the cluster's
       const int qn = min(TM, p.Sq - q0);
+      const bool full = may_skip && kq.has(q0);
       __syncthreads();
       stage_rows<T, DP>(sQ, Q, p.sq_[2], p.sq_[3], q0, qn, p.D, TM);
       stage_rows<T, DP>(sDO, DO, p.sdo_[2], p.sdo_[3], q0, qn, p.D, TM);
@@ -358,7 +364,7 @@ __global__ void __launch_bounds__(NT) simt_bwd_dkdv_kernel(Params p) {
         const int64_t gi = (int64_t)q0 + ii + p.q_off;
         float pr = 0.f, ds = 0.f;
         const float lse = sL[ii];
-        if (r < cols && ii < qn && lse != neg_inf() && keep_elem(p, b, hq, gi, gj)) {
+        if (lse != neg_inf() && (full || (r < cols && ii < qn && keep_elem(p, b, hq, gi, gj)))) {
           float t;
           const float dot = sdot[u];
           const float val = transform_logit(dot, p.scale, p.soft_cap, slope, gi, gj, &t);
